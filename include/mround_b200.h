@@ -1,0 +1,173 @@
+/*
+ * mround_b200.h -- C ABI of libmround_b200.so, the sm_100a kernels of the
+ * SignRound v2 block-tuning path.
+ *
+ * The library fills the slot MRound leaves empty (reference
+ * mround/kernels/__init__.py:1-10, "empty by design"): every entry point below
+ * replaces one reference call site, named in its comment as file:line of the
+ * fbaldassarri/mround tree (version 0.1.0a6).
+ *
+ * Conventions, for every entry point:
+ *  - All pointers are DEVICE pointers, contiguous row-major, 16-byte aligned
+ *    unless stated.  bf16 tensors are passed as uint16_t bit patterns.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Every call is asynchronous and stream-ordered; nothing synchronizes
+ *    except where stated.
+ *  - Nothing allocates, frees, or keeps a pointer past the call.  Scratch
+ *    ("workspace") is passed in by the caller, sized by the matching *_bytes
+ *    query.
+ *  - The return value is a status: 0 = MR_OK, negative on error (see
+ *    mr_status_string).  No exception or abort crosses the ABI.
+ *
+ * Weight layout: a layer's weight is (rows = out_features, cols = in_features);
+ * a quantization group is `group` consecutive elements of a row, so the
+ * grouped view (rows, cols/group, group) of the reference is the same bytes.
+ * V has the weight's shape; alpha and beta are (rows, cols/group).
+ * Supported on the device: asymmetric observed-range schemes, bits 2..8,
+ * group in {8, 16, 32, 64, 128, 256} dividing cols.
+ */
+#ifndef MROUND_B200_H_
+#define MROUND_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MR_OK = 0,
+  MR_ERR_ARGUMENT = -1,   /* bad shape, bits, group or size */
+  MR_ERR_ALIGNMENT = -2,  /* a pointer or leading dimension is misaligned */
+  MR_ERR_LAUNCH = -3,     /* a CUDA launch or runtime call failed */
+  MR_ERR_DEVICE = -4,     /* no sm_100 device, or the device is unusable */
+  MR_ERR_TIMEOUT = -5,    /* a bounded device-side wait gave up */
+  MR_ERR_WORKSPACE = -6   /* workspace pointer missing or too small */
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mr_version(void);
+
+/* Static description of a status code. */
+const char* mr_status_string(int status);
+
+/* 0 when the current device is an sm_100 part the library was built for. */
+int mr_device_check(void);
+
+/* Last CUDA error string seen by the library on this host thread. */
+const char* mr_last_cuda_error(void);
+
+/*
+ * K1 -- fused asymmetric fake-quant forward.
+ * Replaces fake_quantize (mround/core/quantizer.py:287-347, asym branch
+ * 341-347) as called by _TunableLinear.__call__ (mround/pipeline/runner.py:364-366).
+ *   scale = max((max(gmax,0)*alpha - min(gmin,0)*beta) / (2^bits-1), eps)
+ *   zp    = rint(-w_min / scale)
+ *   q     = clamp(rint(w/scale + v) + zp, 0, 2^bits-1)
+ *   wq    = scale * (q - zp)
+ * Outputs (any may be NULL): wq_hi = bf16(wq), wq_lo = bf16(wq - wq_hi) (the
+ * split that lets two bf16 GEMM operands carry a float32 weight), wq_f32,
+ * scale and zp per group (float32, (rows, cols/group)).
+ * IEEE division and ties-to-even rounding: codes are bit-exact.
+ */
+int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
+                  const float* beta, int64_t rows, int64_t cols, int group, int bits,
+                  float eps, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_f32,
+                  float* scale, float* zp, void* stream);
+
+/*
+ * K2 -- straight-through backward fused with signSGD and projection.
+ * Replaces the autodiff of fake_quantize (mround/core/quantizer.py:110-149,
+ * 254-266, 341-345; hand form mround/reference/quantize.py:488-520) and
+ * SignSGD.apply + project_params (mround/core/signsgd.py:125-145,
+ * mround/core/quantizer.py:430-446; called at mround/pipeline/runner.py:926-931).
+ * gq = dL/dwq, float32 (rows, cols).  With update != 0, V, alpha and beta are
+ * updated in place:  p <- clip(p - lr*sign(g_p), lo, hi)  (V bounded by 0.5,
+ * alpha and beta by [coef_lo, coef_hi]).
+ * Optional outputs (NULL to skip): the gradients gv (rows, cols), galpha and
+ * gbeta (rows, cols/group); and, when update != 0, the NEXT step's operands
+ * wq_hi/wq_lo recomputed from the updated parameters (fusing K1).
+ */
+int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
+                   float* beta, int64_t rows, int64_t cols, int group, int bits,
+                   float eps, float lr, float coef_lo, float coef_hi, int update,
+                   float* gv, float* galpha, float* gbeta, uint16_t* wq_hi,
+                   uint16_t* wq_lo, void* stream);
+
+/*
+ * K5 -- commit and MLX packing in one pass.
+ * Replaces quantize_codes (mround/core/quantizer.py:395-398), narrow_codes
+ * (mround/formats/mlx_export.py:109-125), pack_codes
+ * (mround/formats/packing.py:119-163) and to_affine
+ * (mround/formats/mlx_export.py:159-195) for asymmetric schemes:
+ *   packed (rows, cols*bits/32) uint32, element 0 in the least significant
+ *   bits; 2/4/8 bits tile words, 3/5/6/7 form a little-endian bitstream;
+ *   scales = bf16(scale), biases = bf16(-scales * bf16(zp)), (rows, cols/group).
+ * codes (uint8, rows x cols) is optional.  Bit-exact.
+ * cols must be a multiple of 32 for 3/5/6/7 bits and of 32/bits otherwise.
+ */
+int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* alpha,
+                const float* beta, int64_t rows, int64_t cols, int group, int bits,
+                float eps, uint32_t* packed, uint16_t* scales_bf16,
+                uint16_t* biases_bf16, uint8_t* codes, void* stream);
+
+/*
+ * K4 -- block-output loss, the exact global outlier threshold and dL/dpred.
+ * Replaces reconstruction_loss / outlier_suppressed_loss / outlier_threshold /
+ * piece_loss (mround/core/losses.py:42-56, 59-93, 96-107, 110-130; called at
+ * mround/pipeline/runner.py:866).
+ *   r = pred - target (float32), n elements.
+ *   suppress: thr = k-th largest |r| (radix select, exact), keep = |r| < thr.
+ *   loss = sum((r*keep)^2) / denom   (float64, written to *loss)
+ *   grad = 2 * r * keep / denom      (float32, may be NULL)
+ * `denom` is the element count of the whole batch (a piece passes the whole
+ * batch's count).  thr_in >= 0 skips the selection and uses that threshold
+ * (micro-batch pieces); otherwise the selected threshold is written to
+ * *thr_out (device float, may be NULL).  `workspace` must hold
+ * mr_loss_workspace_bytes() bytes.
+ */
+size_t mr_loss_workspace_bytes(void);
+int mr_loss_outlier(const float* pred, const float* target, int64_t n, int64_t k,
+                    int suppress, double denom, float thr_in, float* grad,
+                    double* loss, float* thr_out, void* workspace, void* stream);
+
+/*
+ * K4, distributed form: one radix pass of the global threshold selection.
+ * pass = 0, 1, 2 over key bits [21,31), [10,21), [0,10) of |r|.  Each pass
+ * writes this rank's histogram of the candidates to hist (2048 uint32); the
+ * caller sums hist across ranks (an all-reduce) and then calls
+ * mr_loss_select_digit, which narrows the device-side selection state.
+ * mr_loss_outlier uses the same passes with no exchange.
+ */
+int mr_loss_hist_pass(const float* pred, const float* target, int64_t n, int pass,
+                      const void* state, uint32_t* hist, void* stream);
+int mr_loss_select_digit(const uint32_t* hist, int64_t k, int pass, void* state,
+                         float* thr_out, void* stream);
+int mr_loss_apply(const float* pred, const float* target, int64_t n, double denom,
+                  const float* thr_dev, int suppress, float* grad, double* loss,
+                  void* workspace, void* stream);
+
+/*
+ * K6 -- DeltaLoss reduction for the mixed-precision planner.
+ * Replaces the per-layer term of _accumulate (mround/pipeline/scoring.py:262,
+ * definition mround/planner/sensitivity.py:190-229):
+ *   out[j] += sum |g * (RTN_{bits[j]}(w) - w)|   for j < n_bits,
+ * RTN being the quantizer with v = 0 and unit coefficients.  Float64
+ * accumulation.  out is device memory (n_bits doubles), accumulated into.
+ */
+int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t cols,
+                 int group, const int* bits, int n_bits, float eps, double* out,
+                 void* stream);
+
+/*
+ * Operand preparation for the split-precision GEMMs: x (float32, n elements)
+ * -> hi = bf16(x), lo = bf16(x - hi) (lo may be NULL).
+ */
+int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MROUND_B200_H_ */

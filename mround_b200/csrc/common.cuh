@@ -1,0 +1,68 @@
+// Shared device helpers of libmround_b200 (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/mround_b200.h"
+
+namespace mr {
+
+constexpr int kSMs = 148;  // B200: 2 dies x 74 SMs
+
+// Record the last CUDA error string for mr_last_cuda_error().
+void set_cuda_error(cudaError_t e);
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return MR_ERR_LAUNCH;
+  }
+  return MR_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Grid size: a multiple of the SM count, capped by the work available.
+inline int grid_for(int64_t work_items, int threads, int per_sm = 8) {
+  int64_t want = (work_items + threads - 1) / threads;
+  int64_t cap = int64_t(kSMs) * per_sm;
+  if (want < 1) want = 1;
+  return int(want < cap ? want : cap);
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) {
+  return __uint_as_float(uint32_t(b) << 16);
+}
+
+// float32 -> bfloat16, round to nearest even (finite inputs).
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// Unpack 8 bf16 held in a uint4 into floats (exact).
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const uint16_t (&h)[8]) {
+  uint4 u;
+  u.x = uint32_t(h[0]) | (uint32_t(h[1]) << 16);
+  u.y = uint32_t(h[2]) | (uint32_t(h[3]) << 16);
+  u.z = uint32_t(h[4]) | (uint32_t(h[5]) << 16);
+  u.w = uint32_t(h[6]) | (uint32_t(h[7]) << 16);
+  return u;
+}
+
+// Streaming loads/stores: the weight-sized tensors are touched once per pass.
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) { return __ldcs(p); }
+__device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
+
+}  // namespace mr

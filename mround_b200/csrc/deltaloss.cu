@@ -1,0 +1,131 @@
+// K6 -- DeltaLoss sensitivity reduction: out[j] += sum |g * (RTN_bits[j](w) - w)|.
+//
+// One pass over the layer's gradient (float32) and weight (bf16) evaluates
+// every candidate width in registers: the round-to-nearest quantize-dequantize
+// at width b is the asymmetric quantizer with v = 0 and unit clipping
+// coefficients (reference mround/pipeline/scoring.py:213-221), recomputed from
+// the group extremes rather than stored.  The per-element term is float32, as
+// the reference's ``mx.sum(mx.abs(gradient * perturbation))``
+// (mround/pipeline/scoring.py:262) forms it; accumulation is float64
+// (mround/planner/sensitivity.py:190-229).  Same warp-tile layout as the
+// quantizer kernels: 8 elements per lane, a group over group/8 lanes.
+
+#include "common.cuh"
+
+namespace mr {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTile = 256;
+constexpr int kMaxWidths = 8;
+
+struct Widths {
+  int n;
+  float maxq[kMaxWidths];
+};
+
+template <int LPG>
+__global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __restrict__ g,
+                                                             const uint16_t* __restrict__ w,
+                                                             int64_t n, Widths widths, float eps,
+                                                             double* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  double acc[kMaxWidths];
+#pragma unroll
+  for (int j = 0; j < kMaxWidths; ++j) acc[j] = 0.0;
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
+       t += int64_t(gridDim.x) * kWarps) {
+    const int64_t e = t * kTile + lane * 8;
+    const bool in = e < n;
+    float wf[8], gf[8];
+    if (in) {
+      unpack8(__ldcs(reinterpret_cast<const uint4*>(w + e)), wf);
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(g + e));
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(g + e) + 1);
+      gf[0] = a.x; gf[1] = a.y; gf[2] = a.z; gf[3] = a.w;
+      gf[4] = b.x; gf[5] = b.y; gf[6] = b.z; gf[7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wf[i] = gf[i] = 0.f;
+    }
+    float gmax = wf[0], gmin = wf[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) {
+      gmax = fmaxf(gmax, wf[i]);
+      gmin = fminf(gmin, wf[i]);
+    }
+#pragma unroll
+    for (int off = 1; off < LPG; off <<= 1) {
+      gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
+      gmin = fminf(gmin, __shfl_xor_sync(0xffffffffu, gmin, off));
+    }
+    if (!in) continue;
+    const float w_max = gmax > 0.f ? gmax : 0.f;
+    const float w_min = gmin < 0.f ? gmin : 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxWidths; ++j) {
+      if (j >= widths.n) break;
+      const float maxq = widths.maxq[j];
+      const float scale = fmaxf(__fdiv_rn(__fsub_rn(w_max, w_min), maxq), eps);
+      const float zp = rintf(__fdiv_rn(-w_min, scale));
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = __fadd_rn(rintf(__fdiv_rn(wf[i], scale)), zp);
+        const float q = __fmul_rn(scale, __fsub_rn(fminf(fmaxf(x, 0.f), maxq), zp));
+        part = __fadd_rn(part, fabsf(__fmul_rn(gf[i], __fsub_rn(q, wf[i]))));
+      }
+      acc[j] += double(part);
+    }
+  }
+  __shared__ double sh[kWarps][kMaxWidths];
+#pragma unroll
+  for (int j = 0; j < kMaxWidths; ++j) {
+    double a = acc[j];
+    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    if (lane == 0) sh[threadIdx.x >> 5][j] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x < widths.n) {
+    double s = 0.0;
+    for (int wi = 0; wi < kWarps; ++wi) s += sh[wi][threadIdx.x];
+    atomicAdd(&out[threadIdx.x], s);
+  }
+}
+
+}  // namespace
+}  // namespace mr
+
+using namespace mr;
+
+extern "C" int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t cols,
+                            int group, const int* bits, int n_bits, float eps, double* out,
+                            void* stream) {
+  if (!g || !w_bf16 || !bits || !out || rows <= 0 || cols <= 0) return MR_ERR_ARGUMENT;
+  if (n_bits < 1 || n_bits > kMaxWidths) return MR_ERR_ARGUMENT;
+  if (group != 8 && group != 16 && group != 32 && group != 64 && group != 128 && group != 256)
+    return MR_ERR_ARGUMENT;
+  if (cols % group) return MR_ERR_ARGUMENT;
+  if (!aligned16(g) || !aligned16(w_bf16)) return MR_ERR_ALIGNMENT;
+  Widths widths{};
+  widths.n = n_bits;
+  for (int j = 0; j < n_bits; ++j) {
+    if (bits[j] < 2 || bits[j] > 8) return MR_ERR_ARGUMENT;
+    widths.maxq[j] = float((1 << bits[j]) - 1);
+  }
+  const int64_t n = rows * cols;
+  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (group / 8) {
+    case 1: deltaloss_kernel<1><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
+    case 2: deltaloss_kernel<2><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
+    case 4: deltaloss_kernel<4><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
+    case 8: deltaloss_kernel<8><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
+    case 16: deltaloss_kernel<16><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
+    case 32: deltaloss_kernel<32><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
+    default: return MR_ERR_ARGUMENT;
+  }
+  return launch_status();
+}

@@ -1,0 +1,386 @@
+// K1 (fake-quant forward), K2 (straight-through backward + signSGD +
+// projection, optionally fused with the next step's K1) and K5 (codes + MLX
+// uint32 packing + affine scales/biases).
+//
+// Work decomposition, shared by the three kernels: the weight is a flat
+// stream of rows*cols elements in which every quantization group is `group`
+// consecutive elements.  A warp owns a 256-element tile; each lane owns 8
+// consecutive elements (one 16-byte bf16 load of W, two 16-byte float loads
+// of V or of the gradient), so a group spans group/8 adjacent lanes and its
+// extremes and gradient sums are warp-shuffle reductions over those lanes.
+// Groups never straddle a tile because group divides 256.
+//
+// Arithmetic follows the float32 operation order of the reference quantizer
+// (mround/core/quantizer.py:185-195, 254-266, 341-347, 395-398) with IEEE
+// division (__fdiv_rn) and ties-to-even rounding (rintf), and no contraction
+// into FMA on the code path, so codes and reconstructions are bit-exact
+// against a float32 implementation of the same formulas.
+
+#include "common.cuh"
+
+namespace mr {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTile = 256;  // elements per warp tile
+
+struct GroupQ {
+  float scale, zp, w_min, wmax_raw, wmin_raw;
+  bool live;  // scale above the eps floor, i.e. a function of alpha/beta
+};
+
+template <int LPG>
+__device__ __forceinline__ void group_extremes(const float (&w)[8], float& gmax, float& gmin) {
+  gmax = w[0];
+  gmin = w[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    gmax = fmaxf(gmax, w[i]);
+    gmin = fminf(gmin, w[i]);
+  }
+#pragma unroll
+  for (int off = 1; off < LPG; off <<= 1) {
+    gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
+    gmin = fminf(gmin, __shfl_xor_sync(0xffffffffu, gmin, off));
+  }
+}
+
+template <int LPG>
+__device__ __forceinline__ float group_sum(float x) {
+#pragma unroll
+  for (int off = 1; off < LPG; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+
+// scale and zero point of one group (reference asymmetric_scale).
+__device__ __forceinline__ GroupQ group_params(float gmax, float gmin, float alpha, float beta,
+                                               float maxq, float eps) {
+  GroupQ q;
+  q.wmax_raw = gmax > 0.f ? gmax : 0.f;
+  q.wmin_raw = gmin < 0.f ? gmin : 0.f;
+  const float w_max = __fmul_rn(q.wmax_raw, alpha);
+  const float w_min = __fmul_rn(q.wmin_raw, beta);
+  const float span = __fdiv_rn(__fsub_rn(w_max, w_min), maxq);
+  q.live = span > eps;
+  q.scale = fmaxf(span, eps);
+  q.zp = rintf(__fdiv_rn(-w_min, q.scale));
+  q.w_min = w_min;
+  return q;
+}
+
+// x = rint(w/scale + v) + zp, before the clamp.
+__device__ __forceinline__ float unclamped_code(float w, float v, const GroupQ& q) {
+  return __fadd_rn(rintf(__fadd_rn(__fdiv_rn(w, q.scale), v)), q.zp);
+}
+
+__device__ __forceinline__ float clamp_code(float x, float maxq) {
+  return fminf(fmaxf(x, 0.f), maxq);
+}
+
+__device__ __forceinline__ float dequant(float code, const GroupQ& q) {
+  return __fmul_rn(q.scale, __fsub_rn(code, q.zp));
+}
+
+__device__ __forceinline__ float signf(float x) {
+  return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+}
+
+__device__ __forceinline__ void load_f8(const float* p, float (&x)[8]) {
+  const float4 a = ld_stream(reinterpret_cast<const float4*>(p));
+  const float4 b = ld_stream(reinterpret_cast<const float4*>(p) + 1);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+__device__ __forceinline__ void store_f8(float* p, const float (&x)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+__device__ __forceinline__ void store_split(const float (&wq)[8], int64_t e, uint16_t* hi,
+                                            uint16_t* lo) {
+  uint16_t h[8], l[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[i] = f32_to_bf16(wq[i]);
+    l[i] = f32_to_bf16(__fsub_rn(wq[i], bf16_to_f32(h[i])));
+  }
+  if (hi) *reinterpret_cast<uint4*>(hi + e) = pack8(h);
+  if (lo) *reinterpret_cast<uint4*>(lo + e) = pack8(l);
+}
+
+// ---------------------------------------------------------------- K1
+template <int LPG>
+__global__ void __launch_bounds__(kThreads) fq_forward_kernel(
+    const uint16_t* __restrict__ w, const float* __restrict__ v, const float* __restrict__ alpha,
+    const float* __restrict__ beta, int64_t n, int group, float maxq, float eps,
+    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo, float* __restrict__ wq_f32,
+    float* __restrict__ scale_out, float* __restrict__ zp_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
+       t += int64_t(gridDim.x) * kWarps) {
+    const int64_t e = t * kTile + lane * 8;
+    const bool in = e < n;
+    float wf[8], vf[8];
+    if (in) {
+      unpack8(ld_stream(reinterpret_cast<const uint4*>(w + e)), wf);
+      load_f8(v + e, vf);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wf[i] = vf[i] = 0.f;
+    }
+    float gmax, gmin;
+    group_extremes<LPG>(wf, gmax, gmin);
+    if (!in) continue;  // whole groups lie past the end together
+    const int64_t gi = e / group;
+    const GroupQ q = group_params(gmax, gmin, alpha[gi], beta[gi], maxq, eps);
+    float wq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wq[i] = dequant(clamp_code(unclamped_code(wf[i], vf[i], q), maxq), q);
+    store_split(wq, e, wq_hi, wq_lo);
+    if (wq_f32) store_f8(wq_f32 + e, wq);
+    if ((lane & (LPG - 1)) == 0) {
+      if (scale_out) scale_out[gi] = q.scale;
+      if (zp_out) zp_out[gi] = q.zp;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- K2
+template <int LPG>
+__global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
+    const float* __restrict__ gq, const uint16_t* __restrict__ w, float* __restrict__ v,
+    float* __restrict__ alpha, float* __restrict__ beta, int64_t n, int group, float maxq,
+    float eps, float lr, float lo, float hi, int update, float* __restrict__ gv_out,
+    float* __restrict__ ga_out, float* __restrict__ gb_out, uint16_t* __restrict__ wq_hi,
+    uint16_t* __restrict__ wq_lo) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
+       t += int64_t(gridDim.x) * kWarps) {
+    const int64_t e = t * kTile + lane * 8;
+    const bool in = e < n;
+    float wf[8], vf[8], g[8];
+    if (in) {
+      unpack8(ld_stream(reinterpret_cast<const uint4*>(w + e)), wf);
+      load_f8(v + e, vf);
+      load_f8(gq + e, g);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wf[i] = vf[i] = g[i] = 0.f;
+    }
+    float gmax, gmin;
+    group_extremes<LPG>(wf, gmax, gmin);
+    const int64_t gi = in ? e / group : 0;
+    const float a = in ? alpha[gi] : 1.f;
+    const float b = in ? beta[gi] : 1.f;
+    const GroupQ q = group_params(gmax, gmin, a, b, maxq, eps);
+
+    float gv[8];
+    float sum_t = 0.f, sum_out = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = unclamped_code(wf[i], vf[i], q);
+      const bool inside = (x >= 0.f) && (x <= maxq);
+      const float code = clamp_code(x, maxq);
+      const float cz = __fsub_rn(code, q.zp);
+      // d(wq)/d(scale): (code - zp) - w/scale inside the clamp, (code - zp) - w_min/scale outside
+      const float d = inside ? __fsub_rn(cz, __fdiv_rn(wf[i], q.scale))
+                             : __fsub_rn(cz, __fdiv_rn(q.w_min, q.scale));
+      sum_t = __fadd_rn(sum_t, __fmul_rn(g[i], d));
+      if (!inside) sum_out = __fadd_rn(sum_out, g[i]);
+      gv[i] = inside ? __fmul_rn(g[i], q.scale) : 0.f;
+    }
+    sum_t = group_sum<LPG>(sum_t);
+    sum_out = group_sum<LPG>(sum_out);
+    if (!in) continue;
+    const float gs = q.live ? __fdiv_rn(sum_t, maxq) : 0.f;
+    const float ga = __fmul_rn(gs, q.wmax_raw);
+    const float gb = __fmul_rn(__fsub_rn(sum_out, gs), q.wmin_raw);
+    const bool leader = (lane & (LPG - 1)) == 0;
+    if (gv_out) store_f8(gv_out + e, gv);
+    if (leader) {
+      if (ga_out) ga_out[gi] = ga;
+      if (gb_out) gb_out[gi] = gb;
+    }
+    if (!update) continue;
+    float vn[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      vn[i] = fminf(fmaxf(__fsub_rn(vf[i], __fmul_rn(lr, signf(gv[i]))), -0.5f), 0.5f);
+    const float an = fminf(fmaxf(__fsub_rn(a, __fmul_rn(lr, signf(ga))), lo), hi);
+    const float bn = fminf(fmaxf(__fsub_rn(b, __fmul_rn(lr, signf(gb))), lo), hi);
+    store_f8(v + e, vn);
+    if (leader) {
+      alpha[gi] = an;
+      beta[gi] = bn;
+    }
+    if (wq_hi || wq_lo) {
+      const GroupQ qn = group_params(gmax, gmin, an, bn, maxq, eps);
+      float wq[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        wq[i] = dequant(clamp_code(unclamped_code(wf[i], vn[i], qn), maxq), qn);
+      store_split(wq, e, wq_hi, wq_lo);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- K5
+template <int LPG>
+__global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
+    const uint16_t* __restrict__ w, const float* __restrict__ v, const float* __restrict__ alpha,
+    const float* __restrict__ beta, int64_t n, int group, int bits, float maxq, float eps,
+    uint32_t* __restrict__ packed, uint16_t* __restrict__ scales, uint16_t* __restrict__ biases,
+    uint8_t* __restrict__ codes_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  const int64_t total_words = n * bits / 32;
+  const int chunk_bits = 8 * bits;  // bits one lane contributes, 16..64
+  for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
+       t += int64_t(gridDim.x) * kWarps) {
+    const int64_t e = t * kTile + lane * 8;
+    const bool in = e < n;
+    float wf[8], vf[8];
+    if (in) {
+      unpack8(ld_stream(reinterpret_cast<const uint4*>(w + e)), wf);
+      load_f8(v + e, vf);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wf[i] = vf[i] = 0.f;
+    }
+    float gmax, gmin;
+    group_extremes<LPG>(wf, gmax, gmin);
+    uint64_t chunk = 0;
+    if (in) {
+      const int64_t gi = e / group;
+      const GroupQ q = group_params(gmax, gmin, alpha[gi], beta[gi], maxq, eps);
+      uint8_t c8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t c = uint32_t(clamp_code(unclamped_code(wf[i], vf[i], q), maxq));
+        c8[i] = uint8_t(c);
+        chunk |= uint64_t(c) << (i * bits);
+      }
+      if (codes_out) {
+        uint2 u;
+        u.x = uint32_t(c8[0]) | (uint32_t(c8[1]) << 8) | (uint32_t(c8[2]) << 16) | (uint32_t(c8[3]) << 24);
+        u.y = uint32_t(c8[4]) | (uint32_t(c8[5]) << 8) | (uint32_t(c8[6]) << 16) | (uint32_t(c8[7]) << 24);
+        *reinterpret_cast<uint2*>(codes_out + e) = u;
+      }
+      if ((lane & (LPG - 1)) == 0) {
+        const uint16_t sb = f32_to_bf16(q.scale);
+        const uint16_t zb = f32_to_bf16(q.zp);
+        scales[gi] = sb;
+        biases[gi] = f32_to_bf16(__fmul_rn(-bf16_to_f32(sb), bf16_to_f32(zb)));
+      }
+    }
+    // Word j of this tile takes its bits from lane j*32/chunk_bits and the
+    // next one; a tile holds 8*bits words, so each lane forms up to two.
+#pragma unroll
+    for (int j = lane; j < 64; j += 32) {
+      const int bitpos = j * 32;
+      const int src = bitpos / chunk_bits;
+      const int off = bitpos - src * chunk_bits;
+      const uint32_t lo0 = __shfl_sync(0xffffffffu, uint32_t(chunk), src & 31);
+      const uint32_t hi0 = __shfl_sync(0xffffffffu, uint32_t(chunk >> 32), src & 31);
+      const uint32_t lo1 = __shfl_sync(0xffffffffu, uint32_t(chunk), (src + 1) & 31);
+      const uint32_t hi1 = __shfl_sync(0xffffffffu, uint32_t(chunk >> 32), (src + 1) & 31);
+      if (j < chunk_bits) {
+        const uint64_t c0 = (uint64_t(hi0) << 32) | lo0;
+        const uint64_t c1 = (src + 1 < 32) ? ((uint64_t(hi1) << 32) | lo1) : 0ull;
+        uint64_t word = c0 >> off;
+        const int up = chunk_bits - off;
+        if (up < 64) word |= c1 << up;
+        const int64_t wi = t * (kTile * bits / 32) + j;
+        if (wi < total_words) packed[wi] = uint32_t(word);
+      }
+    }
+  }
+}
+
+int check_common(const void* w, const void* v, int64_t rows, int64_t cols, int group, int bits) {
+  if (rows <= 0 || cols <= 0) return MR_ERR_ARGUMENT;
+  if (bits < 2 || bits > 8) return MR_ERR_ARGUMENT;
+  if (group != 8 && group != 16 && group != 32 && group != 64 && group != 128 && group != 256)
+    return MR_ERR_ARGUMENT;
+  if (cols % group) return MR_ERR_ARGUMENT;
+  if (!w || !v) return MR_ERR_ARGUMENT;
+  if (!aligned16(w) || !aligned16(v)) return MR_ERR_ALIGNMENT;
+  return MR_OK;
+}
+
+}  // namespace
+}  // namespace mr
+
+using namespace mr;
+
+#define MR_DISPATCH_LPG(group, KERNEL, GRID, STREAM, ...)                             \
+  switch ((group) / 8) {                                                             \
+    case 1: KERNEL<1><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
+    case 2: KERNEL<2><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
+    case 4: KERNEL<4><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
+    case 8: KERNEL<8><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
+    case 16: KERNEL<16><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
+    case 32: KERNEL<32><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
+    default: return MR_ERR_ARGUMENT;                                                 \
+  }
+
+extern "C" int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
+                             const float* beta, int64_t rows, int64_t cols, int group, int bits,
+                             float eps, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_f32,
+                             float* scale, float* zp, void* stream) {
+  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  if (st) return st;
+  if (!alpha || !beta) return MR_ERR_ARGUMENT;
+  if ((wq_hi && !aligned16(wq_hi)) || (wq_lo && !aligned16(wq_lo)) || (wq_f32 && !aligned16(wq_f32)))
+    return MR_ERR_ALIGNMENT;
+  const int64_t n = rows * cols;
+  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
+  const float maxq = float((1 << bits) - 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MR_DISPATCH_LPG(group, fq_forward_kernel, grid, s, w_bf16, v, alpha, beta, n, group, maxq, eps,
+                  wq_hi, wq_lo, wq_f32, scale, zp);
+  return launch_status();
+}
+
+extern "C" int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
+                              float* beta, int64_t rows, int64_t cols, int group, int bits,
+                              float eps, float lr, float coef_lo, float coef_hi, int update,
+                              float* gv, float* galpha, float* gbeta, uint16_t* wq_hi,
+                              uint16_t* wq_lo, void* stream) {
+  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  if (st) return st;
+  if (!gq || !alpha || !beta) return MR_ERR_ARGUMENT;
+  if (!aligned16(gq) || (gv && !aligned16(gv)) || (wq_hi && !aligned16(wq_hi)) ||
+      (wq_lo && !aligned16(wq_lo)))
+    return MR_ERR_ALIGNMENT;
+  const int64_t n = rows * cols;
+  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
+  const float maxq = float((1 << bits) - 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MR_DISPATCH_LPG(group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, n, group, maxq,
+                  eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo);
+  return launch_status();
+}
+
+extern "C" int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* alpha,
+                           const float* beta, int64_t rows, int64_t cols, int group, int bits,
+                           float eps, uint32_t* packed, uint16_t* scales_bf16,
+                           uint16_t* biases_bf16, uint8_t* codes, void* stream) {
+  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  if (st) return st;
+  if (!alpha || !beta || !packed || !scales_bf16 || !biases_bf16) return MR_ERR_ARGUMENT;
+  if (32 % bits == 0 ? (cols % (32 / bits)) : (cols % 32)) return MR_ERR_ARGUMENT;
+  if (codes && (reinterpret_cast<uintptr_t>(codes) & 7u)) return MR_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(packed) & 3u) return MR_ERR_ALIGNMENT;
+  const int64_t n = rows * cols;
+  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
+  const float maxq = float((1 << bits) - 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MR_DISPATCH_LPG(group, pack_mlx_kernel, grid, s, w_bf16, v, alpha, beta, n, group, bits, maxq,
+                  eps, packed, scales_bf16, biases_bf16, codes);
+  return launch_status();
+}

@@ -1,0 +1,211 @@
+"""Torch-tensor front end of the native kernels (the ``mround/kernels`` slot).
+
+Each function validates the tensors it is handed (device, dtype, contiguity,
+shape), passes raw pointers and the current CUDA stream to one C entry point
+of ``libmround_b200.so``, and returns without synchronizing.  Every function
+runs only on the GPU: a CPU tensor is refused with ``PlatformError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from mround_b200._native import check, lib
+from mround_b200.exceptions import PlatformError, SchemeError
+
+__all__ = [
+    "LossWorkspace",
+    "deltaloss",
+    "fq_forward",
+    "gemm",
+    "loss_apply",
+    "loss_hist_pass",
+    "loss_outlier",
+    "loss_select_digit",
+    "pack_mlx",
+    "split_bf16",
+    "ste_signsgd",
+]
+
+DEVICE_GROUPS = (8, 16, 32, 64, 128, 256)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None, dtype: torch.dtype, name: str, numel: int | None = None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise PlatformError(f"{name} must be a CUDA tensor (the tuning path has no CPU fallback)")
+    if t.dtype != dtype:
+        raise SchemeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise SchemeError(f"{name} must be contiguous")
+    if numel is not None and t.numel() != numel:
+        raise SchemeError(f"{name} has {t.numel()} elements, expected {numel}")
+    return t.data_ptr()
+
+
+def _weight_args(w, v, alpha, beta, group):
+    if w.dim() != 2:
+        raise SchemeError(f"expected a 2-D weight, got shape {tuple(w.shape)}")
+    rows, cols = w.shape
+    if group not in DEVICE_GROUPS or cols % group:
+        raise SchemeError(f"group {group} is not supported on the device for {cols} columns")
+    ng = rows * (cols // group)
+    return (
+        rows,
+        cols,
+        _ptr(w, torch.bfloat16, "w", rows * cols),
+        _ptr(v, torch.float32, "v", rows * cols),
+        _ptr(alpha, torch.float32, "alpha", ng),
+        _ptr(beta, torch.float32, "beta", ng),
+    )
+
+
+def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=None, wq_lo=None,
+               wq_f32=None, scale=None, zp=None) -> None:
+    """K1: write the fake-quantized weight (bf16 hi/lo split and/or float32)."""
+    rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
+    n, ng = rows * cols, rows * (cols // group)
+    status = lib().mr_fq_forward(
+        pw, pv, pa, pb, rows, cols, group, bits, eps,
+        _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
+        _ptr(wq_f32, torch.float32, "wq_f32", n), _ptr(scale, torch.float32, "scale", ng),
+        _ptr(zp, torch.float32, "zp", ng), _stream())
+    check(status, "mr_fq_forward")
+
+
+def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr: float,
+                lo: float, hi: float, update: bool = True, gv=None, galpha=None, gbeta=None,
+                wq_hi=None, wq_lo=None) -> None:
+    """K2: straight-through gradients, then (if ``update``) the signed step in place."""
+    rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
+    n, ng = rows * cols, rows * (cols // group)
+    status = lib().mr_ste_signsgd(
+        _ptr(gq, torch.float32, "gq", n), pw, pv, pa, pb, rows, cols, group, bits, eps, lr, lo,
+        hi, int(bool(update)), _ptr(gv, torch.float32, "gv", n),
+        _ptr(galpha, torch.float32, "galpha", ng), _ptr(gbeta, torch.float32, "gbeta", ng),
+        _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
+        _stream())
+    check(status, "mr_ste_signsgd")
+
+
+def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes: bool = False):
+    """K5: ``(packed uint32 as int32, scales bf16, biases bf16, codes uint8 or None)``."""
+    rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
+    if 32 % bits == 0:
+        if cols % (32 // bits):
+            raise SchemeError(f"cols={cols} does not tile {bits}-bit words")
+        words = cols // (32 // bits)
+    else:
+        if cols % 32:
+            raise SchemeError(f"cols={cols} is not a multiple of 32 at {bits} bits")
+        words = cols // 32 * bits
+    dev = w.device
+    packed = torch.empty((rows, words), dtype=torch.int32, device=dev)
+    scales = torch.empty((rows, cols // group), dtype=torch.bfloat16, device=dev)
+    biases = torch.empty_like(scales)
+    codes = torch.empty((rows, cols), dtype=torch.uint8, device=dev) if want_codes else None
+    status = lib().mr_pack_mlx(
+        pw, pv, pa, pb, rows, cols, group, bits, eps, packed.data_ptr(), scales.data_ptr(),
+        biases.data_ptr(), None if codes is None else codes.data_ptr(), _stream())
+    check(status, "mr_pack_mlx")
+    return packed, scales, biases, codes
+
+
+class LossWorkspace:
+    """Device scratch of the loss kernels (selection state, histogram, partial sums)."""
+
+    def __init__(self, device: torch.device | str = "cuda") -> None:
+        nbytes = int(lib().mr_loss_workspace_bytes())
+        self.buffer = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.loss = torch.zeros((), dtype=torch.float64, device=device)
+        self.thr = torch.zeros((), dtype=torch.float32, device=device)
+        self.hist = torch.zeros(2048, dtype=torch.int32, device=device)
+
+    @property
+    def ptr(self) -> int:
+        return self.buffer.data_ptr()
+
+
+def loss_outlier(pred, target, ws: LossWorkspace, *, suppress: bool, denom: float, k: int,
+                 grad=None, threshold: float | None = None) -> None:
+    """K4 single-device: loss into ``ws.loss``, threshold into ``ws.thr``, grad optional."""
+    n = pred.numel()
+    pp = _ptr(pred, torch.float32, "pred")
+    pt = _ptr(target, torch.float32, "target", n)
+    status = lib().mr_loss_outlier(
+        pp, pt, n, int(k), int(bool(suppress)), float(denom),
+        -1.0 if threshold is None else float(threshold), _ptr(grad, torch.float32, "grad", n),
+        ws.loss.data_ptr(), ws.thr.data_ptr(), ws.ptr, _stream())
+    check(status, "mr_loss_outlier")
+
+
+def loss_hist_pass(pred, target, ws: LossWorkspace, pass_index: int) -> torch.Tensor:
+    """One radix pass of the threshold selection; returns this rank's histogram."""
+    n = pred.numel()
+    status = lib().mr_loss_hist_pass(
+        _ptr(pred, torch.float32, "pred"), _ptr(target, torch.float32, "target", n), n,
+        int(pass_index), ws.ptr, ws.hist.data_ptr(), _stream())
+    check(status, "mr_loss_hist_pass")
+    return ws.hist
+
+
+def loss_select_digit(ws: LossWorkspace, k: int, pass_index: int) -> None:
+    """Narrow the selection with the (possibly all-reduced) histogram in ``ws.hist``."""
+    status = lib().mr_loss_select_digit(ws.hist.data_ptr(), int(k), int(pass_index), ws.ptr,
+                                        ws.thr.data_ptr(), _stream())
+    check(status, "mr_loss_select_digit")
+
+
+def loss_apply(pred, target, ws: LossWorkspace, *, suppress: bool, denom: float, grad=None) -> None:
+    """Loss and gradient with the threshold already in ``ws.thr``."""
+    n = pred.numel()
+    status = lib().mr_loss_apply(
+        _ptr(pred, torch.float32, "pred"), _ptr(target, torch.float32, "target", n), n,
+        float(denom), ws.thr.data_ptr(), int(bool(suppress)), _ptr(grad, torch.float32, "grad", n),
+        ws.loss.data_ptr(), ws.ptr, _stream())
+    check(status, "mr_loss_apply")
+
+
+def deltaloss(g, w, *, bits: list[int] | tuple[int, ...], group: int, eps: float, out) -> None:
+    """K6: ``out[j] += sum |g * (RTN_bits[j](w) - w)|`` (``out`` float64, on device)."""
+    import ctypes
+
+    if w.dim() != 2:
+        raise SchemeError("expected a 2-D weight")
+    rows, cols = w.shape
+    widths = (ctypes.c_int * len(bits))(*[int(b) for b in bits])
+    status = lib().mr_deltaloss(
+        _ptr(g, torch.float32, "g", rows * cols), _ptr(w, torch.bfloat16, "w", rows * cols),
+        rows, cols, group, ctypes.cast(widths, ctypes.c_void_p), len(bits), eps,
+        _ptr(out, torch.float64, "out", len(bits)), _stream())
+    check(status, "mr_deltaloss")
+
+
+def split_bf16(x, hi=None, lo=None, *, want_lo: bool = True):
+    """float32 -> (bf16 hi, bf16 lo); ``hi + lo`` carries 16 significant bits."""
+    n = x.numel()
+    if hi is None:
+        hi = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    if lo is None and want_lo:
+        lo = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    status = lib().mr_split_bf16(_ptr(x, torch.float32, "x"), n, _ptr(hi, torch.bfloat16, "hi", n),
+                                 _ptr(lo, torch.bfloat16, "lo", n) if lo is not None else None,
+                                 _stream())
+    check(status, "mr_split_bf16")
+    return hi, lo
+
+
+def gemm(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool,
+         lda: int, ldb: int, ldc: int, precision: int, bias=None, accumulate: bool = False) -> None:
+    """K3: ``C[m, n] (+)= sum_k A[m, k] B[n, k]`` on the tcgen05 tensor cores."""
+    status = lib().mr_gemm(
+        _ptr(a_hi, torch.bfloat16, "a_hi"), _ptr(a_lo, torch.bfloat16, "a_lo"), lda, int(a_kmajor),
+        _ptr(b_hi, torch.bfloat16, "b_hi"), _ptr(b_lo, torch.bfloat16, "b_lo"), ldb, int(b_kmajor),
+        _ptr(c, torch.float32, "c"), ldc, _ptr(bias, torch.float32, "bias"), int(bool(accumulate)),
+        m, n, k, precision, _stream())
+    check(status, "mr_gemm")

@@ -1,0 +1,58 @@
+"""The C-ABI library loads and exports every symbol the public header declares.
+
+No compute call is made here, so these run without a GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from mround_b200 import _native
+
+
+def test_header_declares_the_kernels():
+    names = _native.declared_symbols()
+    for required in ("mr_fq_forward", "mr_ste_signsgd", "mr_pack_mlx", "mr_loss_outlier",
+                     "mr_deltaloss", "mr_split_bf16"):
+        assert required in names
+
+
+def test_every_declared_symbol_is_exported():
+    handle = ctypes.CDLL(str(_native.LIB_PATH))
+    missing = [n for n in _native.declared_symbols() if not hasattr(handle, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_library_loads_and_reports_version():
+    lib = _native.lib()
+    assert lib.mr_version() == 100
+    assert lib.mr_status_string(0).decode() == "ok"
+    assert "misaligned" in lib.mr_status_string(-2).decode()
+    assert lib.mr_loss_workspace_bytes() > 2048 * 4
+
+
+def test_every_declared_symbol_has_a_signature():
+    for name in _native.declared_symbols():
+        assert name in _native._SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_status_maps_to_exceptions():
+    from mround_b200.exceptions import DeviceError, SchemeError
+
+    _native.check(0, "ok")
+    with pytest.raises(SchemeError):
+        _native.check(-1, "x")
+    with pytest.raises(DeviceError):
+        _native.check(-3, "x")
+
+
+def test_argument_errors_are_refused_before_any_launch():
+    lib = _native.lib()
+    # group 12 is not a device group: refused on the host side of the ABI
+    st = lib.mr_fq_forward(None, None, None, None, 4, 48, 12, 2, 1e-8, None, None, None, None,
+                           None, None)
+    assert st == -1
+    st = lib.mr_pack_mlx(None, None, None, None, 4, 64, 64, 9, 1e-8, None, None, None, None, None)
+    assert st == -1
