@@ -138,6 +138,8 @@ int mr_loss_outlier(const float* pred, const float* target, int64_t n, int64_t k
  * writes this rank's histogram of the candidates to hist (2048 uint32); the
  * caller sums hist across ranks (an all-reduce) and then calls
  * mr_loss_select_digit, which narrows the device-side selection state.
+ * `state` is the workspace of mr_loss_workspace_bytes() (its selection
+ * state comes first).
  * mr_loss_outlier uses the same passes with no exchange.
  */
 int mr_loss_hist_pass(const float* pred, const float* target, int64_t n, int pass,
@@ -165,6 +167,31 @@ int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t c
  * -> hi = bf16(x), lo = bf16(x - hi) (lo may be NULL).
  */
 int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* stream);
+
+/*
+ * K3 -- tcgen05/TMEM GEMM, bf16 operands, float32 accumulate in tensor memory.
+ * The contraction of every decoder-block linear in the tuning step
+ * (mround/pipeline/runner.py:367, y = x @ Wq.T, and the two products its
+ * backward needs, which MLX autodiff forms at runner.py:920).
+ *   C[m, n] (+)= sum_k A[m, k] * B[n, k]   (+ bias[n])
+ * A is K-major (a_kmajor = 1: element (m,k) at a[m*lda + k]) or M-major
+ * (a_kmajor = 0: at a[k*lda + m]); B likewise with N.
+ * precision = 1: a_hi*b_hi.  precision = 2: a_hi*b_hi + a_lo*b_hi (B exact in
+ * bf16).  precision = 3: a_hi*b_hi + a_hi*b_lo + a_lo*b_hi, the split that
+ * carries float32 operands (x = hi + lo) through bf16 tensor cores.
+ * accumulate != 0 adds into C.  Any m, n, k >= 1 (edges are zero-filled by
+ * TMA); leading dimensions multiples of 8 elements; bf16 pointers 16-byte
+ * aligned.  Device-side waits are bounded: a wait that gives up sets a status
+ * word read (synchronously) by mr_gemm_status.
+ */
+int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
+            const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
+            float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
+            int64_t n, int64_t k, int precision, void* stream);
+
+/* Device status word of K3: 0, or MR_ERR_TIMEOUT.  Synchronizes the device;
+ * reset != 0 clears it. */
+int mr_gemm_status(int reset);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,458 @@
+// K3 -- tcgen05/TMEM GEMM for the decoder-block linears (sm_100a).
+//
+//   C[m, n] (+)= sum_k A[m, k] * B[n, k]  (+ bias[n]),  float32 accumulate.
+//
+// Operands are bf16 and may carry a second "lo" part (x = hi + lo, lo =
+// bf16(x - hi)), so float32 activations and fake-quantized weights reach the
+// tensor cores with 16 significant bits: precision 3 issues hi*hi + hi*lo +
+// lo*hi into one TMEM accumulator, precision 2 hi*hi + lo*hi (B exact in
+// bf16), precision 1 hi*hi.
+//
+// Structure (one 128 x BN output tile per CTA, 128 threads):
+//   warp 0, one lane : TMA producer.  Loads 64-wide K slices of A and B (hi
+//                      and lo parts) into a ring of shared-memory stages with
+//                      128-byte swizzle; completion is tracked by the
+//                      stage's "full" mbarrier (transaction bytes).
+//   warp 1           : allocates the TMEM accumulator (BN columns); one lane
+//                      issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K
+//                      step and per product, then tcgen05.commit to the
+//                      stage's "empty" mbarrier so the producer can refill it.
+//   warps 0-3        : epilogue.  After the final commit, each warp reads its
+//                      32 TMEM lanes (rows) with tcgen05.ld 32x32b.x32, adds
+//                      bias / the previous C, and stores float32 rows.
+// Operand majorness: K-major tiles are TMA boxes {64 (K), rows}; MN-major
+// tiles are boxes {64 (M or N), 64 (K)}, one per 64-wide MN chunk.  The UMMA
+// shared-memory descriptors describe the canonical SWIZZLE_128B layouts of
+// both (K-major: 8-row groups 1024 B apart; MN-major: 8-K-row groups 1024 B
+// apart, 64-wide MN chunks one box apart).
+// Every mbarrier wait is bounded in time: a wait that exceeds the limit sets
+// the device status word (read with mr_gemm_status), and all roles skip their
+// remaining work, wait (bounded) for their own issued copies and MMAs, and
+// free TMEM before returning.  Loads are plain tiled TMA (no multicast).
+
+#include <cuda.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace mr {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 128;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+__device__ int g_gemm_status = 0;
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; returns false (and raises the status word) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        atomicExch(&g_gemm_status, MR_ERR_TIMEOUT);
+        return false;
+      }
+      if (*reinterpret_cast<volatile int*>(&g_gemm_status) != 0) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t addr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(addr), "r"(cols));
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 lanes x 32 columns of float32 from TMEM: thread i gets row (lane base + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- descriptors
+// UMMA shared-memory descriptor for a SWIZZLE_128B canonical layout.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;  // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, M=128, N=BN, given majorness.
+__host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn) {
+  return (1u << 4)                       // D format f32
+         | (1u << 7)                     // A bf16
+         | (1u << 10)                    // B bf16
+         | (uint32_t(a_mn) << 15)        // A major
+         | (uint32_t(b_mn) << 16)        // B major
+         | (uint32_t(n >> 3) << 17)      // N
+         | (uint32_t(BM >> 4) << 24);    // M
+}
+
+template <int BN, int PREC>
+struct Cfg {
+  static constexpr int kA = BM * BK * 2;                  // bytes of one A part per stage
+  static constexpr int kB = BN * BK * 2;                  // bytes of one B part per stage
+  static constexpr int kAParts = PREC >= 2 ? 2 : 1;
+  static constexpr int kBParts = PREC == 3 ? 2 : 1;
+  static constexpr int kStage = kA * kAParts + kB * kBParts;
+  static constexpr int kStages = (200 * 1024) / kStage > 4 ? 4 : (200 * 1024) / kStage;
+  static constexpr int kSmem = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+};
+
+struct Maps {
+  CUtensorMap a_hi, a_lo, b_hi, b_lo;
+};
+
+// Load one operand part (rows x 64 K) of a stage.  K-major: one box {64, rows}.
+// MN-major: rows/64 boxes {64, 64} at 8 KB spacing.
+template <int ROWS>
+__device__ __forceinline__ void load_part(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                          bool kmajor, int row0, int k0) {
+  if (kmajor) {
+    tma_load_2d(dst, map, bar, k0, row0);
+  } else {
+#pragma unroll
+    for (int c = 0; c < ROWS / 64; ++c) tma_load_2d(dst + c * 64 * BK * 2, map, bar, row0 + c * 64, k0);
+  }
+}
+
+__device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int rows, int kstep) {
+  // K-major: +32 B per 16-wide K step inside the 128 B swizzle row; SBO 1024.
+  // MN-major: +2048 B (two 8-row K groups) per K step; LBO = one 64-wide box.
+  return kmajor ? smem_desc(base + kstep * 32, 16, 1024)
+                : smem_desc(base + kstep * 2048, 64 * BK * 2, 1024);
+}
+
+template <int BN, int PREC>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
+                const float* __restrict__ bias, int accumulate, int m, int n, int k, int a_kmajor,
+                int b_kmajor) {
+  using C = Cfg<BN, PREC>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStage);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* done = empty + C::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // grouped rasterization: 16 M-tiles share each sweep over N
+  const int m_tiles = (m + BM - 1) / BM;
+  const int n_tiles = (n + BN - 1) / BN;
+  constexpr int G = 16;
+  const int tile = blockIdx.x;
+  const int group = tile / (G * n_tiles);
+  const int first_m = group * G;
+  const int gm = min(G, m_tiles - first_m);
+  const int tm = first_m + (tile % (G * n_tiles)) % gm;
+  const int tn = (tile % (G * n_tiles)) / gm;
+  const int m0 = tm * BM;
+  const int n0 = tn * BN;
+  const int k_tiles = (k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a_hi)));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b_hi)));
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ producer
+    for (int kt = 0; kt < k_tiles && ok; ++kt) {
+      const int s = kt % C::kStages;
+      const uint32_t round = kt / C::kStages;
+      if (kt >= C::kStages) ok = mbar_wait(&empty[s], (round - 1) & 1);
+      if (!ok) break;
+      uint8_t* st = smem + s * C::kStage;
+      mbar_expect_tx(&full[s], C::kStage);
+      const int k0 = kt * BK;
+      load_part<BM>(st, &maps.a_hi, &full[s], a_kmajor, m0, k0);
+      if (C::kAParts == 2) load_part<BM>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, m0, k0);
+      uint8_t* sb = st + C::kA * C::kAParts;
+      load_part<BN>(sb, &maps.b_hi, &full[s], b_kmajor, n0, k0);
+      if (C::kBParts == 2) load_part<BN>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, n0, k0);
+    }
+    if (!ok) {
+      // let issued copies land before the CTA exits (bounded)
+      for (int s = 0; s < C::kStages; ++s) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(&full[s], 0) && !mbar_try_wait(&full[s], 1) &&
+               globaltimer() - t0 < kWaitLimitNs / 4) {
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    const uint32_t idesc = instr_desc(BN, !a_kmajor, !b_kmajor);
+    for (int kt = 0; kt < k_tiles; ++kt) {
+      const int s = kt % C::kStages;
+      ok = mbar_wait(&full[s], (kt / C::kStages) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t st = smem_u32(smem + s * C::kStage);
+      const uint32_t a_hi = st;
+      const uint32_t a_lo = st + C::kA;
+      const uint32_t b_hi = st + C::kA * C::kAParts;
+      const uint32_t b_lo = b_hi + C::kB;
+#pragma unroll
+      for (int ks = 0; ks < BK / 16; ++ks) {
+        const uint32_t acc0 = (kt > 0 || ks > 0) ? 1u : 0u;
+        const uint64_t dah = part_desc(a_hi, a_kmajor, BM, ks);
+        const uint64_t dbh = part_desc(b_hi, b_kmajor, BN, ks);
+        umma_bf16(tmem, dah, dbh, idesc, acc0);
+        if (PREC == 3) umma_bf16(tmem, dah, part_desc(b_lo, b_kmajor, BN, ks), idesc, 1u);
+        if (PREC >= 2) umma_bf16(tmem, part_desc(a_lo, a_kmajor, BM, ks), dbh, idesc, 1u);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);  // fires when every MMA issued above has completed
+  }
+  __syncwarp();
+
+  // ------------------------------------------------ epilogue (all 4 warps)
+  ok = mbar_wait(done, 0);
+  tc_fence_after();
+  const bool run_epilogue =
+      __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(&g_gemm_status) == 0);
+  if (run_epilogue) {
+    const int row = m0 + warp * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+#pragma unroll 1
+    for (int col = 0; col < BN; col += 32) {
+      float v[32];
+      tmem_ld32(lane_base + col, v);
+      const int gc = n0 + col;
+      if (row < m && gc < n) {
+        float* dst = c + int64_t(row) * ldc + gc;
+        const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+        if (full_chunk) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (bias) {
+              o.x += bias[gc + j]; o.y += bias[gc + j + 1];
+              o.z += bias[gc + j + 2]; o.w += bias[gc + j + 3];
+            }
+            if (accumulate) {
+              const float4 p = *reinterpret_cast<const float4*>(dst + j);
+              o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+            }
+            *reinterpret_cast<float4*>(dst + j) = o;
+          }
+        } else {
+          for (int j = 0; j < 32 && gc + j < n; ++j) {
+            float o = v[j];
+            if (bias) o += bias[gc + j];
+            if (accumulate) o += dst[j];
+            dst[j] = o;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
+              uint32_t box_inner, uint32_t box_outer) {
+  const cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  CUresult r = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                      const_cast<void*>(base), dims, strides, box, elem_strides,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Map for an operand with `rows` logical rows (M or N) and K columns.
+bool operand_map(CUtensorMap* map, const void* p, bool kmajor, int64_t rows, int64_t k,
+                 int64_t ld, int tile_rows) {
+  if (kmajor) return make_map(map, p, k, rows, ld, BK, uint32_t(tile_rows));
+  return make_map(map, p, rows, k, ld, 64, BK);
+}
+
+template <int BN, int PREC>
+int launch(const Maps& maps, float* c, int64_t ldc, const float* bias, int accumulate, int m, int n,
+           int k, int a_kmajor, int b_kmajor, cudaStream_t stream) {
+  using C = Cfg<BN, PREC>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, PREC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return MR_ERR_LAUNCH;
+    }
+    configured = true;
+  }
+  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  gemm_kernel<BN, PREC><<<tiles, kThreads, C::kSmem, stream>>>(maps, c, ldc, bias, accumulate, m,
+                                                                 n, k, a_kmajor, b_kmajor);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace mr
+
+using namespace mr;
+
+extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
+                       const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
+                       float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
+                       int64_t n, int64_t k, int precision, void* stream) {
+  if (!a_hi || !b_hi || !c || m <= 0 || n <= 0 || k <= 0) return MR_ERR_ARGUMENT;
+  if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
+  if (precision < 1 || precision > 3) return MR_ERR_ARGUMENT;
+  if (precision >= 2 && !a_lo) return MR_ERR_ARGUMENT;
+  if (precision == 3 && !b_lo) return MR_ERR_ARGUMENT;
+  if (!aligned16(a_hi) || !aligned16(b_hi) || (a_lo && !aligned16(a_lo)) ||
+      (b_lo && !aligned16(b_lo)))
+    return MR_ERR_ALIGNMENT;
+  if ((lda % 8) || (ldb % 8)) return MR_ERR_ALIGNMENT;
+  if (a_kmajor ? lda < k : lda < m) return MR_ERR_ARGUMENT;
+  if (b_kmajor ? ldb < k : ldb < n) return MR_ERR_ARGUMENT;
+  if (ldc < n) return MR_ERR_ARGUMENT;
+  constexpr int BN = 256;
+  Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  bool good = operand_map(&maps.a_hi, a_hi, a_kmajor, m, k, lda, BM) &&
+              operand_map(&maps.b_hi, b_hi, b_kmajor, n, k, ldb, BN);
+  if (good && precision >= 2) good = operand_map(&maps.a_lo, a_lo, a_kmajor, m, k, lda, BM);
+  if (good && precision == 3) good = operand_map(&maps.b_lo, b_lo, b_kmajor, n, k, ldb, BN);
+  if (!good) return MR_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (precision) {
+    case 1: return launch<BN, 1>(maps, c, ldc, bias, accumulate, int(m), int(n), int(k), a_kmajor, b_kmajor, s);
+    case 2: return launch<BN, 2>(maps, c, ldc, bias, accumulate, int(m), int(n), int(k), a_kmajor, b_kmajor, s);
+    default: return launch<BN, 3>(maps, c, ldc, bias, accumulate, int(m), int(n), int(k), a_kmajor, b_kmajor, s);
+  }
+}
+
+// Device status word of the GEMM (0 ok, MR_ERR_TIMEOUT after a wait gave up).
+// Synchronizes the device; `reset` clears the word.
+extern "C" int mr_gemm_status(int reset) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(int));
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return MR_ERR_LAUNCH;
+  }
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int));
+  }
+  return v;
+}

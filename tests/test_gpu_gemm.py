@@ -1,0 +1,107 @@
+"""K3 (tcgen05 GEMM) against a float64 product of the same bf16 operand parts.
+
+The tensor cores multiply bf16 values exactly and accumulate in float32, so
+the kernel must agree with the float64 reference of the products it was asked
+for to float32 accumulation error (bound here: 2e-5 relative to the largest
+output, plus an absolute term for cancellation).  Tested: every operand
+majorness, each precision mode, ragged m/n/k edges (TMA zero fill), bias and
+accumulation, and a long-K case.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from mround_b200 import kernels
+
+    return kernels
+
+
+def split(x):
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    return hi, lo
+
+
+def run_case(K, m, n, k, a_kmajor, b_kmajor, precision, bias=False, accumulate=False, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(n, k, device="cuda", generator=g) * 0.02
+    a_hi, a_lo = split(a)
+    b_hi, b_lo = split(b)
+    # storage layouts
+    A_hi = a_hi if a_kmajor else a_hi.t().contiguous()
+    A_lo = a_lo if a_kmajor else a_lo.t().contiguous()
+    B_hi = b_hi if b_kmajor else b_hi.t().contiguous()
+    B_lo = b_lo if b_kmajor else b_lo.t().contiguous()
+    lda = k if a_kmajor else m
+    ldb = k if b_kmajor else n
+    c = torch.randn(m, n, device="cuda", generator=g) if accumulate else torch.zeros(m, n, device="cuda")
+    c0 = c.clone()
+    bvec = torch.randn(n, device="cuda", generator=g) if bias else None
+    K.gemm(A_hi, A_lo if precision >= 2 else None, B_hi, B_lo if precision == 3 else None, c,
+           m=m, n=n, k=k, a_kmajor=a_kmajor, b_kmajor=b_kmajor, lda=lda, ldb=ldb, ldc=n,
+           precision=precision, bias=bvec, accumulate=accumulate)
+    torch.cuda.synchronize()
+    ah, al = a_hi.double(), a_lo.double()
+    bh, bl = b_hi.double(), b_lo.double()
+    ref = ah @ bh.t()
+    if precision == 3:
+        ref = ref + ah @ bl.t() + al @ bh.t()
+    elif precision == 2:
+        ref = ref + al @ bh.t()
+    if bias:
+        ref = ref + bvec.double()
+    if accumulate:
+        ref = ref + c0.double()
+    err = (c.double() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    bound = 2e-5 * scale + 1e-6 * (k ** 0.5)
+    assert err <= bound, f"max err {err:.3e} > {bound:.3e} (scale {scale:.3e})"
+    from mround_b200._native import lib
+
+    assert lib().mr_gemm_status(1) == 0
+
+
+@pytest.mark.parametrize("a_kmajor", [True, False])
+@pytest.mark.parametrize("b_kmajor", [True, False])
+@pytest.mark.parametrize("precision", [1, 2, 3])
+def test_layouts_and_precisions(K, a_kmajor, b_kmajor, precision):
+    run_case(K, 256, 512, 320, a_kmajor, b_kmajor, precision)
+
+
+@pytest.mark.parametrize("m,n,k", [(200, 300, 100), (128, 960, 576), (37, 8, 16), (384, 256, 1000)])
+def test_ragged_edges(K, m, n, k):
+    # the K-major/M-major leading dimensions must stay multiples of 8
+    run_case(K, m, n, k, True, True, 3)
+    if m % 8 == 0 and n % 8 == 0:
+        run_case(K, m, n, k, False, False, 3)
+
+
+def test_bias_and_accumulate(K):
+    run_case(K, 256, 384, 192, True, True, 3, bias=True)
+    run_case(K, 256, 384, 192, False, False, 1, accumulate=True)
+    run_case(K, 128, 256, 64, True, False, 2, bias=True, accumulate=True)
+
+
+def test_long_k(K):
+    run_case(K, 256, 256, 8192, False, False, 3)
+
+
+def test_misaligned_leading_dimension_refused(K):
+    from mround_b200.exceptions import SchemeError
+
+    a = torch.zeros(128, 100, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(128, 100, dtype=torch.bfloat16, device="cuda")
+    c = torch.zeros(128, 128, device="cuda")
+    with pytest.raises(SchemeError):
+        K.gemm(a, None, b, None, c, m=128, n=128, k=100, a_kmajor=True, b_kmajor=True, lda=100,
+               ldb=100, ldc=128, precision=1)

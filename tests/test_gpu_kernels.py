@@ -108,10 +108,10 @@ def test_edge_groups_on_device(K):
     # single-sign, all-zero and boundary groups, widened to the device's group of 8
     rows = [[-2.0, -1.5, -1.0, -0.5], [1.0, 1.5, 2.0, 0.25], [-1.0, 0.0, 1.0, 0.5],
             [0.0, 0.0, 0.0, 0.0], [1.0, 0.9, 0.5, -0.3]]
-    w = np.array([r + r for r in rows], np.float32) * 0.01
+    w = np.array([r * 4 for r in rows], np.float32) * 0.01  # 16 columns, groups of 8
     w = o_pack.bf16_to_f32(o_pack.bf16_bits(w))
     for bits in (2, 4, 8):
-        ones = np.ones((w.shape[0], 1), np.float32)
+        ones = np.ones((w.shape[0], 2), np.float32)
         qdq, codes, scale, zp = o_q.fake_quantize(w, np.zeros_like(w), ones, ones, bits, 8)
         dw, dv, da, db = to_dev(w, np.zeros_like(w), ones, ones)
         f32, z = torch.empty_like(dv), torch.empty_like(da)
