@@ -88,8 +88,7 @@ def build(verbose: bool = False) -> Path:
         objs = list(pool.map(lambda s: _compile(s, extra), sources))
     if LIB.exists() and LIB.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
         return LIB
-    cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(LIB),
-           "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(LIB)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
