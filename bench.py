@@ -1,0 +1,410 @@
+"""Benchmark: SignRound v2 block tuning of a Qwen2.5-7B-architecture block on B200.
+
+Metric: Qwen2.5-7B-arch W2 g64 tuning, blocks/s (and wall-s per
+model) at 1/2/4/8 B200.  A *step* is one pass of the hot path over one
+calibration batch: block forward on the fake-quantized weights, the outlier-
+suppressed loss, backward, and the signed update of V/alpha/beta -- one
+iteration of ``_tune`` (reference mround/pipeline/runner.py:914-937).  A block
+is 200 such steps plus 4 forward passes over each of the 16 batches (score
+before, score after, targets, advance), so
+
+    blocks/s = 1 / (200 * t_step + 64 * t_forward_batch)
+
+with both times measured here with CUDA events on the launching stream
+(t_forward in a second timed region right after the K steps).
+
+Workload: one block of the Qwen2.5-7B architecture (hidden 3584, 28/4 heads,
+SwiGLU 18944, QKV bias), random-init N(0, 0.02) bf16 weights, W2 asym g64;
+16 calibration batches of 8 x 2048 Zipf(1.1) tokens, block-0 inputs (token
+embeddings, float32) -- synthetic stand-ins for pile-10k and the checkpoint.
+Every batch input (8 x 2048 x 3584 float32 = 235 MB) is larger than L2, so
+no flush is needed between steps.  Under torchrun each of N ranks holds 8/N
+sequences of every batch (strong scaling: the global batch is fixed).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ITERS = 200
+N_BATCHES = 16
+BATCH = 8
+SEQ = 2048
+PASSES_PER_BATCH = 4
+METRIC = "Qwen2.5-7B-arch W2g64 tuning: blocks/s (wall-s/model in 'wall_s_model')"
+UNIT = "blocks/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--arch", default="qwen2.5-7b")
+    ap.add_argument("--bits", type=int, default=2)
+    ap.add_argument("--group", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- workload
+def build_workload(args, dist, device):
+    from mround_b200.pipeline.arch import get_arch
+    from mround_b200.pipeline.block import DeviceBlock, Precision
+    from mround_b200.pipeline.model import SyntheticModel, zipf_tokens
+
+    arch = get_arch(args.arch)
+    model = SyntheticModel(arch, seed=0)
+    tokens = zipf_tokens(arch.vocab, N_BATCHES * BATCH, SEQ, seed=42)
+    batches = [tokens[i * BATCH:(i + 1) * BATCH] for i in range(N_BATCHES)]
+    embed = model.embed_tokens()
+    rows = dist.shard(BATCH)
+    inputs = []
+    for b in batches:
+        ids = torch.as_tensor(b[rows], dtype=torch.long)
+        inputs.append(embed[ids].float().to(device).contiguous())
+    block = DeviceBlock(arch, model.block(0), device)
+    prec = Precision()
+    with torch.no_grad():
+        targets = [block.forward(x, prec) for x in inputs]
+    return arch, model, block, inputs, targets
+
+
+def make_tuner(args, block, dist):
+    from mround_b200.pipeline.runner import QuantizationRunner
+    from mround_b200.schemes import QuantScheme, TuningConfig
+
+    scheme = QuantScheme(bits=args.bits, group_size=args.group, symmetry="asym")
+    runner = QuantizationRunner(scheme, TuningConfig(iters=ITERS), dist=dist)
+    return runner.tuner_for(block, "model.layers.0")
+
+
+def timed(fn, n, dist, device):
+    """Run fn(i) n times between barriers; device time (CUDA events), max over ranks."""
+    dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(n):
+        fn(i)
+    end.record()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    ms = start.elapsed_time(end)
+    return dist.max_scalar(ms, device)
+
+
+def block_seconds(t_step_ms, t_fwd_ms):
+    return (ITERS * t_step_ms + PASSES_PER_BATCH * N_BATCHES * t_fwd_ms) / 1e3
+
+
+# ----------------------------------------------------------------- e2e
+class HostStreams:
+    """Calibration shards in pinned host memory, copied to the device per step
+    on a side stream (double-buffered) -- the path for streams that do not stay
+    resident in HBM."""
+
+    def __init__(self, inputs, targets, device):
+        self.host = [(x.cpu().pin_memory(), t.cpu().pin_memory()) for x, t in zip(inputs, targets)]
+        self.device = device
+        self.copy = torch.cuda.Stream(device)
+        self.slots = [(torch.empty_like(inputs[0]), torch.empty_like(targets[0])) for _ in range(2)]
+        self.ready = [torch.cuda.Event(), torch.cuda.Event()]
+        self.free = [torch.cuda.Event(), torch.cuda.Event()]
+        self.h2d_bytes = inputs[0].numel() * 4 * 2
+
+    def prefetch(self, i, b):
+        slot = i % 2
+        with torch.cuda.stream(self.copy):
+            self.copy.wait_event(self.free[slot])
+            x, t = self.slots[slot]
+            hx, ht = self.host[b]
+            x.copy_(hx, non_blocking=True)
+            t.copy_(ht, non_blocking=True)
+            self.ready[slot].record(self.copy)
+
+    def get(self, i):
+        slot = i % 2
+        torch.cuda.current_stream().wait_event(self.ready[slot])
+        return self.slots[slot]
+
+    def release(self, i):
+        self.free[i % 2].record(torch.cuda.current_stream())
+
+
+# ----------------------------------------------------------------- cpu
+def cpu_sample(args, model, arch, budget_s: float = 25.0):
+    """The oracle's CPU step on a bounded sample, extrapolated to blocks/s."""
+    from oracle.block_tuner import LINEARS, OracleBlock, fake_quant_ste, loss_fn
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ob = OracleBlock(arch, model.block(0), {p: args.bits for p in LINEARS}, args.group)
+    params = ob.init_params()
+    t0 = time.perf_counter()
+    leaves = {q: tuple(t.clone().requires_grad_(True) for t in params[q]) for q in params}
+    s = 0
+    for q in LINEARS:
+        w = fake_quant_ste(ob.w[q], *leaves[q], args.bits, args.group)
+        s = s + (w * w).sum()
+    s.backward()
+    t_fq = time.perf_counter() - t0
+    tok = 512
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, tok, arch.hidden, generator=g) * 0.02
+    with torch.no_grad():
+        tgt = ob.forward(x) + 1e-3
+    times = []
+    while not times or (sum(times) < budget_s - t_fq and len(times) < 3):
+        leaves = {q: tuple(t.clone().requires_grad_(True) for t in params[q]) for q in params}
+        t1 = time.perf_counter()
+        loss, _ = loss_fn(ob.forward(x, leaves), tgt, True)
+        loss.backward()
+        times.append(time.perf_counter() - t1)
+    t_sample = min(times)
+    scale = BATCH * SEQ / tok
+    t_step = t_fq + (t_sample - t_fq) * scale
+    with torch.no_grad():
+        t1 = time.perf_counter()
+        ob.forward(x, None)
+        t_fwd_sample = time.perf_counter() - t1
+    t_fwd = t_fwd_sample * scale
+    blk = ITERS * t_step + PASSES_PER_BATCH * N_BATCHES * t_fwd
+    return {
+        "value": 1.0 / blk, "unit": UNIT, "cores": threads, "kind": "port",
+        "sample": (f"torch-CPU float32 restatement (oracle/block_tuner.py), not the reference's MLX "
+                   f"code: one step of one {args.arch} block on 1 sequence x {tok} tokens "
+                   f"(best of {len(times)}: {t_sample:.2f} s) plus the token-independent fake-quant "
+                   f"fwd+bwd ({t_fq:.2f} s), scaled x{scale:.0f} to the 8x2048 batch, x{ITERS} steps "
+                   f"+ {PASSES_PER_BATCH * N_BATCHES} forward passes; attention scaled linearly"),
+        "t_step_s": t_step,
+    }
+
+
+# ----------------------------------------------------------------- main
+def main():
+    args = parse()
+    from mround_b200.pipeline.dist import init_from_env
+
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    dist = init_from_env()
+    device = torch.device("cuda", torch.cuda.current_device())
+    from mround_b200 import kernels
+    from mround_b200._native import lib
+
+    if lib().mr_device_check() != 0:
+        raise SystemExit("libmround_b200 needs an sm_100 device")
+    arch, model, block, inputs, targets = build_workload(args, dist, device)
+    tuner = make_tuner(args, block, dist)
+
+    def step(i):
+        b = i % N_BATCHES
+        tuner.step(inputs[b], targets[b], i, ITERS)
+
+    for i in range(args.warmup):
+        step(i)
+    launches0 = kernels.LAUNCHES[0]
+    with ClockSampler(device.index) as clocks:
+        ms_steps = timed(lambda i: step(args.warmup + i), args.steps, dist, device)
+    launches = kernels.LAUNCHES[0] - launches0
+    t_step = ms_steps / args.steps
+    n_fwd = min(N_BATCHES, max(4, args.steps))
+    ms_fwd = timed(lambda i: tuner.batch_loss(inputs[i % N_BATCHES], targets[i % N_BATCHES]),
+                   n_fwd, dist, device)
+    t_fwd = ms_fwd / n_fwd
+    blk_s = block_seconds(t_step, t_fwd)
+    value = 1.0 / blk_s
+
+    # GEMM roofline: per-launch events over one instrumented step
+    kernels.GEMM_EVENTS = []
+    step(args.warmup + args.steps)
+    torch.cuda.synchronize(device)
+    ev, kernels.GEMM_EVENTS = kernels.GEMM_EVENTS, None
+    gemm_ms = sum(s.elapsed_time(e) for s, e, _, _ in ev)
+    alg_flops = sum(f for _, _, f, _ in ev)
+    exe_flops = sum(f * p for _, _, f, p in ev)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "of measured (bf16_tflops_sustained)"
+    if peak is None:
+        peak, peak_src = 1400.0, "of fallback (sustained 1.4 PFLOP/s)"
+    achieved = alg_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
+
+    # end to end: streams in pinned host memory, per-step H2D + loss D2H
+    e2e = None
+    if not args.no_e2e:
+        hs = HostStreams(inputs[:4], targets[:4], device)
+        host_loss = torch.empty((), dtype=torch.float64).pin_memory()
+
+        def e2e_step(i):
+            x, t = hs.get(i)
+            loss = tuner.step(x, t, i, ITERS)
+            hs.release(i)
+            hs.prefetch(i + 2, (i + 2) % 4)
+            host_loss.copy_(loss, non_blocking=True)
+
+        hs.prefetch(0, 0)
+        hs.prefetch(1, 1)
+        for i in range(2):
+            e2e_step(i)
+        ms_e2e = timed(lambda i: e2e_step(2 + i), args.steps, dist, device)
+
+        def e2e_fwd(i):
+            x, t = hs.get(i)
+            loss = tuner.batch_loss(x, t)
+            hs.release(i)
+            hs.prefetch(i + 2, (i + 2) % 4)
+            host_loss.copy_(loss, non_blocking=True)
+
+        base = 2 + args.steps
+        ms_e2e_fwd = timed(lambda i: e2e_fwd(base + i), n_fwd, dist, device)
+        blk_e2e = block_seconds(ms_e2e / args.steps, ms_e2e_fwd / n_fwd)
+        e2e = {"value": 1.0 / blk_e2e, "unit": UNIT, "h2d_bytes_per_step": hs.h2d_bytes,
+               "d2h_bytes_per_step": 8,
+               "path": "BlockTuner.step on pinned-host calibration shards, double-buffered H2D"}
+        torch.cuda.synchronize(device)
+
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 via bf16x3 split tcgen05 GEMMs (float32 accumulate)",
+        "data": "synthetic (random-init N(0,0.02) weights, Zipf(1.1) tokens)",
+        "config": {"workload": f"{args.arch} block SignRound step, W{args.bits} asym g{args.group}, "
+                               f"global batch {BATCH}x{SEQ}, {ITERS} it/block, {N_BATCHES} batches",
+                   "global_batch": BATCH, "seq_len": SEQ, "parallelism": f"dp{dist.world}",
+                   "l2": "inputs larger than L2 (235 MB per batch input)"},
+        "ms_forward_batch": t_fwd, "block_seconds": blk_s, "wall_s_model": blk_s * arch.layers,
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "mround_b200 gemm_kernel (K3)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_src,
+                     "executed_tflops": exe_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0,
+                     "executed_frac": (exe_flops / (gemm_ms / 1e3) / 1e12) / peak if gemm_ms else 0.0,
+                     "gemm_share_of_step": gemm_ms / t_step if t_step else None,
+                     "traffic": None},
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_sample(args, model, arch)
+        except Exception as exc:  # noqa: BLE001 - the baseline is reported, not required
+            out["cpu_baseline"] = {"value": None, "error": str(exc)}
+    if dist.rank == 0:
+        print(json.dumps(out), flush=True)
+    if dist.world > 1:
+        import torch.distributed as tdist
+
+        tdist.destroy_process_group()
+
+
+def reference_arm(args):
+    """The reference path's CPU implementation (the oracle restatement; the
+    reference's MLX loop cannot run here), timed on this host's cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from mround_b200.pipeline.arch import get_arch
+    from mround_b200.pipeline.model import SyntheticModel
+
+    arch = get_arch(args.arch)
+    model = SyntheticModel(arch, seed=0)
+    res = cpu_sample(args, model, arch, budget_s=20.0)
+    cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res["t_step_s"] * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": f"{args.arch} block SignRound step, W{args.bits} asym g{args.group}, "
+                               f"global batch {BATCH}x{SEQ}, {ITERS} it/block, {N_BATCHES} batches",
+                   "global_batch": BATCH, "seq_len": SEQ, "parallelism": "cpu"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

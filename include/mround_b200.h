@@ -189,6 +189,20 @@ int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajo
             float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
             int64_t n, int64_t k, int precision, void* stream);
 
+/*
+ * K3, batched: `batch` independent GEMMs of the same shape, operand i at
+ * a + i*stride_a, b + i*stride_b, c + i*stride_c (elements; strides multiples
+ * of 8 for bf16 operands).  One launch (grid.y = batch).  Serves the
+ * attention products of the decoder block (scores, probabilities times
+ * values, and their gradients), which the reference runs inside the mlx-lm
+ * layer (mround/pipeline/blocks.py:578-606).
+ */
+int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int64_t stride_a,
+                    int a_kmajor, const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb,
+                    int64_t stride_b, int b_kmajor, float* c, int64_t ldc, int64_t stride_c,
+                    const float* bias, int accumulate, int64_t m, int64_t n, int64_t k,
+                    int64_t batch, int precision, void* stream);
+
 /* Device status word of K3: 0, or MR_ERR_TIMEOUT.  Synchronizes the device;
  * reset != 0 clears it. */
 int mr_gemm_status(int reset);

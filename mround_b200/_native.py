@@ -54,6 +54,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_split_bf16": (_I, [_P, _I64, _P, _P, _P]),
     "mr_gemm": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _P, _I64, _P, _I, _I64, _I64, _I64,
                      _I, _P]),
+    "mr_gemm_batched": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _I64, _I64, _I, _P, _I64, _I64, _P,
+                             _I, _I64, _I64, _I64, _I64, _I, _P]),
     "mr_gemm_status": (_I, [_I]),
 }
 

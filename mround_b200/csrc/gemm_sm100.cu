@@ -94,12 +94,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                            int32_t x, int32_t y) {
+// Tiled 3-D TMA load (x innermost, z = batch); no multicast.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -197,12 +198,13 @@ struct Maps {
 // MN-major: rows/64 boxes {64, 64} at 8 KB spacing.
 template <int ROWS>
 __device__ __forceinline__ void load_part(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
-                                          bool kmajor, int row0, int k0) {
+                                          bool kmajor, int row0, int k0, int z) {
   if (kmajor) {
-    tma_load_2d(dst, map, bar, k0, row0);
+    tma_load_3d(dst, map, bar, k0, row0, z);
   } else {
 #pragma unroll
-    for (int c = 0; c < ROWS / 64; ++c) tma_load_2d(dst + c * 64 * BK * 2, map, bar, row0 + c * 64, k0);
+    for (int c = 0; c < ROWS / 64; ++c)
+      tma_load_3d(dst + c * 64 * BK * 2, map, bar, row0 + c * 64, k0, z);
   }
 }
 
@@ -216,8 +218,8 @@ __device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int ro
 template <int BN, int PREC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
-                const float* __restrict__ bias, int accumulate, int m, int n, int k, int a_kmajor,
-                int b_kmajor) {
+                int64_t stride_c, const float* __restrict__ bias, int accumulate, int m, int n,
+                int k, int a_kmajor, int b_kmajor) {
   using C = Cfg<BN, PREC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -242,6 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m0 = tm * BM;
   const int n0 = tn * BN;
   const int k_tiles = (k + BK - 1) / BK;
+  const int z = blockIdx.y;  // batch index
+  c += int64_t(z) * stride_c;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -270,11 +274,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* st = smem + s * C::kStage;
       mbar_expect_tx(&full[s], C::kStage);
       const int k0 = kt * BK;
-      load_part<BM>(st, &maps.a_hi, &full[s], a_kmajor, m0, k0);
-      if (C::kAParts == 2) load_part<BM>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, m0, k0);
+      load_part<BM>(st, &maps.a_hi, &full[s], a_kmajor, m0, k0, z);
+      if (C::kAParts == 2) load_part<BM>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, m0, k0, z);
       uint8_t* sb = st + C::kA * C::kAParts;
-      load_part<BN>(sb, &maps.b_hi, &full[s], b_kmajor, n0, k0);
-      if (C::kBParts == 2) load_part<BN>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, n0, k0);
+      load_part<BN>(sb, &maps.b_hi, &full[s], b_kmajor, n0, k0, z);
+      if (C::kBParts == 2) load_part<BN>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, n0, k0, z);
     }
     if (!ok) {
       // let issued copies land before the CTA exits (bounded)
@@ -384,14 +388,15 @@ EncodeTiledFn encode_fn() {
 }
 
 bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
-              uint32_t box_inner, uint32_t box_outer) {
+              int64_t batch, int64_t batch_stride, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn encode = encode_fn();
   if (!encode) return false;
-  const cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
-  const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t elem_strides[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+  const cuuint64_t dims[3] = {cuuint64_t(inner), cuuint64_t(outer), cuuint64_t(batch)};
+  const cuuint64_t strides[2] = {cuuint64_t(ld) * 2,
+                                 cuuint64_t(batch > 1 ? batch_stride : ld * outer) * 2};
+  const cuuint32_t box[3] = {box_inner, box_outer, 1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
                       strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -400,14 +405,15 @@ bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
 
 // Map for an operand with `rows` logical rows (M or N) and K columns.
 bool operand_map(CUtensorMap* map, const void* p, bool kmajor, int64_t rows, int64_t k,
-                 int64_t ld, int tile_rows) {
-  if (kmajor) return make_map(map, p, k, rows, ld, BK, uint32_t(tile_rows));
-  return make_map(map, p, rows, k, ld, 64, BK);
+                 int64_t ld, int64_t batch, int64_t batch_stride, int tile_rows) {
+  if (kmajor) return make_map(map, p, k, rows, ld, batch, batch_stride, BK, uint32_t(tile_rows));
+  return make_map(map, p, rows, k, ld, batch, batch_stride, 64, BK);
 }
 
 template <int BN, int PREC>
-int launch(const Maps& maps, float* c, int64_t ldc, const float* bias, int accumulate, int m, int n,
-           int k, int a_kmajor, int b_kmajor, cudaStream_t stream) {
+int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const float* bias,
+           int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
+           cudaStream_t stream) {
   using C = Cfg<BN, PREC>;
   static bool configured = false;
   if (!configured) {
@@ -420,8 +426,8 @@ int launch(const Maps& maps, float* c, int64_t ldc, const float* bias, int accum
     configured = true;
   }
   const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-  gemm_kernel<BN, PREC><<<tiles, kThreads, C::kSmem, stream>>>(maps, c, ldc, bias, accumulate, m,
-                                                                 n, k, a_kmajor, b_kmajor);
+  gemm_kernel<BN, PREC><<<dim3(tiles, batch), kThreads, C::kSmem, stream>>>(
+      maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor);
   return launch_status();
 }
 
@@ -430,12 +436,15 @@ int launch(const Maps& maps, float* c, int64_t ldc, const float* bias, int accum
 
 using namespace mr;
 
-extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
-                       const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
-                       float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
-                       int64_t n, int64_t k, int precision, void* stream) {
-  if (!a_hi || !b_hi || !c || m <= 0 || n <= 0 || k <= 0) return MR_ERR_ARGUMENT;
-  if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
+extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda,
+                               int64_t stride_a, int a_kmajor, const uint16_t* b_hi,
+                               const uint16_t* b_lo, int64_t ldb, int64_t stride_b, int b_kmajor,
+                               float* c, int64_t ldc, int64_t stride_c, const float* bias,
+                               int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
+                               int precision, void* stream) {
+  if (!a_hi || !b_hi || !c || m <= 0 || n <= 0 || k <= 0 || batch <= 0) return MR_ERR_ARGUMENT;
+  if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1 || batch > 65535)
+    return MR_ERR_ARGUMENT;
   if (precision < 1 || precision > 3) return MR_ERR_ARGUMENT;
   if (precision >= 2 && !a_lo) return MR_ERR_ARGUMENT;
   if (precision == 3 && !b_lo) return MR_ERR_ARGUMENT;
@@ -443,23 +452,44 @@ extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, 
       (b_lo && !aligned16(b_lo)))
     return MR_ERR_ALIGNMENT;
   if ((lda % 8) || (ldb % 8)) return MR_ERR_ALIGNMENT;
+  if (batch > 1 && ((stride_a % 8) || (stride_b % 8))) return MR_ERR_ALIGNMENT;
   if (a_kmajor ? lda < k : lda < m) return MR_ERR_ARGUMENT;
   if (b_kmajor ? ldb < k : ldb < n) return MR_ERR_ARGUMENT;
   if (ldc < n) return MR_ERR_ARGUMENT;
-  constexpr int BN = 256;
+  // narrow outputs (attention's head dimension) use 128-wide tiles
+  const int BNsel = n <= 128 ? 128 : 256;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
-  bool good = operand_map(&maps.a_hi, a_hi, a_kmajor, m, k, lda, BM) &&
-              operand_map(&maps.b_hi, b_hi, b_kmajor, n, k, ldb, BN);
-  if (good && precision >= 2) good = operand_map(&maps.a_lo, a_lo, a_kmajor, m, k, lda, BM);
-  if (good && precision == 3) good = operand_map(&maps.b_lo, b_lo, b_kmajor, n, k, ldb, BN);
+  bool good = operand_map(&maps.a_hi, a_hi, a_kmajor, m, k, lda, batch, stride_a, BM) &&
+              operand_map(&maps.b_hi, b_hi, b_kmajor, n, k, ldb, batch, stride_b, BNsel);
+  if (good && precision >= 2)
+    good = operand_map(&maps.a_lo, a_lo, a_kmajor, m, k, lda, batch, stride_a, BM);
+  if (good && precision == 3)
+    good = operand_map(&maps.b_lo, b_lo, b_kmajor, n, k, ldb, batch, stride_b, BNsel);
   if (!good) return MR_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (precision) {
-    case 1: return launch<BN, 1>(maps, c, ldc, bias, accumulate, int(m), int(n), int(k), a_kmajor, b_kmajor, s);
-    case 2: return launch<BN, 2>(maps, c, ldc, bias, accumulate, int(m), int(n), int(k), a_kmajor, b_kmajor, s);
-    default: return launch<BN, 3>(maps, c, ldc, bias, accumulate, int(m), int(n), int(k), a_kmajor, b_kmajor, s);
+  const int bt = int(batch);
+  const int M = int(m), N = int(n), Kk = int(k);
+  if (BNsel == 128) {
+    switch (precision) {
+      case 1: return launch<128, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+      case 2: return launch<128, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+      default: return launch<128, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+    }
   }
+  switch (precision) {
+    case 1: return launch<256, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+    case 2: return launch<256, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+    default: return launch<256, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+  }
+}
+
+extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
+                       const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
+                       float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
+                       int64_t n, int64_t k, int precision, void* stream) {
+  return mr_gemm_batched(a_hi, a_lo, lda, 0, a_kmajor, b_hi, b_lo, ldb, 0, b_kmajor, c, ldc, 0,
+                         bias, accumulate, m, n, k, 1, precision, stream);
 }
 
 // Device status word of the GEMM (0 ok, MR_ERR_TIMEOUT after a wait gave up).

@@ -18,6 +18,7 @@ __all__ = [
     "deltaloss",
     "fq_forward",
     "gemm",
+    "gemm_batched",
     "loss_apply",
     "loss_hist_pass",
     "loss_outlier",
@@ -28,6 +29,16 @@ __all__ = [
 ]
 
 DEVICE_GROUPS = (8, 16, 32, 64, 128, 256)
+
+# Kernel launches issued through this module (bench.py reports them), and an
+# optional timing hook for GEMM launches: when ``GEMM_EVENTS`` is a list, each
+# K3 launch appends ``(start_event, end_event, algorithmic_flops)``.
+LAUNCHES = [0]
+GEMM_EVENTS: list | None = None
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
 
 
 def _stream() -> int:
@@ -76,6 +87,7 @@ def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=No
         _ptr(wq_f32, torch.float32, "wq_f32", n), _ptr(scale, torch.float32, "scale", ng),
         _ptr(zp, torch.float32, "zp", ng), _stream())
     check(status, "mr_fq_forward")
+    _count()
 
 
 def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr: float,
@@ -91,6 +103,7 @@ def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr:
         _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
         _stream())
     check(status, "mr_ste_signsgd")
+    _count()
 
 
 def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes: bool = False):
@@ -113,6 +126,7 @@ def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes
         pw, pv, pa, pb, rows, cols, group, bits, eps, packed.data_ptr(), scales.data_ptr(),
         biases.data_ptr(), None if codes is None else codes.data_ptr(), _stream())
     check(status, "mr_pack_mlx")
+    _count()
     return packed, scales, biases, codes
 
 
@@ -142,6 +156,7 @@ def loss_outlier(pred, target, ws: LossWorkspace, *, suppress: bool, denom: floa
         -1.0 if threshold is None else float(threshold), _ptr(grad, torch.float32, "grad", n),
         ws.loss.data_ptr(), ws.thr.data_ptr(), ws.ptr, _stream())
     check(status, "mr_loss_outlier")
+    _count(8 if (suppress and threshold is None) else 2)
 
 
 def loss_hist_pass(pred, target, ws: LossWorkspace, pass_index: int) -> torch.Tensor:
@@ -151,6 +166,7 @@ def loss_hist_pass(pred, target, ws: LossWorkspace, pass_index: int) -> torch.Te
         _ptr(pred, torch.float32, "pred"), _ptr(target, torch.float32, "target", n), n,
         int(pass_index), ws.ptr, ws.hist.data_ptr(), _stream())
     check(status, "mr_loss_hist_pass")
+    _count()
     return ws.hist
 
 
@@ -159,6 +175,7 @@ def loss_select_digit(ws: LossWorkspace, k: int, pass_index: int) -> None:
     status = lib().mr_loss_select_digit(ws.hist.data_ptr(), int(k), int(pass_index), ws.ptr,
                                         ws.thr.data_ptr(), _stream())
     check(status, "mr_loss_select_digit")
+    _count()
 
 
 def loss_apply(pred, target, ws: LossWorkspace, *, suppress: bool, denom: float, grad=None) -> None:
@@ -169,6 +186,7 @@ def loss_apply(pred, target, ws: LossWorkspace, *, suppress: bool, denom: float,
         float(denom), ws.thr.data_ptr(), int(bool(suppress)), _ptr(grad, torch.float32, "grad", n),
         ws.loss.data_ptr(), ws.ptr, _stream())
     check(status, "mr_loss_apply")
+    _count(2)
 
 
 def deltaloss(g, w, *, bits: list[int] | tuple[int, ...], group: int, eps: float, out) -> None:
@@ -184,6 +202,7 @@ def deltaloss(g, w, *, bits: list[int] | tuple[int, ...], group: int, eps: float
         rows, cols, group, ctypes.cast(widths, ctypes.c_void_p), len(bits), eps,
         _ptr(out, torch.float64, "out", len(bits)), _stream())
     check(status, "mr_deltaloss")
+    _count()
 
 
 def split_bf16(x, hi=None, lo=None, *, want_lo: bool = True):
@@ -197,15 +216,44 @@ def split_bf16(x, hi=None, lo=None, *, want_lo: bool = True):
                                  _ptr(lo, torch.bfloat16, "lo", n) if lo is not None else None,
                                  _stream())
     check(status, "mr_split_bf16")
+    _count()
     return hi, lo
 
 
 def gemm(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool,
          lda: int, ldb: int, ldc: int, precision: int, bias=None, accumulate: bool = False) -> None:
     """K3: ``C[m, n] (+)= sum_k A[m, k] B[n, k]`` on the tcgen05 tensor cores."""
+    timing = GEMM_EVENTS is not None
+    if timing:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
     status = lib().mr_gemm(
         _ptr(a_hi, torch.bfloat16, "a_hi"), _ptr(a_lo, torch.bfloat16, "a_lo"), lda, int(a_kmajor),
         _ptr(b_hi, torch.bfloat16, "b_hi"), _ptr(b_lo, torch.bfloat16, "b_lo"), ldb, int(b_kmajor),
         _ptr(c, torch.float32, "c"), ldc, _ptr(bias, torch.float32, "bias"), int(bool(accumulate)),
         m, n, k, precision, _stream())
     check(status, "mr_gemm")
+    _count()
+    if timing:
+        end.record()
+        GEMM_EVENTS.append((start, end, 2.0 * m * n * k, precision))
+
+
+def gemm_batched(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, batch: int, a_kmajor: bool,
+                 b_kmajor: bool, lda: int, ldb: int, ldc: int, stride_a: int, stride_b: int,
+                 stride_c: int, precision: int, accumulate: bool = False) -> None:
+    """K3 over ``batch`` equally shaped problems in one launch."""
+    timing = GEMM_EVENTS is not None
+    if timing:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+    status = lib().mr_gemm_batched(
+        _ptr(a_hi, torch.bfloat16, "a_hi"), _ptr(a_lo, torch.bfloat16, "a_lo"), lda, stride_a,
+        int(a_kmajor), _ptr(b_hi, torch.bfloat16, "b_hi"), _ptr(b_lo, torch.bfloat16, "b_lo"), ldb,
+        stride_b, int(b_kmajor), _ptr(c, torch.float32, "c"), ldc, stride_c, None,
+        int(bool(accumulate)), m, n, k, batch, precision, _stream())
+    check(status, "mr_gemm_batched")
+    _count()
+    if timing:
+        end.record()
+        GEMM_EVENTS.append((start, end, 2.0 * m * n * k * batch, precision))

@@ -33,6 +33,7 @@ import torch.nn.functional as F
 
 from mround_b200 import kernels
 from mround_b200.pipeline.arch import Arch
+from mround_b200.pipeline.attention import attention
 from mround_b200.pipeline.model import BlockParams
 
 __all__ = ["FusedLinear", "DeviceBlock", "Precision", "FUSION"]
@@ -222,8 +223,7 @@ class DeviceBlock:
         cos, sin = self._tables(s)
         q = apply_rope(q, cos, sin)
         k = apply_rope(k, cos, sin)
-        att = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=1.0 / math.sqrt(a.head_dim),
-                                             enable_gqa=True)
+        att = attention(q, k, v, 1.0 / math.sqrt(a.head_dim))
         att = att.transpose(1, 2).reshape(b, s, a.q_dim)
         h = x + lin("o", att)
         h2 = rms_norm(h, self.post_norm, a.rms_eps)

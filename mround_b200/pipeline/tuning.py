@@ -1,0 +1,312 @@
+"""The per-block tuning step on one GPU (or one data-parallel rank).
+
+One step of ``QuantizationRunner._tune`` (reference
+mround/pipeline/runner.py:914-937) is, here:
+
+1. forward of the block on the fake-quantized operands (K3 GEMMs, torch for
+   norms/rope/attention/SwiGLU);
+2. K4: residual, exact outlier threshold (radix select; the histograms are
+   all-reduced across data-parallel ranks), loss and dL/dout;
+3. backward: K3 GEMMs for dX and dW, each fused weight's dW all-reduced over
+   NCCL as soon as it is produced (overlapping the rest of the backward);
+4. K2 per tunable linear: straight-through gradient, signed step, projection
+   and -- fused into the same pass -- the next step's fake-quantized operand.
+
+No host synchronisation happens inside a step: per-step losses stay on the
+device and are read once per block.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from mround_b200 import kernels
+from mround_b200.core.quantizer import require_device_scheme
+from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision
+from mround_b200.pipeline.dist import DistContext
+from mround_b200.schemes import QuantScheme
+
+__all__ = ["BlockTuner", "Member", "QuantizedLayer", "TunableLayer", "piece_bounds"]
+
+OUTLIER_FRACTION = 0.001
+
+
+def piece_bounds(size: int, pieces: int) -> list[tuple[int, int]]:
+    """Contiguous, near-even runs (reference mround/pipeline/blocks.py:609-624)."""
+    count = max(1, min(pieces, size))
+    base, extra = divmod(size, count)
+    bounds, start = [], 0
+    for piece in range(count):
+        stop = start + base + (1 if piece < extra else 0)
+        bounds.append((start, stop))
+        start = stop
+    return bounds
+
+
+@dataclasses.dataclass
+class QuantizedLayer:
+    """One committed layer, already in MLX's stored form.
+
+    ``packed`` uint32 words (held as int32) (out, in*bits/32), ``scales`` and
+    ``biases`` bf16 (out, n_groups), ``codes`` uint8 (out, in) when kept.
+    """
+
+    packed: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    scheme: QuantScheme
+    shape: tuple[int, int]
+    codes: torch.Tensor | None = None
+
+
+@dataclasses.dataclass
+class Member:
+    path: str
+    rows: tuple[int, int]
+    scheme: QuantScheme
+    group: int
+    lr0: float
+
+
+class TunableLayer:
+    """V / alpha / beta of one fused weight and the operands derived from them."""
+
+    def __init__(self, layer: FusedLinear, members: list[Member], eps: float) -> None:
+        self.layer = layer
+        self.members = members
+        self.eps = eps
+        out, inn = layer.w.shape
+        groups = {m.group for m in members}
+        if len(groups) != 1:
+            raise ValueError("members of one fused weight must share a group size")
+        self.group = groups.pop()
+        dev = layer.w.device
+        self.v = torch.zeros((out, inn), dtype=torch.float32, device=dev)
+        self.alpha = torch.ones((out, inn // self.group), dtype=torch.float32, device=dev)
+        self.beta = torch.ones_like(self.alpha)
+        tuned_rows = sum(m.rows[1] - m.rows[0] for m in members)
+        if tuned_rows == out:
+            layer.wq_hi = torch.empty_like(layer.w)
+            layer.wq_lo = torch.empty_like(layer.w)
+        else:  # rows of untuned members stay exact
+            layer.wq_hi = layer.w.clone()
+            layer.wq_lo = torch.zeros_like(layer.w)
+        layer.grad = torch.empty((out, inn), dtype=torch.float32, device=dev)
+        self.requantize()
+
+    def _slices(self, m: Member):
+        r0, r1 = m.rows
+        return (self.layer.w[r0:r1], self.v[r0:r1], self.alpha[r0:r1], self.beta[r0:r1])
+
+    def requantize(self) -> None:
+        """K1 on every member: refresh the operand from the current parameters."""
+        for m in self.members:
+            w, v, a, b = self._slices(m)
+            r0, r1 = m.rows
+            kernels.fq_forward(w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps,
+                               wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1])
+
+    def update(self, step: int, iters: int) -> None:
+        """K2 on every member with the linearly decayed rate of this step."""
+        for m in self.members:
+            w, v, a, b = self._slices(m)
+            r0, r1 = m.rows
+            lr = m.lr0 * (1.0 - step / iters) if step < iters else 0.0
+            lo, hi = m.scheme.coefficient_bounds
+            kernels.ste_signsgd(self.layer.grad[r0:r1], w, v, a, b, bits=m.scheme.bits,
+                                group=m.group, eps=self.eps, lr=lr, lo=lo, hi=hi, update=True,
+                                wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1])
+
+    def gradients(self) -> dict[str, tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+        """K2 without the update: (gV, galpha, gbeta) per member, from ``layer.grad``."""
+        out = {}
+        for m in self.members:
+            w, v, a, b = self._slices(m)
+            r0, r1 = m.rows
+            gv, ga, gb = torch.empty_like(v), torch.empty_like(a), torch.empty_like(b)
+            kernels.ste_signsgd(self.layer.grad[r0:r1], w, v, a, b, bits=m.scheme.bits,
+                                group=m.group, eps=self.eps, lr=0.0, lo=0.0, hi=1.0, update=False,
+                                gv=gv, galpha=ga, gbeta=gb)
+            out[m.path] = (gv, ga, gb)
+        return out
+
+    def load(self, path: str, v: torch.Tensor, alpha: torch.Tensor, beta: torch.Tensor) -> None:
+        """Set one member's parameters (used by parity tests and resume)."""
+        for m in self.members:
+            if m.path == path:
+                r0, r1 = m.rows
+                self.v[r0:r1].copy_(v)
+                self.alpha[r0:r1].copy_(alpha)
+                self.beta[r0:r1].copy_(beta)
+        self.requantize()
+
+    def reset(self) -> None:
+        self.v.zero_()
+        self.alpha.fill_(1.0)
+        self.beta.fill_(1.0)
+        self.requantize()
+
+    def commit(self, keep_codes: bool = False) -> dict[str, QuantizedLayer]:
+        """K5 per member, then make the layer's weight bf16(reconstruction)
+        (reference mround/pipeline/runner.py:775-787)."""
+        out: dict[str, QuantizedLayer] = {}
+        committed = self.layer.w.clone()
+        for m in self.members:
+            w, v, a, b = self._slices(m)
+            r0, r1 = m.rows
+            packed, scales, biases, codes = kernels.pack_mlx(
+                w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps, want_codes=keep_codes)
+            kernels.fq_forward(w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps,
+                               wq_hi=committed[r0:r1])
+            out[m.path] = QuantizedLayer(packed.cpu(), scales.cpu(), biases.cpu(), m.scheme,
+                                         (r1 - r0, w.shape[1]),
+                                         None if codes is None else codes.cpu())
+        self.layer.wq_hi, self.layer.wq_lo, self.layer.grad = committed, None, None
+        return out
+
+
+class BlockTuner:
+    """Runs the tuning of one block over this rank's shard of the batches."""
+
+    def __init__(self, block: DeviceBlock, schemes: dict[str, QuantScheme], lrs: dict[str, float],
+                 *, suppress: bool, eps: float, precision: Precision, dist: DistContext,
+                 pieces: int = 1) -> None:
+        self.block = block
+        self.suppress = suppress
+        self.precision = precision
+        self.dist = dist
+        self.pieces = pieces
+        self.tunables: list[TunableLayer] = []
+        self.skipped: list[tuple[str, str]] = []
+        for layer in block.layers.values():
+            members = []
+            for path, r0, r1 in layer.members:
+                if path not in schemes:
+                    continue
+                scheme = schemes[path]
+                try:
+                    group = require_device_scheme(scheme, layer.in_features)
+                except Exception as exc:  # noqa: BLE001 - reported like the reference's skip
+                    self.skipped.append((path, str(exc)))
+                    continue
+                members.append(Member(path, (r0, r1), scheme, group, lrs[path]))
+            if members:
+                self.tunables.append(TunableLayer(layer, members, eps))
+                if dist.world > 1:
+                    layer.grad_ready.append(self._reduce_hook)
+        self.ws = kernels.LossWorkspace(block.device)
+        self._pending: dict[int, object] = {}
+        self._last_piece = True
+
+    # ------------------------------------------------------------ pieces
+    def _reduce_hook(self, layer: FusedLinear) -> None:
+        if self._last_piece:
+            self._pending[id(layer)] = self.dist.all_reduce_async(layer.grad)
+
+    def _wait(self, layer: FusedLinear) -> None:
+        work = self._pending.pop(id(layer), None)
+        if work is not None:
+            work.wait()
+
+    # ------------------------------------------------------------ loss
+    def _threshold(self, pred: torch.Tensor, target: torch.Tensor, k: int) -> None:
+        """Exact global k-th largest |r| into ``ws.thr`` (three radix passes)."""
+        for p in range(3):
+            kernels.loss_hist_pass(pred, target, self.ws, p)
+            self.dist.all_reduce_(self.ws.hist)
+            kernels.loss_select_digit(self.ws, k, p)
+
+    def loss(self, pred: torch.Tensor, target: torch.Tensor, *, grad: torch.Tensor | None,
+             threshold_ready: bool = False) -> torch.Tensor:
+        """This rank's share of the batch loss (device float64 scalar)."""
+        n_global = pred.numel() * self.dist.world if not threshold_ready else self._n_global
+        k = max(1, int(n_global * OUTLIER_FRACTION))
+        if self.dist.world == 1 and not threshold_ready:
+            kernels.loss_outlier(pred, target, self.ws, suppress=self.suppress, denom=float(n_global),
+                                 k=k, grad=grad)
+        else:
+            if self.suppress and not threshold_ready:
+                self._threshold(pred, target, k)
+            kernels.loss_apply(pred, target, self.ws, suppress=self.suppress,
+                               denom=float(n_global), grad=grad)
+        return self.ws.loss.clone()
+
+    # ------------------------------------------------------------ passes
+    def output(self, x: torch.Tensor) -> torch.Tensor:
+        with torch.no_grad():
+            if self.pieces == 1:
+                return self.block.forward(x, self.precision)
+            parts = [self.block.forward(x[lo:hi], self.precision)
+                     for lo, hi in piece_bounds(x.shape[0], self.pieces)]
+            return torch.cat(parts, 0)
+
+    def batch_loss(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        return self.loss(self.output(x), target, grad=None)
+
+    def mean_loss(self, inputs: list[torch.Tensor], targets: list[torch.Tensor],
+                  batches: list[int]) -> float:
+        """Mean over batches of the global batch loss; one host read."""
+        vals = torch.stack([self.batch_loss(inputs[i], targets[i]) for i in batches])
+        self.dist.all_reduce_(vals)
+        return float(vals.mean().item())
+
+    def step(self, x: torch.Tensor, target: torch.Tensor, step: int, iters: int) -> torch.Tensor:
+        """One signed-gradient step on one batch; returns this rank's loss share."""
+        bounds = piece_bounds(x.shape[0], self.pieces)
+        if len(bounds) == 1:
+            self._last_piece = True
+            for t in self.tunables:
+                t.layer.accumulate_grad = False
+            out = self.block.forward(x, self.precision, train=True)
+            grad = torch.empty_like(out)
+            loss = self.loss(out, target, grad=grad)
+            out.backward(grad)
+        else:
+            # whole-batch threshold first, then each piece against it
+            self._n_global = x.numel() * self.dist.world
+            if self.suppress:
+                k = max(1, int(self._n_global * OUTLIER_FRACTION))
+                self._threshold(self.output(x), target, k)
+            loss = torch.zeros((), dtype=torch.float64, device=x.device)
+            for i, (lo, hi) in enumerate(bounds):
+                self._last_piece = i == len(bounds) - 1
+                for t in self.tunables:
+                    t.layer.accumulate_grad = i > 0
+                out = self.block.forward(x[lo:hi], self.precision, train=True)
+                grad = torch.empty_like(out)
+                loss += self.loss(out, target[lo:hi], grad=grad, threshold_ready=True)
+                out.backward(grad)
+        for t in self.tunables:
+            self._wait(t.layer)
+            t.update(step, iters)
+        return loss
+
+    def gradient_only(self, x: torch.Tensor, target: torch.Tensor):
+        """Forward, loss and backward without a step; returns (loss, grads by path)."""
+        self._last_piece = True
+        for t in self.tunables:
+            t.layer.accumulate_grad = False
+        out = self.block.forward(x, self.precision, train=True)
+        grad = torch.empty_like(out)
+        loss = self.loss(out, target, grad=grad)
+        out.backward(grad)
+        grads = {}
+        for t in self.tunables:
+            self._wait(t.layer)
+            grads.update(t.gradients())
+        return loss, grads
+
+    def reset(self) -> None:
+        for t in self.tunables:
+            t.reset()
+
+    def snapshot(self) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+        return [(t.v.clone(), t.alpha.clone(), t.beta.clone()) for t in self.tunables]
+
+    def commit(self, keep_codes: bool = False) -> dict[str, QuantizedLayer]:
+        out: dict[str, QuantizedLayer] = {}
+        for t in self.tunables:
+            out.update(t.commit(keep_codes))
+        return out

@@ -54,3 +54,26 @@ def loss_and_grad(pred, target, *, suppress: bool, elements: int | None = None,
     loss = float(np.sum(kept.astype(np.float64) ** 2) / n)
     grad = (np.float32(2.0) * kept / np.float32(n)).astype(np.float32)
     return loss, grad, thr
+
+
+def radix_digit_hist(residual: np.ndarray, pass_index: int, prefix: int, mask: int) -> np.ndarray:
+    """Histogram of one radix digit of |r|'s bit pattern among keys matching the
+    prefix -- the same digit layout as the device selection ([21,31), [10,21), [0,10))."""
+    keys = np.abs(np.asarray(residual, np.float32)).reshape(-1).view(np.uint32) & np.uint32(0x7FFFFFFF)
+    shift = (21, 10, 0)[pass_index]
+    dmask = (0x3FF, 0x7FF, 0x3FF)[pass_index]
+    sel = keys[(keys & np.uint32(mask)) == np.uint32(prefix)]
+    return np.bincount(((sel >> np.uint32(shift)) & np.uint32(dmask)).astype(np.int64),
+                       minlength=2048).astype(np.int64)
+
+
+def radix_select_step(hist: np.ndarray, k_left: int, pass_index: int, prefix: int, mask: int):
+    """Pick the digit holding the k_left-th largest; returns (prefix, mask, k_left)."""
+    shift = (21, 10, 0)[pass_index]
+    dmask = (0x3FF, 0x7FF, 0x3FF)[pass_index]
+    above = 0
+    for b in range(dmask, -1, -1):
+        if above + int(hist[b]) >= k_left:
+            return prefix | (b << shift), mask | (dmask << shift), k_left - above
+        above += int(hist[b])
+    raise ValueError("k exceeds the candidate count")
