@@ -133,6 +133,28 @@ int mr_loss_outlier(const float* pred, const float* target, int64_t n, int64_t k
                     double* loss, float* thr_out, void* workspace, void* stream);
 
 /*
+ * K4 without a workspace argument.  No counterpart in the reference: MRound
+ * has no native code and no caller that must avoid allocation.  It exists
+ * for callers of this library that cannot allocate device memory themselves
+ * -- a host binding the C ABI through an FFI with no device allocator, or an
+ * asynchronous pipeline that must not call cudaMalloc because cudaMalloc can
+ * synchronize the device.  Same arguments and results as mr_loss_outlier,
+ * but the scratch lives in a fixed 16 KiB array compiled into the library
+ * (mr_loss_noalloc_scratch_bytes), held by every GPU that loads the library
+ * until the process exits.  n above 2^32 - 1 elements is refused with
+ * MR_ERR_ARGUMENT (the selection counters are 32-bit).  The first call on
+ * each device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls that overlap on the GPU (two streams, or two host threads on
+ * one device) race and must be serialized by the caller.  Nothing is
+ * allocated or freed.
+ */
+size_t mr_loss_noalloc_scratch_bytes(void);
+int mr_loss_outlier_noalloc(const float* pred, const float* target, int64_t n, int64_t k,
+                            int suppress, double denom, float thr_in, float* grad,
+                            double* loss, float* thr_out, void* stream);
+
+/*
  * K4, distributed form: one radix pass of the global threshold selection.
  * pass = 0, 1, 2 over key bits [21,31), [10,21), [0,10) of |r|.  Each pass
  * writes this rank's histogram of the candidates to hist (2048 uint32); the

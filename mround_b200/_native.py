@@ -47,6 +47,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_pack_mlx": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _P, _P, _P]),
     "mr_loss_workspace_bytes": (ctypes.c_size_t, []),
     "mr_loss_outlier": (_I, [_P, _P, _I64, _I64, _I, _D, _F, _P, _P, _P, _P, _P]),
+    "mr_loss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "mr_loss_outlier_noalloc": (_I, [_P, _P, _I64, _I64, _I, _D, _F, _P, _P, _P, _P]),
     "mr_loss_hist_pass": (_I, [_P, _P, _I64, _I, _P, _P, _P]),
     "mr_loss_select_digit": (_I, [_P, _I64, _I, _P, _P, _P]),
     "mr_loss_apply": (_I, [_P, _P, _I64, _D, _P, _I, _P, _P, _P, _P]),

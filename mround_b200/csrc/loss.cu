@@ -13,6 +13,8 @@
 // The loss sum is deterministic: per-block float64 partials are reduced by a
 // single block in a fixed order.
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mr {
@@ -248,4 +250,72 @@ extern "C" int mr_loss_outlier(const float* pred, const float* target, int64_t n
                                                  suppress, grad, ws->partial);
   finish_kernel<<<1, kThreads, 0, s>>>(ws->partial, kApplyBlocks, denom, loss);
   return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of mr_loss_outlier.
+//
+// Some callers of this library cannot hand it device memory: a host that
+// binds the plain C ABI through an FFI and owns no device allocator, or a
+// pipeline that must not call cudaMalloc because cudaMalloc may synchronize
+// the device in the middle of its asynchronous work.  For them the loss
+// kernels' scratch (selection state, one histogram, per-block partial sums:
+// sizeof(Workspace) bytes) lives in a fixed array compiled into the library.
+// Every GPU that loads the library holds this array until the process exits.
+namespace mr {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16384;  // stated maximum: 16 KiB
+static_assert(sizeof(Workspace) <= kNoAllocScratchBytes, "loss scratch exceeds the static array");
+
+static __device__ __align__(256) unsigned char g_loss_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// Device address of the array on the current device.  Host code may not use
+// the symbol itself as a pointer (it names a host-side stand-in), so the
+// address is looked up once per device, with that device current.
+int scratch_for_current_device(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return MR_ERR_DEVICE;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return MR_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_loss_scratch);
+    if (e != cudaSuccess || !p) {
+      set_cuda_error(e);
+      return MR_ERR_DEVICE;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return MR_OK;
+}
+
+}  // namespace
+}  // namespace mr
+
+extern "C" size_t mr_loss_noalloc_scratch_bytes(void) { return mr::kNoAllocScratchBytes; }
+
+extern "C" int mr_loss_outlier_noalloc(const float* pred, const float* target, int64_t n,
+                                       int64_t k, int suppress, double denom, float thr_in,
+                                       float* grad, double* loss, float* thr_out, void* stream) {
+  // histogram counters are 32-bit: larger inputs are refused rather than miscounted
+  if (n > int64_t(0xFFFFFFFFll)) return MR_ERR_ARGUMENT;
+  void* scratch = nullptr;
+  int st = mr::scratch_for_current_device(&scratch);
+  if (st) return st;
+  // Every field of the scratch that is read is first written by this call:
+  // the histogram is cleared by each pass, the selection state is reset by
+  // pass 0, and the partial sums are overwritten -- stale contents from an
+  // earlier call are never read.
+  return mr_loss_outlier(pred, target, n, k, suppress, denom, thr_in, grad, loss, thr_out,
+                         scratch, stream);
 }
