@@ -1,0 +1,118 @@
+"""Data-parallel step on 2 GPUs (NCCL) against one process on the whole batch.
+
+Each rank holds half the sequences of the batch; the threshold comes from
+all-reduced histograms, the weight gradients from an all-reduce, and every
+rank applies the same K2 step.  Against a single-process step on the whole
+batch: the loss agrees to float64 summation order and the exact outlier
+threshold is identical; V after the step agrees except where a gradient's
+sign flips between two summation orders (bounded here at 0.1 % of entries);
+and the two ranks hold bitwise identical parameters.  Skipped with fewer
+than two GPUs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+ARCH = "tiny-qwen2"
+SHAPE = (4, 64)
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _setup(device):
+    from mround_b200.pipeline.arch import get_arch
+    from mround_b200.pipeline.block import DeviceBlock
+    from mround_b200.pipeline.model import SyntheticModel
+
+    arch = get_arch(ARCH)
+    params = SyntheticModel(arch, seed=21).block(0)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(*SHAPE, arch.hidden, generator=g) * 0.02
+    tgt = x + 1e-3 * torch.randn(*SHAPE, arch.hidden, generator=g)
+    return arch, DeviceBlock(arch, params, device), x, tgt
+
+
+def _tuner(block, dist):
+    from mround_b200.pipeline.block import Precision
+    from mround_b200.pipeline.tuning import BlockTuner
+    from mround_b200.schemes import QuantScheme
+    from oracle.block_tuner import LINEARS
+
+    scheme = QuantScheme(bits=2, group_size=32, symmetry="asym")
+    return BlockTuner(block, {p: scheme for p in LINEARS}, {p: 0.05 for p in LINEARS},
+                      suppress=True, eps=1e-8, precision=Precision(), dist=dist)
+
+
+def _rank(rank, world, port, q):
+    import torch.distributed as tdist
+
+    from mround_b200.pipeline.dist import DistContext
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+
+    tdist.init_process_group("nccl", rank=rank, world_size=world,
+                             timeout=datetime.timedelta(seconds=120))
+    try:
+        ctx = DistContext(rank, world)
+        dev = torch.device("cuda", rank)
+        _, block, x, tgt = _setup(dev)
+        rows = ctx.shard(SHAPE[0])
+        tuner = _tuner(block, ctx)
+        loss = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 0, 10)
+        total = loss.clone()
+        ctx.all_reduce_(total)
+        torch.cuda.synchronize(dev)
+        q.put((rank, float(total.item()), float(tuner.ws.thr.item()),
+               [t.v.cpu().numpy() for t in tuner.tunables],
+               [t.alpha.cpu().numpy() for t in tuner.tunables]))
+        tdist.barrier()
+    finally:
+        tdist.destroy_process_group()
+
+
+def test_two_gpu_step_matches_single_process():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from mround_b200.pipeline.dist import DistContext
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # single process, whole batch, on GPU 0
+    dev = torch.device("cuda", 0)
+    _, block, x, tgt = _setup(dev)
+    tuner = _tuner(block, DistContext())
+    loss = tuner.step(x.to(dev), tgt.to(dev), 0, 10)
+    torch.cuda.synchronize(dev)
+    want_v = [t.v.cpu().numpy() for t in tuner.tunables]
+    assert res[0][1] == pytest.approx(loss.item(), rel=1e-6)
+    assert res[0][2] == tuner.ws.thr.item()
+    for a, b in zip(res[0][3], res[1][3]):
+        assert np.array_equal(a, b), "ranks must hold identical parameters"
+    for a, b in zip(res[0][4], res[1][4]):
+        assert np.array_equal(a, b)
+    differing = sum(int((a != b).sum()) for a, b in zip(res[0][3], want_v))
+    total = sum(a.size for a in want_v)
+    assert differing / total < 1e-3, f"{differing} of {total} V entries differ"
