@@ -1,0 +1,189 @@
+"""DeltaLoss sensitivity scoring of every block layer at every candidate width.
+
+Restates ``score_widths`` (reference mround/pipeline/scoring.py:425-583) on the
+device: a whole-model causal-LM backward (mean shifted cross-entropy,
+``_causal_loss`` 183-192) through block linears whose weights are replaced by
+their round-to-nearest quantize-dequantize (``_anchor`` 224-235), then for every
+layer and width ``sum |g * (Q_b(W) - W)|`` accumulated over batches
+(``_accumulate`` 238-266, the term of line 262).  The term is K6
+(``mr_deltaloss``): it runs the moment a layer's weight-gradient GEMM finishes,
+reading the gradient once for all widths it scores, so no gradient or
+perturbation is ever held beyond its layer.
+
+``own_width`` takes one backward per width at that width's anchors (the
+reference's procedure); ``widest`` one backward at the widest width, scoring
+every width's perturbation against it.  Sequences are padded to a multiple of
+8 tokens at the end; causal attention keeps real positions unaffected and the
+loss averages the real positions only.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import time
+from collections.abc import Callable, Sequence
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from mround_b200 import kernels
+from mround_b200.exceptions import SchemeError
+from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision, rms_norm
+from mround_b200.pipeline.model import SyntheticModel
+from mround_b200.schemes import DEFAULT_EPS_FP32, QuantScheme
+
+__all__ = ["SensitivityScores", "score_widths"]
+
+
+@dataclasses.dataclass(frozen=True)
+class SensitivityScores:
+    scores: dict[str, dict[int, float]]
+    shapes: dict[str, tuple[int, int]]
+    skipped: tuple[tuple[str, str], ...]
+    seconds: float
+
+
+class _LMHead(torch.autograd.Function):
+    """logits = h @ E^T with E exact in bf16 (two products); dh = dlogits @ E."""
+
+    @staticmethod
+    def forward(ctx, h, weight):
+        t, d = h.shape
+        v = weight.shape[0]
+        h_hi, h_lo = kernels.split_bf16(h.contiguous())
+        logits = torch.empty((t, v), dtype=torch.float32, device=h.device)
+        kernels.gemm(h_hi, h_lo, weight, None, logits, m=t, n=v, k=d, a_kmajor=True, b_kmajor=True,
+                     lda=d, ldb=d, ldc=v, precision=2)
+        ctx.weight = weight
+        return logits
+
+    @staticmethod
+    def backward(ctx, dlogits):
+        weight = ctx.weight
+        v, d = weight.shape
+        dl = dlogits.contiguous().float()
+        t = dl.shape[0]
+        g_hi, g_lo = kernels.split_bf16(dl)
+        dh = torch.empty((t, d), dtype=torch.float32, device=dl.device)
+        kernels.gemm(g_hi, g_lo, weight, None, dh, m=t, n=d, k=v, a_kmajor=True, b_kmajor=False,
+                     lda=v, ldb=d, ldc=d, precision=2)
+        return dh, None
+
+
+def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: Sequence[int],
+                 base_scheme: QuantScheme, *, expected_blocks: int | None = None,
+                 eps: float = DEFAULT_EPS_FP32, gradient_source: str = "own_width",
+                 progress: Callable[[str], None] | None = None,
+                 device: torch.device | str = "cuda") -> SensitivityScores:
+    """Score every block linear at every width (float64 sums on the device)."""
+    if not widths:
+        raise ValueError("no candidate widths to score")
+    if gradient_source not in ("own_width", "widest"):
+        raise ValueError(f"gradient_source must be 'own_width' or 'widest', got {gradient_source!r}")
+    started = time.perf_counter()
+    dev = torch.device(device)
+    arch = model.arch
+    if expected_blocks is not None and expected_blocks != arch.layers:
+        from mround_b200.exceptions import ArchitectureError
+
+        raise ArchitectureError(f"found {arch.layers} blocks but the configuration says {expected_blocks}")
+    group = base_scheme.group_size
+    widths = sorted(int(w) for w in widths)
+    prec = Precision()
+    blocks = [DeviceBlock(arch, model.block(i), dev) for i in range(arch.layers)]
+    shapes, skipped, paths_by_layer = {}, [], {}
+    for blk in blocks:
+        name = model.block_name(blk.index)
+        for layer in blk.layers.values():
+            members = []
+            for path, r0, r1 in layer.members:
+                full = f"{name}.{path}"
+                if layer.in_features % group:
+                    skipped.append((full, f"last dimension {layer.in_features} is not a multiple of {group}"))
+                    continue
+                if group not in kernels.DEVICE_GROUPS:
+                    raise SchemeError(f"group size {group} is not a device group size")
+                shapes[full] = (r1 - r0, layer.in_features)
+                members.append((full, r0, r1))
+            paths_by_layer[id(layer)] = members
+    if not shapes:
+        raise ValueError("no layer in any block can be quantized at this group size")
+    # one float32 gradient buffer per fused shape, shared by all blocks
+    grad_pool: dict[tuple[int, int], torch.Tensor] = {}
+    for blk in blocks:
+        for layer in blk.layers.values():
+            key = tuple(layer.w.shape)
+            if key not in grad_pool:
+                grad_pool[key] = torch.empty(key, dtype=torch.float32, device=dev)
+            layer.grad = grad_pool[key]
+    acc = {p: torch.zeros(len(widths), dtype=torch.float64, device=dev) for p in shapes}
+    active: dict[str, list[int]] = {}
+
+    def on_grad(layer: FusedLinear) -> None:
+        for full, r0, r1 in paths_by_layer[id(layer)]:
+            bits = active["bits"]
+            out = torch.zeros(len(bits), dtype=torch.float64, device=dev)
+            kernels.deltaloss(layer.grad[r0:r1], layer.w[r0:r1], bits=bits, group=group, eps=eps,
+                              out=out)
+            idx = [widths.index(b) for b in bits]
+            acc[full][idx] += out
+
+    for blk in blocks:
+        for layer in blk.layers.values():
+            layer.grad_ready.append(on_grad)
+
+    def set_anchors(bits: int) -> None:
+        ones = {}
+        for blk in blocks:
+            for layer in blk.layers.values():
+                o, i = layer.w.shape
+                if layer.in_features % group:
+                    layer.use_dense()
+                    continue
+                key = (o, i // group)
+                if key not in ones:
+                    ones[key] = torch.ones(key, dtype=torch.float32, device=dev)
+                zeros = torch.zeros((o, i), dtype=torch.float32, device=dev)
+                hi, lo = torch.empty_like(layer.w), torch.empty_like(layer.w)
+                kernels.fq_forward(layer.w, zeros, ones[key], ones[key], bits=bits, group=group,
+                                   eps=eps, wq_hi=hi, wq_lo=lo)
+                layer.wq_hi, layer.wq_lo = hi, lo
+
+    embed = model.embed_tokens().to(dev)
+    head = model.lm_head().to(dev)
+    final_norm = model.final_norm().to(dev)
+
+    def backward_pass(batch: np.ndarray) -> None:
+        tokens = torch.as_tensor(batch, dtype=torch.long, device=dev)
+        inp, labels = tokens[:, :-1], tokens[:, 1:]
+        b, s = inp.shape
+        pad = (-s) % 8
+        if pad:
+            inp = torch.cat([inp, inp[:, -1:].expand(b, pad)], dim=1)
+        x = embed[inp].float()
+        for blk in blocks:
+            x = blk.forward(x, prec, train=True)
+        h = rms_norm(x, final_norm, arch.rms_eps)[:, :s].reshape(b * s, -1)
+        logits = _LMHead.apply(h, head)
+        loss = F.cross_entropy(logits, labels.reshape(-1), reduction="mean")
+        loss.backward()
+
+    schedule = [(w, [w]) for w in widths] if gradient_source == "own_width" else [(widths[-1], widths)]
+    done = 0
+    for anchor_bits, scored in schedule:
+        set_anchors(anchor_bits)
+        active["bits"] = scored
+        for batch in batches:
+            backward_pass(batch)
+            done += 1
+            if progress is not None:
+                progress(f"  scoring: backward {done}/{len(batches) * len(schedule)} "
+                         f"at {time.perf_counter() - started:.0f}s")
+    torch.cuda.synchronize(dev)
+    for blk in blocks:
+        for layer in blk.layers.values():
+            layer.grad_ready.clear()
+            layer.grad = None
+    scores = {p: {w: float(acc[p][j].item()) for j, w in enumerate(widths)} for p in shapes}
+    return SensitivityScores(scores, shapes, tuple(skipped), time.perf_counter() - started)
