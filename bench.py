@@ -141,7 +141,7 @@ def build_workload(args, dist, device):
     block = DeviceBlock(arch, model.block(0), device)
     prec = Precision()
     with torch.no_grad():
-        targets = [block.forward(x, prec) for x in inputs]
+        targets = [block.forward_fused(x, prec, False)[0] for x in inputs]
     return arch, model, block, inputs, targets
 
 

@@ -191,6 +191,44 @@ int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t c
 int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* stream);
 
 /*
+ * Fused element-wise operators of the decoder block (the mlx-lm layer the
+ * reference runs inside block_output, mround/pipeline/blocks.py:578-606).
+ * Each reads float32 activations and writes the next GEMM operand directly as
+ * a bf16 hi/lo pair.  Token t = b*S + s; attention operands are (B, H, S, D).
+ *   mr_rmsnorm_split:     y = x * rsqrt(mean(x^2) + eps) * w; rstd per row
+ *   mr_rmsnorm_bwd_split: dx = resid + rstd * (g - xhat * mean(g * xhat)), g = dy * w
+ *   mr_rope_split:        qkv (T, (Hq+2Hkv)*D) -> rope(q), rope(k), v as (B,H,S,D)
+ *   mr_rope_bwd_split:    dq, dk, dv (B,H,S,D) -> dqkv (T, (Hq+2Hkv)*D)
+ *   mr_heads_split:       merge=1: (B,H,S,D) -> (T, H*D); merge=0: the reverse
+ *   mr_swiglu_split:      act = silu(g) * u, gu = [g | u] per row
+ *   mr_swiglu_bwd_split:  dgu = [dact * u * silu'(g) | dact * silu(g)]
+ *   mr_softmax_causal_split: rows of length S, row r at position r % S:
+ *                         P = softmax(scale * scores) over columns <= position,
+ *                         written in place (float32) and as hi/lo
+ *   mr_softmax_bwd_split: dS = scale * P * (dP - sum(dP * P))
+ */
+int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows, int h, float eps,
+                     uint16_t* hi, uint16_t* lo, float* rstd, void* stream);
+int mr_rmsnorm_bwd_split(const float* dy, const float* x, const uint16_t* w, const float* rstd,
+                         const float* resid, int64_t rows, int h, uint16_t* hi, uint16_t* lo,
+                         void* stream);
+int mr_rope_split(const float* qkv, const float* cosv, const float* sinv, int b, int s, int hq,
+                  int hkv, int d, uint16_t* q_hi, uint16_t* q_lo, uint16_t* k_hi, uint16_t* k_lo,
+                  uint16_t* v_hi, uint16_t* v_lo, void* stream);
+int mr_rope_bwd_split(const float* dq, const float* dk, const float* dv, const float* cosv,
+                      const float* sinv, int b, int s, int hq, int hkv, int d, uint16_t* hi,
+                      uint16_t* lo, void* stream);
+int mr_heads_split(const float* src, int b, int s, int h, int d, int merge, uint16_t* hi,
+                   uint16_t* lo, void* stream);
+int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo, void* stream);
+int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t, int i, uint16_t* hi,
+                        uint16_t* lo, void* stream);
+int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale, uint16_t* hi,
+                            uint16_t* lo, void* stream);
+int mr_softmax_bwd_split(const float* dp, const float* p, int64_t rows, int s, float scale,
+                         uint16_t* hi, uint16_t* lo, void* stream);
+
+/*
  * K3 -- tcgen05/TMEM GEMM, bf16 operands, float32 accumulate in tensor memory.
  * The contraction of every decoder-block linear in the tuning step
  * (mround/pipeline/runner.py:367, y = x @ Wq.T, and the two products its

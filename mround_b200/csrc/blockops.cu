@@ -1,0 +1,433 @@
+// Fused element-wise kernels of the decoder block (forward and backward).
+//
+// Each kernel reads float32 activations once and writes the next GEMM's
+// operand directly as a bf16 hi/lo pair (hi = bf16(y), lo = bf16(y - hi)),
+// so no float32 intermediate is materialised between an element-wise op and
+// the tcgen05 GEMM that consumes it.  The math is the mlx-lm decoder layer's
+// (the layer the reference runs in block_output,
+// mround/pipeline/blocks.py:578-606): RMSNorm, non-interleaved RoPE, causal
+// softmax, SwiGLU, and their derivatives.  All HBM-bound.
+//
+// Layouts: token t = b*S + s; qkv rows are [q heads | k heads | v heads] x D;
+// attention operands are (B, H, S, D) contiguous.
+
+#include "common.cuh"
+
+namespace mr {
+namespace {
+
+__device__ __forceinline__ void put_split(uint16_t* hi, uint16_t* lo, int64_t i, float v) {
+  const uint16_t h = f32_to_bf16(v);
+  hi[i] = h;
+  lo[i] = f32_to_bf16(__fsub_rn(v, bf16_to_f32(h)));
+}
+
+__device__ __forceinline__ void put_split4(uint16_t* hi, uint16_t* lo, int64_t i, float4 v) {
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  uint16_t h[4], l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    h[j] = f32_to_bf16(f[j]);
+    l[j] = f32_to_bf16(__fsub_rn(f[j], bf16_to_f32(h[j])));
+  }
+  *reinterpret_cast<uint2*>(hi + i) = make_uint2(uint32_t(h[0]) | (uint32_t(h[1]) << 16),
+                                                 uint32_t(h[2]) | (uint32_t(h[3]) << 16));
+  *reinterpret_cast<uint2*>(lo + i) = make_uint2(uint32_t(l[0]) | (uint32_t(l[1]) << 16),
+                                                 uint32_t(l[2]) | (uint32_t(l[3]) << 16));
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < THREADS / 32; ++i) s += sh[i];
+  __syncthreads();
+  return s;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_max(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) sh[w] = v;
+  __syncthreads();
+  float s = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < THREADS / 32; ++i) s = fmaxf(s, sh[i]);
+  __syncthreads();
+  return s;
+}
+
+constexpr int kRowThreads = 128;
+constexpr int kMaxVec = 16;  // float4 per thread: rows up to 8192
+
+// y = x * rsqrt(mean(x^2) + eps) * w  -> hi/lo, and rstd per row.
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_split_kernel(
+    const float* __restrict__ x, const uint16_t* __restrict__ w, int h, float eps,
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ rstd) {
+  __shared__ float sh[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * h);
+  const int n4 = h / 4;
+  float4 v[kMaxVec];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < n4) {
+      v[i] = xr[c];
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+  }
+  ss = block_sum<kRowThreads>(ss, sh);
+  const float r = rsqrtf(ss / float(h) + eps);
+  if (threadIdx.x == 0) rstd[row] = r;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < n4) {
+      const int e = c * 4;
+      float4 y;
+      y.x = __fmul_rn(__fmul_rn(v[i].x, r), bf16_to_f32(w[e]));
+      y.y = __fmul_rn(__fmul_rn(v[i].y, r), bf16_to_f32(w[e + 1]));
+      y.z = __fmul_rn(__fmul_rn(v[i].z, r), bf16_to_f32(w[e + 2]));
+      y.w = __fmul_rn(__fmul_rn(v[i].w, r), bf16_to_f32(w[e + 3]));
+      put_split4(hi, lo, row * h + e, y);
+    }
+  }
+}
+
+// dx = resid + rstd * (g - xhat * mean(g * xhat)),  g = dy * w,  xhat = x * rstd.
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_split_kernel(
+    const float* __restrict__ dy, const float* __restrict__ x, const uint16_t* __restrict__ w,
+    const float* __restrict__ rstd, const float* __restrict__ resid, int h,
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  __shared__ float sh[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const float r = rstd[row];
+  const float4* dyr = reinterpret_cast<const float4*>(dy + row * h);
+  const float4* xr = reinterpret_cast<const float4*>(x + row * h);
+  const int n4 = h / 4;
+  float4 g[kMaxVec], xh[kMaxVec];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < n4) {
+      const int e = c * 4;
+      const float4 a = dyr[c], b = xr[c];
+      g[i] = make_float4(a.x * bf16_to_f32(w[e]), a.y * bf16_to_f32(w[e + 1]),
+                         a.z * bf16_to_f32(w[e + 2]), a.w * bf16_to_f32(w[e + 3]));
+      xh[i] = make_float4(b.x * r, b.y * r, b.z * r, b.w * r);
+      dot += g[i].x * xh[i].x + g[i].y * xh[i].y + g[i].z * xh[i].z + g[i].w * xh[i].w;
+    }
+  }
+  dot = block_sum<kRowThreads>(dot, sh) / float(h);
+  const float4* rr = reinterpret_cast<const float4*>(resid + row * h);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < n4) {
+      const float4 q = rr[c];
+      float4 d;
+      d.x = q.x + r * (g[i].x - xh[i].x * dot);
+      d.y = q.y + r * (g[i].y - xh[i].y * dot);
+      d.z = q.z + r * (g[i].z - xh[i].z * dot);
+      d.w = q.w + r * (g[i].w - xh[i].w * dot);
+      put_split4(hi, lo, row * h + c * 4, d);
+    }
+  }
+}
+
+// qkv (T, (Hq+2Hkv)*D) -> rope(q), rope(k), v as (B,H,S,D) hi/lo.
+__global__ void rope_split_kernel(const float* __restrict__ qkv, const float* __restrict__ cosv,
+                                  const float* __restrict__ sinv, int B, int S, int Hq, int Hkv,
+                                  int D, uint16_t* __restrict__ q_hi, uint16_t* __restrict__ q_lo,
+                                  uint16_t* __restrict__ k_hi, uint16_t* __restrict__ k_lo,
+                                  uint16_t* __restrict__ v_hi, uint16_t* __restrict__ v_lo) {
+  const int half = D / 2;
+  const int H = Hq + 2 * Hkv;
+  const int64_t total = int64_t(B) * S * H * half;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int j = int(idx % half);
+    const int head = int((idx / half) % H);
+    const int64_t t = idx / (int64_t(half) * H);
+    const int s = int(t % S);
+    const int b = int(t / S);
+    const float* src = qkv + t * int64_t(H) * D + int64_t(head) * D;
+    const float x1 = src[j], x2 = src[j + half];
+    float o1 = x1, o2 = x2;
+    uint16_t *dh, *dl;
+    int64_t base;
+    if (head < Hq + Hkv) {
+      const float c = cosv[int64_t(s) * half + j], sn = sinv[int64_t(s) * half + j];
+      o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+      o2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, c));
+    }
+    if (head < Hq) {
+      dh = q_hi; dl = q_lo;
+      base = ((int64_t(b) * Hq + head) * S + s) * D;
+    } else if (head < Hq + Hkv) {
+      dh = k_hi; dl = k_lo;
+      base = ((int64_t(b) * Hkv + (head - Hq)) * S + s) * D;
+    } else {
+      dh = v_hi; dl = v_lo;
+      base = ((int64_t(b) * Hkv + (head - Hq - Hkv)) * S + s) * D;
+    }
+    put_split(dh, dl, base + j, o1);
+    put_split(dh, dl, base + j + half, o2);
+  }
+}
+
+// dq, dk, dv (B,H,S,D) -> dqkv (T, (Hq+2Hkv)*D) hi/lo, undoing the rotation.
+__global__ void rope_bwd_split_kernel(const float* __restrict__ dq, const float* __restrict__ dk,
+                                      const float* __restrict__ dv, const float* __restrict__ cosv,
+                                      const float* __restrict__ sinv, int B, int S, int Hq, int Hkv,
+                                      int D, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int half = D / 2;
+  const int H = Hq + 2 * Hkv;
+  const int64_t total = int64_t(B) * S * H * half;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int j = int(idx % half);
+    const int head = int((idx / half) % H);
+    const int64_t t = idx / (int64_t(half) * H);
+    const int s = int(t % S);
+    const int b = int(t / S);
+    const float* src;
+    if (head < Hq) src = dq + ((int64_t(b) * Hq + head) * S + s) * D;
+    else if (head < Hq + Hkv) src = dk + ((int64_t(b) * Hkv + (head - Hq)) * S + s) * D;
+    else src = dv + ((int64_t(b) * Hkv + (head - Hq - Hkv)) * S + s) * D;
+    const float d1 = src[j], d2 = src[j + half];
+    float g1 = d1, g2 = d2;
+    if (head < Hq + Hkv) {
+      const float c = cosv[int64_t(s) * half + j], sn = sinv[int64_t(s) * half + j];
+      g1 = d1 * c + d2 * sn;
+      g2 = d2 * c - d1 * sn;
+    }
+    const int64_t o = t * int64_t(H) * D + int64_t(head) * D;
+    put_split(hi, lo, o + j, g1);
+    put_split(hi, lo, o + j + half, g2);
+  }
+}
+
+// (B,H,S,D) float32 <-> (T, H*D): merge=1 reads heads and writes token rows.
+__global__ void heads_kernel(const float* __restrict__ src, int B, int S, int H, int D, int merge,
+                             uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int64_t total4 = int64_t(B) * S * H * D / 4;
+  for (int64_t i4 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
+       i4 += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t e = i4 * 4;
+    // e indexes the destination
+    int64_t s_idx;
+    if (merge) {  // dest (t, h, d)
+      const int d = int(e % D);
+      const int h = int((e / D) % H);
+      const int64_t t = e / (int64_t(D) * H);
+      const int s = int(t % S), b = int(t / S);
+      s_idx = ((int64_t(b) * H + h) * S + s) * D + d;
+    } else {  // dest (b, h, s, d) from (t, h, d)
+      const int d = int(e % D);
+      const int s = int((e / D) % S);
+      const int h = int((e / (int64_t(D) * S)) % H);
+      const int b = int(e / (int64_t(D) * S * H));
+      s_idx = ((int64_t(b) * S + s) * H + h) * D + d;
+    }
+    put_split4(hi, lo, e, *reinterpret_cast<const float4*>(src + s_idx));
+  }
+}
+
+__device__ __forceinline__ float silu_of(float g) { return g / (1.f + expf(-g)); }
+
+// act = silu(g) * u, gu = [g | u] per row -> hi/lo (T, I).
+__global__ void swiglu_split_kernel(const float* __restrict__ gu, int64_t T, int I,
+                                    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int64_t total4 = T * I / 4;
+  for (int64_t i4 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
+       i4 += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t e = i4 * 4;
+    const int64_t t = e / I;
+    const int c = int(e % I);
+    const float4 g = *reinterpret_cast<const float4*>(gu + t * 2 * I + c);
+    const float4 u = *reinterpret_cast<const float4*>(gu + t * 2 * I + I + c);
+    float4 a;
+    a.x = silu_of(g.x) * u.x;
+    a.y = silu_of(g.y) * u.y;
+    a.z = silu_of(g.z) * u.z;
+    a.w = silu_of(g.w) * u.w;
+    put_split4(hi, lo, e, a);
+  }
+}
+
+// dgu = [dact * u * silu'(g) | dact * silu(g)] -> hi/lo (T, 2I).
+__global__ void swiglu_bwd_split_kernel(const float* __restrict__ dact,
+                                        const float* __restrict__ gu, int64_t T, int I,
+                                        uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int64_t total4 = T * I / 4;
+  for (int64_t i4 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
+       i4 += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t e = i4 * 4;
+    const int64_t t = e / I;
+    const int c = int(e % I);
+    const float4 d = *reinterpret_cast<const float4*>(dact + e);
+    const float4 g = *reinterpret_cast<const float4*>(gu + t * 2 * I + c);
+    const float4 u = *reinterpret_cast<const float4*>(gu + t * 2 * I + I + c);
+    const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {u.x, u.y, u.z, u.w};
+    const float ds[4] = {d.x, d.y, d.z, d.w};
+    float dg[4], du[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float sg = 1.f / (1.f + expf(-gs[j]));
+      const float sl = gs[j] * sg;
+      dg[j] = ds[j] * us[j] * (sg * (1.f + gs[j] * (1.f - sg)));
+      du[j] = ds[j] * sl;
+    }
+    put_split4(hi, lo, t * 2 * I + c, make_float4(dg[0], dg[1], dg[2], dg[3]));
+    put_split4(hi, lo, t * 2 * I + I + c, make_float4(du[0], du[1], du[2], du[3]));
+  }
+}
+
+constexpr int kSoftThreads = 256;
+constexpr int kSoftVec = 8;  // rows up to 256*8 = 2048... extended by looping
+
+// Causal softmax of scale * scores, row r at position r % S: P in place + hi/lo.
+__global__ void __launch_bounds__(kSoftThreads) softmax_causal_kernel(
+    float* __restrict__ scores, int S, float scale, uint16_t* __restrict__ hi,
+    uint16_t* __restrict__ lo) {
+  __shared__ float sh[kSoftThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int pos = int(row % S);
+  float* r = scores + row * S;
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c <= pos; c += kSoftThreads) m = fmaxf(m, __fmul_rn(r[c], scale));
+  m = block_max<kSoftThreads>(m, sh);
+  float sum = 0.f;
+  for (int c = threadIdx.x; c <= pos; c += kSoftThreads) sum += expf(__fmul_rn(r[c], scale) - m);
+  sum = block_sum<kSoftThreads>(sum, sh);
+  const float inv = 1.f / sum;
+  for (int c = threadIdx.x; c < S; c += kSoftThreads) {
+    const float p = c <= pos ? expf(__fmul_rn(r[c], scale) - m) * inv : 0.f;
+    r[c] = p;
+    put_split(hi, lo, row * S + c, p);
+  }
+}
+
+// dS = scale * P * (dP - sum(dP * P)) -> hi/lo (rows of length S).
+__global__ void __launch_bounds__(kSoftThreads) softmax_bwd_kernel(
+    const float* __restrict__ dp, const float* __restrict__ p, int S, float scale,
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  __shared__ float sh[kSoftThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int pos = int(row % S);
+  const float* dr = dp + row * S;
+  const float* pr = p + row * S;
+  float dot = 0.f;
+  for (int c = threadIdx.x; c <= pos; c += kSoftThreads) dot += dr[c] * pr[c];
+  dot = block_sum<kSoftThreads>(dot, sh);
+  for (int c = threadIdx.x; c < S; c += kSoftThreads) {
+    const float v = c <= pos ? scale * pr[c] * (dr[c] - dot) : 0.f;
+    put_split(hi, lo, row * S + c, v);
+  }
+}
+
+int grid_elems(int64_t n, int threads = 256) { return grid_for(n, threads, 8); }
+
+}  // namespace
+}  // namespace mr
+
+using namespace mr;
+
+extern "C" int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows, int h, float eps,
+                                uint16_t* hi, uint16_t* lo, float* rstd, void* stream) {
+  if (!x || !w || !hi || !lo || !rstd || rows <= 0 || h <= 0 || h % 4 || h > 4 * kMaxVec * kRowThreads)
+    return MR_ERR_ARGUMENT;
+  if (!aligned16(x)) return MR_ERR_ALIGNMENT;
+  rmsnorm_split_kernel<<<unsigned(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, w, h, eps, hi, lo, rstd);
+  return launch_status();
+}
+
+extern "C" int mr_rmsnorm_bwd_split(const float* dy, const float* x, const uint16_t* w,
+                                    const float* rstd, const float* resid, int64_t rows, int h,
+                                    uint16_t* hi, uint16_t* lo, void* stream) {
+  if (!dy || !x || !w || !rstd || !resid || !hi || !lo || rows <= 0 || h <= 0 || h % 4 ||
+      h > 4 * kMaxVec * kRowThreads)
+    return MR_ERR_ARGUMENT;
+  if (!aligned16(dy) || !aligned16(x) || !aligned16(resid)) return MR_ERR_ALIGNMENT;
+  rmsnorm_bwd_split_kernel<<<unsigned(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      dy, x, w, rstd, resid, h, hi, lo);
+  return launch_status();
+}
+
+extern "C" int mr_rope_split(const float* qkv, const float* cosv, const float* sinv, int b, int s,
+                             int hq, int hkv, int d, uint16_t* q_hi, uint16_t* q_lo,
+                             uint16_t* k_hi, uint16_t* k_lo, uint16_t* v_hi, uint16_t* v_lo,
+                             void* stream) {
+  if (!qkv || !cosv || !sinv || b <= 0 || s <= 0 || hq <= 0 || hkv <= 0 || d <= 0 || d % 2)
+    return MR_ERR_ARGUMENT;
+  const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
+  rope_split_kernel<<<grid_elems(total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      qkv, cosv, sinv, b, s, hq, hkv, d, q_hi, q_lo, k_hi, k_lo, v_hi, v_lo);
+  return launch_status();
+}
+
+extern "C" int mr_rope_bwd_split(const float* dq, const float* dk, const float* dv,
+                                 const float* cosv, const float* sinv, int b, int s, int hq,
+                                 int hkv, int d, uint16_t* hi, uint16_t* lo, void* stream) {
+  if (!dq || !dk || !dv || !cosv || !sinv || b <= 0 || s <= 0 || d % 2) return MR_ERR_ARGUMENT;
+  const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
+  rope_bwd_split_kernel<<<grid_elems(total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      dq, dk, dv, cosv, sinv, b, s, hq, hkv, d, hi, lo);
+  return launch_status();
+}
+
+extern "C" int mr_heads_split(const float* src, int b, int s, int h, int d, int merge,
+                              uint16_t* hi, uint16_t* lo, void* stream) {
+  if (!src || !hi || !lo || b <= 0 || s <= 0 || h <= 0 || d % 4) return MR_ERR_ARGUMENT;
+  if (!aligned16(src)) return MR_ERR_ALIGNMENT;
+  const int64_t total4 = int64_t(b) * s * h * d / 4;
+  heads_kernel<<<grid_elems(total4), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, b, s, h, d,
+                                                                                  merge, hi, lo);
+  return launch_status();
+}
+
+extern "C" int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo,
+                               void* stream) {
+  if (!gu || !hi || !lo || t <= 0 || i <= 0 || i % 4) return MR_ERR_ARGUMENT;
+  if (!aligned16(gu)) return MR_ERR_ALIGNMENT;
+  swiglu_split_kernel<<<grid_elems(t * i / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      gu, t, i, hi, lo);
+  return launch_status();
+}
+
+extern "C" int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t, int i,
+                                   uint16_t* hi, uint16_t* lo, void* stream) {
+  if (!dact || !gu || !hi || !lo || t <= 0 || i <= 0 || i % 4) return MR_ERR_ARGUMENT;
+  if (!aligned16(dact) || !aligned16(gu)) return MR_ERR_ALIGNMENT;
+  swiglu_bwd_split_kernel<<<grid_elems(t * i / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      dact, gu, t, i, hi, lo);
+  return launch_status();
+}
+
+extern "C" int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale,
+                                       uint16_t* hi, uint16_t* lo, void* stream) {
+  if (!scores || !hi || !lo || rows <= 0 || s <= 0 || rows % s) return MR_ERR_ARGUMENT;
+  softmax_causal_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      scores, s, scale, hi, lo);
+  return launch_status();
+}
+
+extern "C" int mr_softmax_bwd_split(const float* dp, const float* p, int64_t rows, int s,
+                                    float scale, uint16_t* hi, uint16_t* lo, void* stream) {
+  if (!dp || !p || !hi || !lo || rows <= 0 || s <= 0 || rows % s) return MR_ERR_ARGUMENT;
+  softmax_bwd_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      dp, p, s, scale, hi, lo);
+  return launch_status();
+}

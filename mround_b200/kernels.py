@@ -257,3 +257,108 @@ def gemm_batched(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, batch: in
     if timing:
         end.record()
         GEMM_EVENTS.append((start, end, 2.0 * m * n * k * batch, precision))
+
+
+# ---------------------------------------------------------------- block ops
+def _pair(shape, device):
+    return (torch.empty(shape, dtype=torch.bfloat16, device=device),
+            torch.empty(shape, dtype=torch.bfloat16, device=device))
+
+
+def rmsnorm_split(x, w, eps: float):
+    """x (T, h) float32, w (h,) bf16 -> (hi, lo, rstd)."""
+    t, h = x.shape
+    hi, lo = _pair((t, h), x.device)
+    rstd = torch.empty(t, dtype=torch.float32, device=x.device)
+    st = lib().mr_rmsnorm_split(_ptr(x, torch.float32, "x"), _ptr(w, torch.bfloat16, "w", h), t, h,
+                                eps, hi.data_ptr(), lo.data_ptr(), rstd.data_ptr(), _stream())
+    check(st, "mr_rmsnorm_split")
+    _count()
+    return hi, lo, rstd
+
+
+def rmsnorm_bwd_split(dy, x, w, rstd, resid):
+    t, h = x.shape
+    hi, lo = _pair((t, h), x.device)
+    st = lib().mr_rmsnorm_bwd_split(_ptr(dy, torch.float32, "dy", t * h), _ptr(x, torch.float32, "x"),
+                                    _ptr(w, torch.bfloat16, "w", h), _ptr(rstd, torch.float32, "rstd", t),
+                                    _ptr(resid, torch.float32, "resid", t * h), t, h, hi.data_ptr(),
+                                    lo.data_ptr(), _stream())
+    check(st, "mr_rmsnorm_bwd_split")
+    _count()
+    return hi, lo
+
+
+def rope_split(qkv, cos, sin, b: int, s: int, hq: int, hkv: int, d: int):
+    dev = qkv.device
+    q = _pair((b, hq, s, d), dev)
+    k = _pair((b, hkv, s, d), dev)
+    v = _pair((b, hkv, s, d), dev)
+    st = lib().mr_rope_split(_ptr(qkv, torch.float32, "qkv", b * s * (hq + 2 * hkv) * d),
+                             _ptr(cos, torch.float32, "cos", s * d // 2),
+                             _ptr(sin, torch.float32, "sin", s * d // 2), b, s, hq, hkv, d,
+                             q[0].data_ptr(), q[1].data_ptr(), k[0].data_ptr(), k[1].data_ptr(),
+                             v[0].data_ptr(), v[1].data_ptr(), _stream())
+    check(st, "mr_rope_split")
+    _count()
+    return q, k, v
+
+
+def rope_bwd_split(dq, dk, dv, cos, sin, b: int, s: int, hq: int, hkv: int, d: int):
+    hi, lo = _pair((b * s, (hq + 2 * hkv) * d), dq.device)
+    st = lib().mr_rope_bwd_split(_ptr(dq, torch.float32, "dq"), _ptr(dk, torch.float32, "dk"),
+                                 _ptr(dv, torch.float32, "dv"), _ptr(cos, torch.float32, "cos"),
+                                 _ptr(sin, torch.float32, "sin"), b, s, hq, hkv, d, hi.data_ptr(),
+                                 lo.data_ptr(), _stream())
+    check(st, "mr_rope_bwd_split")
+    _count()
+    return hi, lo
+
+
+def heads_split(src, b: int, s: int, h: int, d: int, *, merge: bool):
+    shape = (b * s, h * d) if merge else (b, h, s, d)
+    hi, lo = _pair(shape, src.device)
+    st = lib().mr_heads_split(_ptr(src, torch.float32, "src", b * s * h * d), b, s, h, d, int(merge),
+                              hi.data_ptr(), lo.data_ptr(), _stream())
+    check(st, "mr_heads_split")
+    _count()
+    return hi, lo
+
+
+def swiglu_split(gu, t: int, i: int):
+    hi, lo = _pair((t, i), gu.device)
+    st = lib().mr_swiglu_split(_ptr(gu, torch.float32, "gu", t * 2 * i), t, i, hi.data_ptr(),
+                               lo.data_ptr(), _stream())
+    check(st, "mr_swiglu_split")
+    _count()
+    return hi, lo
+
+
+def swiglu_bwd_split(dact, gu, t: int, i: int):
+    hi, lo = _pair((t, 2 * i), gu.device)
+    st = lib().mr_swiglu_bwd_split(_ptr(dact, torch.float32, "dact", t * i),
+                                   _ptr(gu, torch.float32, "gu", t * 2 * i), t, i, hi.data_ptr(),
+                                   lo.data_ptr(), _stream())
+    check(st, "mr_swiglu_bwd_split")
+    _count()
+    return hi, lo
+
+
+def softmax_causal_split(scores, rows: int, s: int, scale: float):
+    """Causal softmax in place (row r at position r % s); returns the hi/lo parts."""
+    hi, lo = _pair(scores.shape, scores.device)
+    st = lib().mr_softmax_causal_split(_ptr(scores, torch.float32, "scores", rows * s), rows, s,
+                                       float(scale), hi.data_ptr(), lo.data_ptr(), _stream())
+    check(st, "mr_softmax_causal_split")
+    _count()
+    return hi, lo
+
+
+def softmax_bwd_split(dp, p, rows: int, s: int, scale: float):
+    hi, lo = _pair(dp.shape, dp.device)
+    st = lib().mr_softmax_bwd_split(_ptr(dp, torch.float32, "dp", rows * s),
+                                    _ptr(p, torch.float32, "p", rows * s), rows, s, float(scale),
+                                    hi.data_ptr(), lo.data_ptr(), _stream())
+    check(st, "mr_softmax_bwd_split")
+    _count()
+    return hi, lo

@@ -230,3 +230,144 @@ class DeviceBlock:
         gu = lin("gate_up", h2)
         g, u = gu.split([a.intermediate, a.intermediate], dim=-1)
         return h + lin("down", F.silu(g) * u)
+
+
+# ---------------------------------------------------------------------------
+# Explicit fused path: the same block, forward and backward written out.
+#
+# Every element-wise step is one kernel that writes the next GEMM operand as
+# bf16 hi/lo (csrc/blockops.cu); the residual additions are folded into the
+# GEMMs (C is preloaded with the residual and accumulated into); the backward
+# never forms the block-input gradient, which the tuning step does not need.
+# Saved for the backward: the operand splits, P (float32 and hi/lo), h, gu,
+# and the second norm's rstd.
+
+def _mm(a, b, c, *, m, n, k, a_kmajor, b_kmajor, lda, ldb, prec, bias=None, accumulate=False):
+    kernels.gemm(a[0], a[1] if prec >= 2 else None, b[0], b[1] if prec == 3 else None, c, m=m, n=n,
+                 k=k, a_kmajor=a_kmajor, b_kmajor=b_kmajor, lda=lda, ldb=ldb, ldc=n,
+                 precision=prec, bias=bias, accumulate=accumulate)
+
+
+def _bmm(a, b, c, *, m, n, k, batch, a_kmajor, b_kmajor, lda, ldb, sa, sb, sc):
+    kernels.gemm_batched(a[0], a[1], b[0], b[1], c, m=m, n=n, k=k, batch=batch, a_kmajor=a_kmajor,
+                         b_kmajor=b_kmajor, lda=lda, ldb=ldb, ldc=n, stride_a=sa, stride_b=sb,
+                         stride_c=sc, precision=3)
+
+
+def _wprec(layer: FusedLinear, want: int) -> int:
+    return want if layer.wq_lo is not None else min(want, 2)
+
+
+def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bool):
+    a = self.arch
+    b, s, h = x.shape
+    t = b * s
+    hq, hkv, d, inter = a.heads, a.kv_heads, a.head_dim, a.intermediate
+    rep, nb = hq // hkv, b * hkv
+    scale = 1.0 / math.sqrt(d)
+    x2 = x.reshape(t, h)
+    L = self.layers
+    h1 = kernels.rmsnorm_split(x2, self.input_norm, a.rms_eps)
+    qkv_l = L["qkv"]
+    qkv = torch.empty((t, qkv_l.out_features), dtype=torch.float32, device=x.device)
+    p = _wprec(qkv_l, prec.forward)
+    _mm(h1, (qkv_l.wq_hi, qkv_l.wq_lo), qkv, m=t, n=qkv_l.out_features, k=h, a_kmajor=True,
+        b_kmajor=True, lda=h, ldb=h, prec=p, bias=qkv_l.bias)
+    cos, sin = self._tables(s)
+    q, k, v = kernels.rope_split(qkv, cos, sin, b, s, hq, hkv, d)
+    del qkv
+    scores = torch.empty((nb, rep * s, s), dtype=torch.float32, device=x.device)
+    _bmm(q, k, scores, m=rep * s, n=s, k=d, batch=nb, a_kmajor=True, b_kmajor=True, lda=d, ldb=d,
+         sa=rep * s * d, sb=s * d, sc=rep * s * s)
+    probs = kernels.softmax_causal_split(scores, nb * rep * s, s, scale)  # scores now holds P
+    o = torch.empty((b, hq, s, d), dtype=torch.float32, device=x.device)
+    _bmm(probs, v, o, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,
+         sa=rep * s * s, sb=s * d, sc=rep * s * d)
+    att = kernels.heads_split(o, b, s, hq, d, merge=True)
+    del o
+    o_l = L["o"]
+    hres = x2.clone()
+    _mm(att, (o_l.wq_hi, o_l.wq_lo), hres, m=t, n=h, k=hq * d, a_kmajor=True, b_kmajor=True,
+        lda=hq * d, ldb=hq * d, prec=_wprec(o_l, prec.forward), accumulate=True)
+    h2_hi, h2_lo, rstd2 = kernels.rmsnorm_split(hres, self.post_norm, a.rms_eps)
+    gu_l = L["gate_up"]
+    gu = torch.empty((t, 2 * inter), dtype=torch.float32, device=x.device)
+    _mm((h2_hi, h2_lo), (gu_l.wq_hi, gu_l.wq_lo), gu, m=t, n=2 * inter, k=h, a_kmajor=True,
+        b_kmajor=True, lda=h, ldb=h, prec=_wprec(gu_l, prec.forward))
+    act = kernels.swiglu_split(gu, t, inter)
+    dn_l = L["down"]
+    out = hres.clone()
+    _mm(act, (dn_l.wq_hi, dn_l.wq_lo), out, m=t, n=h, k=inter, a_kmajor=True, b_kmajor=True,
+        lda=inter, ldb=inter, prec=_wprec(dn_l, prec.forward), accumulate=True)
+    saved = None
+    if save:
+        saved = dict(shape=(b, s, h), h1=(h1[0], h1[1]), q=q, k=k, v=v, p=scores, probs=probs,
+                     att=att, hres=hres, rstd2=rstd2, h2=(h2_hi, h2_lo), gu=gu, act=act)
+    return out.view(b, s, h), saved
+
+
+def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Precision) -> None:
+    """Weight gradients of every tunable fused linear into ``layer.grad``."""
+    a = self.arch
+    b, s, h = saved["shape"]
+    t = b * s
+    hq, hkv, d, inter = a.heads, a.kv_heads, a.head_dim, a.intermediate
+    rep, nb = hq // hkv, b * hkv
+    scale = 1.0 / math.sqrt(d)
+    L = self.layers
+    dout2 = dout.reshape(t, h)
+    g_out = kernels.split_bf16(dout2)
+
+    def weight_grad(layer, dy, x_in, n_out, n_in):
+        if layer.grad is None:
+            return
+        kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, m=n_out, n=n_in, k=t,
+                     a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in,
+                     precision=prec.grad_weight, accumulate=layer.accumulate_grad)
+        for hook in layer.grad_ready:
+            hook(layer)
+
+    def input_grad(layer, dy, n_out, n_in):
+        out = torch.empty((t, n_in), dtype=torch.float32, device=dout.device)
+        _mm(dy, (layer.wq_hi, layer.wq_lo), out, m=t, n=n_in, k=n_out, a_kmajor=True,
+            b_kmajor=False, lda=n_out, ldb=n_in, prec=_wprec(layer, prec.grad_input))
+        return out
+
+    dn_l, gu_l, o_l, qkv_l = L["down"], L["gate_up"], L["o"], L["qkv"]
+    weight_grad(dn_l, g_out, saved["act"], h, inter)
+    dact = input_grad(dn_l, g_out, h, inter)
+    g_gu = kernels.swiglu_bwd_split(dact, saved["gu"], t, inter)
+    del dact
+    weight_grad(gu_l, g_gu, saved["h2"], 2 * inter, h)
+    dh2 = input_grad(gu_l, g_gu, 2 * inter, h)
+    del g_gu
+    g_h = kernels.rmsnorm_bwd_split(dh2, saved["hres"], self.post_norm, saved["rstd2"], dout2)
+    del dh2
+    weight_grad(o_l, g_h, saved["att"], h, hq * d)
+    datt = input_grad(o_l, g_h, h, hq * d)
+    g_o = kernels.heads_split(datt, b, s, hq, d, merge=False)
+    del datt
+    q, k, v, p, probs = saved["q"], saved["k"], saved["v"], saved["p"], saved["probs"]
+    dp = torch.empty((nb, rep * s, s), dtype=torch.float32, device=dout.device)
+    _bmm(g_o, v, dp, m=rep * s, n=s, k=d, batch=nb, a_kmajor=True, b_kmajor=True, lda=d, ldb=d,
+         sa=rep * s * d, sb=s * d, sc=rep * s * s)
+    g_s = kernels.softmax_bwd_split(dp, p, nb * rep * s, s, scale)
+    del dp
+    dq = torch.empty((b, hq, s, d), dtype=torch.float32, device=dout.device)
+    _bmm(g_s, k, dq, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,
+         sa=rep * s * s, sb=s * d, sc=rep * s * d)
+    dk = torch.empty((b, hkv, s, d), dtype=torch.float32, device=dout.device)
+    _bmm(g_s, q, dk, m=s, n=d, k=rep * s, batch=nb, a_kmajor=False, b_kmajor=False, lda=s, ldb=d,
+         sa=rep * s * s, sb=rep * s * d, sc=s * d)
+    dv = torch.empty((b, hkv, s, d), dtype=torch.float32, device=dout.device)
+    _bmm(probs, g_o, dv, m=s, n=d, k=rep * s, batch=nb, a_kmajor=False, b_kmajor=False, lda=s,
+         ldb=d, sa=rep * s * s, sb=rep * s * d, sc=s * d)
+    del g_s
+    cos, sin = self._tables(s)
+    g_qkv = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)
+    del dq, dk, dv
+    weight_grad(qkv_l, g_qkv, saved["h1"], qkv_l.out_features, h)
+
+
+DeviceBlock.forward_fused = _fused_forward
+DeviceBlock.backward_fused = _fused_backward

@@ -245,10 +245,11 @@ class QuantizationRunner:
                 with torch.no_grad():
                     if quantized_stream is not None:
                         for i, x in enumerate(reference_stream):
-                            reference_stream[i] = block.forward(x, self.precision)
+                            reference_stream[i] = block.forward_fused(x, self.precision, False)[0]
                         targets = reference_stream
                     else:
-                        targets = [block.forward(x, self.precision) for x in reference_stream]
+                        targets = [block.forward_fused(x, self.precision, False)[0]
+                                   for x in reference_stream]
             inputs = quantized_stream if quantized_stream is not None else reference_stream
             result, layers = self.quantize_block(block, name, inputs, targets,
                                                  scheme_by_layer=scheme_by_layer, meter=meter)
@@ -259,7 +260,7 @@ class QuantizationRunner:
                 if quantized_stream is not None:
                     with torch.no_grad():
                         for i, x in enumerate(quantized_stream):
-                            quantized_stream[i] = block.forward(x, self.precision)
+                            quantized_stream[i] = block.forward_fused(x, self.precision, False)[0]
             if quantized_stream is None:
                 reference_stream = targets
             del block

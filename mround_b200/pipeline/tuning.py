@@ -237,8 +237,8 @@ class BlockTuner:
     def output(self, x: torch.Tensor) -> torch.Tensor:
         with torch.no_grad():
             if self.pieces == 1:
-                return self.block.forward(x, self.precision)
-            parts = [self.block.forward(x[lo:hi], self.precision)
+                return self.block.forward_fused(x, self.precision, False)[0]
+            parts = [self.block.forward_fused(x[lo:hi], self.precision, False)[0]
                      for lo, hi in piece_bounds(x.shape[0], self.pieces)]
             return torch.cat(parts, 0)
 
@@ -259,10 +259,12 @@ class BlockTuner:
             self._last_piece = True
             for t in self.tunables:
                 t.layer.accumulate_grad = False
-            out = self.block.forward(x, self.precision, train=True)
+            out, saved = self.block.forward_fused(x, self.precision, True)
             grad = torch.empty_like(out)
             loss = self.loss(out, target, grad=grad)
-            out.backward(grad)
+            del out
+            self.block.backward_fused(saved, grad, self.precision)
+            del saved
         else:
             # whole-batch threshold first, then each piece against it
             self._n_global = x.numel() * self.dist.world
@@ -274,10 +276,12 @@ class BlockTuner:
                 self._last_piece = i == len(bounds) - 1
                 for t in self.tunables:
                     t.layer.accumulate_grad = i > 0
-                out = self.block.forward(x[lo:hi], self.precision, train=True)
+                out, saved = self.block.forward_fused(x[lo:hi], self.precision, True)
                 grad = torch.empty_like(out)
                 loss += self.loss(out, target[lo:hi], grad=grad, threshold_ready=True)
-                out.backward(grad)
+                del out
+                self.block.backward_fused(saved, grad, self.precision)
+                del saved
         for t in self.tunables:
             self._wait(t.layer)
             t.update(step, iters)
@@ -288,10 +292,10 @@ class BlockTuner:
         self._last_piece = True
         for t in self.tunables:
             t.layer.accumulate_grad = False
-        out = self.block.forward(x, self.precision, train=True)
+        out, saved = self.block.forward_fused(x, self.precision, True)
         grad = torch.empty_like(out)
         loss = self.loss(out, target, grad=grad)
-        out.backward(grad)
+        self.block.backward_fused(saved, grad, self.precision)
         grads = {}
         for t in self.tunables:
             self._wait(t.layer)

@@ -156,3 +156,33 @@ def test_advance_uses_bf16_reconstruction(env):
     with torch.no_grad():
         got = block.forward(x.cuda(), Precision()).cpu()
     assert relative_error(got.numpy(), oracle.forward(x).numpy()) < 2e-5
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen2", "tiny-llama"])
+def test_fused_path_matches_autograd_path(env, name):
+    """The explicit fused forward/backward equals the autograd composition of
+    the same kernels: outputs and every fused weight gradient."""
+    A, SM = env
+    from mround_b200.pipeline.block import DeviceBlock, Precision
+    from mround_b200.pipeline.dist import DistContext
+    from mround_b200.pipeline.tuning import BlockTuner
+    from mround_b200.schemes import QuantScheme
+
+    arch = A.get_arch(name)
+    params = SM(arch, seed=8).block(0)
+    scheme = QuantScheme(bits=3, group_size=32, symmetry="asym")
+    block = DeviceBlock(arch, params)
+    tuner = BlockTuner(block, {p: scheme for p in LINEARS}, {p: 0.01 for p in LINEARS},
+                       suppress=False, eps=1e-8, precision=Precision(), dist=DistContext())
+    x = make_inputs(arch, 1, 2, 64, seed=5)[0].cuda()
+    g = torch.randn(x.shape, device="cuda") * 1e-3
+    out_a = block.forward(x, Precision(), train=True)
+    out_a.backward(g)
+    grads_a = {n: l.grad.clone() for n, l in block.layers.items()}
+    out_f, saved = block.forward_fused(x, Precision(), True)
+    block.backward_fused(saved, g, Precision())
+    torch.cuda.synchronize()
+    assert relative_error(out_f.detach().cpu().numpy(), out_a.detach().cpu().numpy()) < 1e-5
+    for n, l in block.layers.items():
+        assert relative_error(l.grad.cpu().numpy(), grads_a[n].cpu().numpy()) < 1e-4, n
+    del tuner
