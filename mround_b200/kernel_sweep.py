@@ -1,0 +1,130 @@
+"""Kernel sweep: HBM throughput of K1, K2, K5, K6.
+
+Shapes 896x896, 4864x896, 3584x3584, 18944x3584 (bf16 weights N(0, 0.02)
+with 0.1 % outliers x20; V ~ U(-0.5, 0.5); alpha, beta ~ U(0.5, 1.0); upstream
+gradient N(0, 1e-3)), bits {2, 3, 4, 8}, groups {32, 64, 128}.  Each launch is
+timed alone with CUDA events on the launching stream, after writing a buffer
+larger than L2 (so every launch starts cold), median of ``reps``.
+
+Algorithmic bytes per launch (per weight, plus per group):
+  K1 fq_forward        read W 2 + V 4, write Wq hi+lo 4            = 10 B (+ 8 B/group)
+  K2 ste_signsgd       read dWq 4 + W 2 + V 4, write V 4 + Wq 4    = 18 B (+16 B/group)
+  K5 pack_mlx          read W 2 + V 4, write bits/8                 (+12 B/group)
+  K6 deltaloss (3 w.)  read g 4 + W 2                               = 6 B
+
+Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick]
+Prints one JSON line per case, then a summary line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+
+import torch
+
+from mround_b200 import kernels
+
+SHAPES = [(896, 896), (4864, 896), (3584, 3584), (18944, 3584)]
+BITS = (2, 3, 4, 8)
+GROUPS = (32, 64, 128)
+
+
+def _peak() -> tuple[float, str]:
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    try:
+        with open(os.path.join(here, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "of measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "of fallback"
+
+
+def _case(rows, cols, group, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    w = torch.randn(rows, cols, device=device, generator=g) * 0.02
+    hot = torch.rand(rows, cols, device=device, generator=g) < 0.001
+    w = torch.where(hot, w * 20.0, w).to(torch.bfloat16)
+    v = torch.rand(rows, cols, device=device, generator=g) - 0.5
+    ng = cols // group
+    a = 0.5 + 0.5 * torch.rand(rows, ng, device=device, generator=g)
+    b = 0.5 + 0.5 * torch.rand(rows, ng, device=device, generator=g)
+    gq = torch.randn(rows, cols, device=device, generator=g) * 1e-3
+    return w, v, a, b, gq
+
+
+def _time(fn, flush, reps):
+    out = []
+    for _ in range(reps):
+        flush.add_(1.0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        out.append(s.elapsed_time(e))
+    return statistics.median(out)
+
+
+def run(reps: int = 5, quick: bool = False) -> list[dict]:
+    device = torch.device("cuda")
+    peak, src = _peak()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MB > L2
+    shapes = SHAPES[-1:] if quick else SHAPES
+    results = []
+    for rows, cols in shapes:
+        for group in GROUPS:
+            for bits in BITS:
+                w, v, a, b, gq = _case(rows, cols, group, rows + bits + group, device)
+                n = rows * cols
+                ng = n // group
+                hi, lo = torch.empty_like(w), torch.empty_like(w)
+                out = torch.zeros(3, dtype=torch.float64, device=device)
+                cases = {
+                    "K1_fq_forward": (lambda: kernels.fq_forward(w, v, a, b, bits=bits, group=group,
+                                                                 eps=1e-8, wq_hi=hi, wq_lo=lo),
+                                      10 * n + 8 * ng),
+                    "K2_ste_signsgd": (lambda: kernels.ste_signsgd(gq, w, v, a, b, bits=bits, group=group,
+                                                                   eps=1e-8, lr=1e-9, lo=0.1, hi=1.0,
+                                                                   wq_hi=hi, wq_lo=lo),
+                                       18 * n + 16 * ng),
+                    "K5_pack_mlx": (lambda: kernels.pack_mlx(w, v, a, b, bits=bits, group=group, eps=1e-8),
+                                    6 * n + n * bits // 8 + 12 * ng),
+                    "K6_deltaloss": (lambda: kernels.deltaloss(gq, w, bits=(2, 3, 4), group=group,
+                                                               eps=1e-8, out=out),
+                                     6 * n),
+                }
+                for name, (fn, nbytes) in cases.items():
+                    if name == "K6_deltaloss" and bits != 2:
+                        continue  # one pass scores every width; timed once per shape/group
+                    fn()
+                    torch.cuda.synchronize()
+                    ms = _time(fn, flush, reps)
+                    gbs = nbytes / (ms * 1e-3) / 1e9
+                    rec = {"kernel": name, "rows": rows, "cols": cols, "bits": bits, "group": group,
+                           "ms": ms, "bytes": nbytes, "gbs": gbs, "frac": gbs / peak,
+                           "peak_gbs": peak, "peak_source": src}
+                    results.append(rec)
+                    print(json.dumps(rec), flush=True)
+    big = [r for r in results if r["rows"] * r["cols"] >= 3584 * 3584]
+    summary = {}
+    for name in sorted({r["kernel"] for r in results}):
+        sel = [r["frac"] for r in big if r["kernel"] == name]
+        if sel:
+            summary[name] = {"median_frac_large": statistics.median(sel), "min_frac_large": min(sel),
+                             "max_frac_large": max(sel)}
+    print(json.dumps({"summary": summary, "peak_gbs": peak, "peak_source": src}), flush=True)
+    return results
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--quick", action="store_true")
+    args = ap.parse_args()
+    run(args.reps, args.quick)
+
+
+if __name__ == "__main__":
+    main()
