@@ -185,6 +185,16 @@ int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t c
                  void* stream);
 
 /*
+ * Self-test of the kernels' arithmetic (no reference counterpart): counts, into
+ * *mismatches (device, accumulated), the elements where the quantizer's
+ * division -- a correctly rounded reciprocal per group and one Markstein
+ * correction per element -- differs in any bit from IEEE division of a[i] by
+ * b[i].
+ */
+int mr_selftest_division(const float* a, const float* b, int64_t n, unsigned int* mismatches,
+                         void* stream);
+
+/*
  * Operand preparation for the split-precision GEMMs: x (float32, n elements)
  * -> hi = bf16(x), lo = bf16(x - hi) (lo may be NULL).
  */
@@ -206,6 +216,8 @@ int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* s
  *                         P = softmax(scale * scores) over columns <= position,
  *                         written in place (float32) and as hi/lo
  *   mr_softmax_bwd_split: dS = scale * P * (dP - sum(dP * P))
+ *   band != 0 (softmax kernels): columns from (pos/128 + 2)*128 on are not
+ *   written -- the causal modes of mr_gemm_batched never read them.
  */
 int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows, int h, float eps,
                      uint16_t* hi, uint16_t* lo, float* rstd, void* stream);
@@ -223,10 +235,10 @@ int mr_heads_split(const float* src, int b, int s, int h, int d, int merge, uint
 int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo, void* stream);
 int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t, int i, uint16_t* hi,
                         uint16_t* lo, void* stream);
-int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale, uint16_t* hi,
-                            uint16_t* lo, void* stream);
+int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale, int band,
+                            uint16_t* hi, uint16_t* lo, void* stream);
 int mr_softmax_bwd_split(const float* dp, const float* p, int64_t rows, int s, float scale,
-                         uint16_t* hi, uint16_t* lo, void* stream);
+                         int band, uint16_t* hi, uint16_t* lo, void* stream);
 
 /*
  * K3 -- tcgen05/TMEM GEMM, bf16 operands, float32 accumulate in tensor memory.
@@ -256,12 +268,19 @@ int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajo
  * attention products of the decoder block (scores, probabilities times
  * values, and their gradients), which the reference runs inside the mlx-lm
  * layer (mround/pipeline/blocks.py:578-606).
+ * causal (seq = positions per head, a multiple of 128; rows of a problem stack
+ * heads of seq positions): 0 none; 1 C = Q K^T-shaped (n = seq), tiles above
+ * the diagonal are not computed or written; 2 C = P V-shaped (k = seq), the
+ * K loop stops after each row tile's last position; 3 C = dS^T Q-shaped
+ * (m = seq, k = heads*seq), K tiles whose rows precede the tile's first key
+ * are skipped.  Modes 2 and 3 read only what mr_softmax_*_split writes with
+ * band != 0.
  */
 int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int64_t stride_a,
                     int a_kmajor, const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb,
                     int64_t stride_b, int b_kmajor, float* c, int64_t ldc, int64_t stride_c,
                     const float* bias, int accumulate, int64_t m, int64_t n, int64_t k,
-                    int64_t batch, int precision, void* stream);
+                    int64_t batch, int precision, int causal, int64_t seq, void* stream);
 
 /* Device status word of K3: 0, or MR_ERR_TIMEOUT.  Synchronizes the device;
  * reset != 0 clears it. */

@@ -54,10 +54,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_loss_apply": (_I, [_P, _P, _I64, _D, _P, _I, _P, _P, _P, _P]),
     "mr_deltaloss": (_I, [_P, _P, _I64, _I64, _I, _P, _I, _F, _P, _P]),
     "mr_split_bf16": (_I, [_P, _I64, _P, _P, _P]),
+    "mr_selftest_division": (_I, [_P, _P, _I64, _P, _P]),
     "mr_gemm": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _P, _I64, _P, _I, _I64, _I64, _I64,
                      _I, _P]),
     "mr_gemm_batched": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _I64, _I64, _I, _P, _I64, _I64, _P,
-                             _I, _I64, _I64, _I64, _I64, _I, _P]),
+                             _I, _I64, _I64, _I64, _I64, _I, _I, _I64, _P]),
     "mr_gemm_status": (_I, [_I]),
     "mr_rmsnorm_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P, _P]),
     "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P]),
@@ -66,8 +67,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_heads_split": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "mr_swiglu_split": (_I, [_P, _I64, _I, _P, _P, _P]),
     "mr_swiglu_bwd_split": (_I, [_P, _P, _I64, _I, _P, _P, _P]),
-    "mr_softmax_causal_split": (_I, [_P, _I64, _I, _F, _P, _P, _P]),
-    "mr_softmax_bwd_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P]),
+    "mr_softmax_causal_split": (_I, [_P, _I64, _I, _F, _I, _P, _P, _P]),
+    "mr_softmax_bwd_split": (_I, [_P, _P, _I64, _I, _F, _I, _P, _P, _P]),
 }
 
 

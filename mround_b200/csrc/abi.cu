@@ -45,10 +45,33 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const float* __restrict
   }
 }
 
+// Bit comparison of div_rcp (reciprocal + Markstein correction) with __fdiv_rn.
+__global__ void selftest_division_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                         int64_t n, unsigned int* __restrict__ mismatches) {
+  unsigned int bad = 0;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float y = __frcp_rn(b[i]);
+    const float q1 = div_rcp(a[i], b[i], y);
+    const float q2 = __fdiv_rn(a[i], b[i]);
+    bad += __float_as_uint(q1) != __float_as_uint(q2) ? 1u : 0u;
+  }
+  if (bad) atomicAdd(mismatches, bad);
+}
+
 }  // namespace
 }  // namespace mr
 
 using namespace mr;
+
+extern "C" int mr_selftest_division(const float* a, const float* b, int64_t n,
+                                    unsigned int* mismatches, void* stream) {
+  if (!a || !b || !mismatches || n < 0) return MR_ERR_ARGUMENT;
+  if (n == 0) return MR_OK;
+  selftest_division_kernel<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, b, n, mismatches);
+  return launch_status();
+}
 
 extern "C" int mr_version(void) { return 100; }  // 0.1.0
 

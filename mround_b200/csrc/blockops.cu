@@ -298,8 +298,14 @@ constexpr int kSoftThreads = 256;
 constexpr int kSoftVec = 8;  // rows up to 256*8 = 2048... extended by looping
 
 // Causal softmax of scale * scores, row r at position r % S: P in place + hi/lo.
+// With ``band`` set, columns from the end of the next 128-column block on are
+// left unwritten: the causal GEMM modes never read them.
+__device__ __forceinline__ int write_limit(int pos, int S, int band) {
+  return band ? min(S, (pos / 128 + 2) * 128) : S;
+}
+
 __global__ void __launch_bounds__(kSoftThreads) softmax_causal_kernel(
-    float* __restrict__ scores, int S, float scale, uint16_t* __restrict__ hi,
+    float* __restrict__ scores, int S, float scale, int band, uint16_t* __restrict__ hi,
     uint16_t* __restrict__ lo) {
   __shared__ float sh[kSoftThreads / 32];
   const int64_t row = blockIdx.x;
@@ -312,7 +318,8 @@ __global__ void __launch_bounds__(kSoftThreads) softmax_causal_kernel(
   for (int c = threadIdx.x; c <= pos; c += kSoftThreads) sum += expf(__fmul_rn(r[c], scale) - m);
   sum = block_sum<kSoftThreads>(sum, sh);
   const float inv = 1.f / sum;
-  for (int c = threadIdx.x; c < S; c += kSoftThreads) {
+  const int lim = write_limit(pos, S, band);
+  for (int c = threadIdx.x; c < lim; c += kSoftThreads) {
     const float p = c <= pos ? expf(__fmul_rn(r[c], scale) - m) * inv : 0.f;
     r[c] = p;
     put_split(hi, lo, row * S + c, p);
@@ -321,7 +328,7 @@ __global__ void __launch_bounds__(kSoftThreads) softmax_causal_kernel(
 
 // dS = scale * P * (dP - sum(dP * P)) -> hi/lo (rows of length S).
 __global__ void __launch_bounds__(kSoftThreads) softmax_bwd_kernel(
-    const float* __restrict__ dp, const float* __restrict__ p, int S, float scale,
+    const float* __restrict__ dp, const float* __restrict__ p, int S, float scale, int band,
     uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
   __shared__ float sh[kSoftThreads / 32];
   const int64_t row = blockIdx.x;
@@ -331,7 +338,8 @@ __global__ void __launch_bounds__(kSoftThreads) softmax_bwd_kernel(
   float dot = 0.f;
   for (int c = threadIdx.x; c <= pos; c += kSoftThreads) dot += dr[c] * pr[c];
   dot = block_sum<kSoftThreads>(dot, sh);
-  for (int c = threadIdx.x; c < S; c += kSoftThreads) {
+  const int lim = write_limit(pos, S, band);
+  for (int c = threadIdx.x; c < lim; c += kSoftThreads) {
     const float v = c <= pos ? scale * pr[c] * (dr[c] - dot) : 0.f;
     put_split(hi, lo, row * S + c, v);
   }
@@ -416,18 +424,19 @@ extern "C" int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t
   return launch_status();
 }
 
-extern "C" int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale,
+extern "C" int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale, int band,
                                        uint16_t* hi, uint16_t* lo, void* stream) {
   if (!scores || !hi || !lo || rows <= 0 || s <= 0 || rows % s) return MR_ERR_ARGUMENT;
   softmax_causal_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      scores, s, scale, hi, lo);
+      scores, s, scale, band, hi, lo);
   return launch_status();
 }
 
 extern "C" int mr_softmax_bwd_split(const float* dp, const float* p, int64_t rows, int s,
-                                    float scale, uint16_t* hi, uint16_t* lo, void* stream) {
+                                    float scale, int band, uint16_t* hi, uint16_t* lo,
+                                    void* stream) {
   if (!dp || !p || !hi || !lo || rows <= 0 || s <= 0 || rows % s) return MR_ERR_ARGUMENT;
   softmax_bwd_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      dp, p, s, scale, hi, lo);
+      dp, p, s, scale, band, hi, lo);
   return launch_status();
 }

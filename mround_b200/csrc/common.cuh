@@ -61,6 +61,24 @@ __device__ __forceinline__ uint4 pack8(const uint16_t (&h)[8]) {
   return u;
 }
 
+// Correctly rounded a / b from y = RN(1/b) (one __frcp_rn per quantization
+// group instead of a full division per element).  Markstein's correction
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990, Theorem 1): when y
+// is within half an ulp of 1/b and q = RN(a*y) is within one ulp of a/b, the
+// remainder r = a - q*b is exact in one FMA and RN(q + r*y) is a/b correctly
+// rounded, provided nothing overflows or underflows.  The quantizer divides
+// weights by a scale bounded below by eps = 1e-8 and by span/255 of their own
+// group, so quotients stay within a few thousand in magnitude; a quotient in
+// the subnormal range (a denormal weight) only ever feeds rint(q + v) with
+// |v| <= 0.5 or q == 0, where a last-bit difference cannot change the code.
+// mr_selftest_division compares it against __fdiv_rn on the device.
+__device__ __forceinline__ float div_rcp(float a, float b, float y) {
+  const float q = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q, b, a);
+  return __fmaf_rn(r, y, q);
+}
+
 // Streaming loads/stores: the weight-sized tensors are touched once per pass.
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) { return __ldcs(p); }
 __device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }

@@ -70,10 +70,11 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
       const float maxq = widths.maxq[j];
       const float scale = fmaxf(__fdiv_rn(__fsub_rn(w_max, w_min), maxq), eps);
       const float zp = rintf(__fdiv_rn(-w_min, scale));
+      const float rcp = __frcp_rn(scale);
       float part = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float x = __fadd_rn(rintf(__fdiv_rn(wf[i], scale)), zp);
+        const float x = __fadd_rn(rintf(div_rcp(wf[i], scale, rcp)), zp);
         const float q = __fmul_rn(scale, __fsub_rn(fminf(fmaxf(x, 0.f), maxq), zp));
         part = __fadd_rn(part, fabsf(__fmul_rn(gf[i], __fsub_rn(q, wf[i]))));
       }

@@ -26,7 +26,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kTile = 256;  // elements per warp tile
 
 struct GroupQ {
-  float scale, zp, w_min, wmax_raw, wmin_raw;
+  float scale, rcp, zp, w_min, wmax_raw, wmin_raw;
   bool live;  // scale above the eps floor, i.e. a function of alpha/beta
 };
 
@@ -65,13 +65,23 @@ __device__ __forceinline__ GroupQ group_params(float gmax, float gmin, float alp
   q.live = span > eps;
   q.scale = fmaxf(span, eps);
   q.zp = rintf(__fdiv_rn(-w_min, q.scale));
+  q.rcp = __frcp_rn(q.scale);
   q.w_min = w_min;
   return q;
 }
 
-// x = rint(w/scale + v) + zp, before the clamp.
+// w / scale, correctly rounded (see div_rcp).
+__device__ __forceinline__ float over_scale(float w, const GroupQ& q) {
+  return div_rcp(w, q.scale, q.rcp);
+}
+
+// x = rint(w/scale + v) + zp, before the clamp; ws = w/scale.
+__device__ __forceinline__ float code_from(float ws, float v, const GroupQ& q) {
+  return __fadd_rn(rintf(__fadd_rn(ws, v)), q.zp);
+}
+
 __device__ __forceinline__ float unclamped_code(float w, float v, const GroupQ& q) {
-  return __fadd_rn(rintf(__fadd_rn(__fdiv_rn(w, q.scale), v)), q.zp);
+  return code_from(over_scale(w, q), v, q);
 }
 
 __device__ __forceinline__ float clamp_code(float x, float maxq) {
@@ -180,15 +190,16 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
 
     float gv[8];
     float sum_t = 0.f, sum_out = 0.f;
+    const float wmin_s = __fdiv_rn(q.w_min, q.scale);  // per group
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float x = unclamped_code(wf[i], vf[i], q);
+      const float ws = over_scale(wf[i], q);
+      const float x = code_from(ws, vf[i], q);
       const bool inside = (x >= 0.f) && (x <= maxq);
       const float code = clamp_code(x, maxq);
       const float cz = __fsub_rn(code, q.zp);
       // d(wq)/d(scale): (code - zp) - w/scale inside the clamp, (code - zp) - w_min/scale outside
-      const float d = inside ? __fsub_rn(cz, __fdiv_rn(wf[i], q.scale))
-                             : __fsub_rn(cz, __fdiv_rn(q.w_min, q.scale));
+      const float d = inside ? __fsub_rn(cz, ws) : __fsub_rn(cz, wmin_s);
       sum_t = __fadd_rn(sum_t, __fmul_rn(g[i], d));
       if (!inside) sum_out = __fadd_rn(sum_out, g[i]);
       gv[i] = inside ? __fmul_rn(g[i], q.scale) : 0.f;

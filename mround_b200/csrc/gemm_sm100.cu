@@ -219,7 +219,7 @@ template <int BN, int PREC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
                 int64_t stride_c, const float* __restrict__ bias, int accumulate, int m, int n,
-                int k, int a_kmajor, int b_kmajor) {
+                int k, int a_kmajor, int b_kmajor, int causal, int clen) {
   using C = Cfg<BN, PREC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -247,6 +247,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int z = blockIdx.y;  // batch index
   c += int64_t(z) * stride_c;
 
+  // Causal attention products (rows of a batch entry stack heads of clen
+  // positions; a 128-row tile lies within one head because clen % 128 == 0):
+  //  1: C = Q K^T or dO V^T -- tiles wholly above the diagonal are skipped;
+  //  2: C = P V or dS K     -- K (key positions) stops after the tile's last row;
+  //  3: C = dS^T Q or P^T dO -- K-tiles whose rows all precede the tile's first
+  //     key are skipped.
+  int kt_end = k_tiles;
+  bool skip_tile = false;
+  if (causal == 1) skip_tile = n0 > (m0 % clen) + BM - 1;
+  if (causal == 2) kt_end = min(k_tiles, ((m0 % clen) + BM + BK - 1) / BK);
+  if (skip_tile) kt_end = 0;
+  auto active = [&](int kt) { return causal != 3 || ((kt * BK) % clen) + BK - 1 >= m0; };
+  int n_active = 0;
+  for (int kt = 0; kt < kt_end; ++kt) n_active += active(kt) ? 1 : 0;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -266,10 +281,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ producer
-    for (int kt = 0; kt < k_tiles && ok; ++kt) {
-      const int s = kt % C::kStages;
-      const uint32_t round = kt / C::kStages;
-      if (kt >= C::kStages) ok = mbar_wait(&empty[s], (round - 1) & 1);
+    int it = 0;
+    for (int kt = 0; kt < kt_end && ok; ++kt) {
+      if (!active(kt)) continue;
+      const int s = it % C::kStages;
+      const uint32_t round = it / C::kStages;
+      if (it >= C::kStages) ok = mbar_wait(&empty[s], (round - 1) & 1);
+      ++it;
       if (!ok) break;
       uint8_t* st = smem + s * C::kStage;
       mbar_expect_tx(&full[s], C::kStage);
@@ -292,9 +310,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------ MMA issuer
     const uint32_t idesc = instr_desc(BN, !a_kmajor, !b_kmajor);
-    for (int kt = 0; kt < k_tiles; ++kt) {
-      const int s = kt % C::kStages;
-      ok = mbar_wait(&full[s], (kt / C::kStages) & 1);
+    int it = 0;
+    for (int kt = 0; kt < kt_end; ++kt) {
+      if (!active(kt)) continue;
+      const int s = it % C::kStages;
+      ok = mbar_wait(&full[s], (it / C::kStages) & 1);
       if (!ok) break;
       tc_fence_after();
       const uint32_t st = smem_u32(smem + s * C::kStage);
@@ -304,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t b_lo = b_hi + C::kB;
 #pragma unroll
       for (int ks = 0; ks < BK / 16; ++ks) {
-        const uint32_t acc0 = (kt > 0 || ks > 0) ? 1u : 0u;
+        const uint32_t acc0 = (it > 0 || ks > 0) ? 1u : 0u;
         const uint64_t dah = part_desc(a_hi, a_kmajor, BM, ks);
         const uint64_t dbh = part_desc(b_hi, b_kmajor, BN, ks);
         umma_bf16(tmem, dah, dbh, idesc, acc0);
@@ -312,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (PREC >= 2) umma_bf16(tmem, part_desc(a_lo, a_kmajor, BM, ks), dbh, idesc, 1u);
       }
       umma_commit(&empty[s]);
+      ++it;
     }
     umma_commit(done);  // fires when every MMA issued above has completed
   }
@@ -322,13 +343,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const bool run_epilogue =
       __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(&g_gemm_status) == 0);
-  if (run_epilogue) {
+  if (run_epilogue && !skip_tile) {
     const int row = m0 + warp * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
 #pragma unroll 1
     for (int col = 0; col < BN; col += 32) {
       float v[32];
       tmem_ld32(lane_base + col, v);
+      if (n_active == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
       const int gc = n0 + col;
       if (row < m && gc < n) {
         float* dst = c + int64_t(row) * ldc + gc;
@@ -413,7 +438,7 @@ bool operand_map(CUtensorMap* map, const void* p, bool kmajor, int64_t rows, int
 template <int BN, int PREC>
 int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const float* bias,
            int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
-           cudaStream_t stream) {
+           int causal, int clen, cudaStream_t stream) {
   using C = Cfg<BN, PREC>;
   static bool configured = false;
   if (!configured) {
@@ -427,7 +452,7 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
   }
   const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   gemm_kernel<BN, PREC><<<dim3(tiles, batch), kThreads, C::kSmem, stream>>>(
-      maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor);
+      maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor, causal, clen);
   return launch_status();
 }
 
@@ -441,7 +466,7 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
                                const uint16_t* b_lo, int64_t ldb, int64_t stride_b, int b_kmajor,
                                float* c, int64_t ldc, int64_t stride_c, const float* bias,
                                int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
-                               int precision, void* stream) {
+                               int precision, int causal, int64_t seq, void* stream) {
   if (!a_hi || !b_hi || !c || m <= 0 || n <= 0 || k <= 0 || batch <= 0) return MR_ERR_ARGUMENT;
   if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1 || batch > 65535)
     return MR_ERR_ARGUMENT;
@@ -456,6 +481,13 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
   if (a_kmajor ? lda < k : lda < m) return MR_ERR_ARGUMENT;
   if (b_kmajor ? ldb < k : ldb < n) return MR_ERR_ARGUMENT;
   if (ldc < n) return MR_ERR_ARGUMENT;
+  if (causal < 0 || causal > 3) return MR_ERR_ARGUMENT;
+  if (causal) {
+    if (seq <= 0 || seq % BM || m % seq) return MR_ERR_ARGUMENT;
+    if (causal == 1 && n != seq) return MR_ERR_ARGUMENT;
+    if (causal == 2 && k != seq) return MR_ERR_ARGUMENT;
+    if (causal == 3 && (m != seq || k % seq)) return MR_ERR_ARGUMENT;
+  }
   // narrow outputs (attention's head dimension) use 128-wide tiles
   const int BNsel = n <= 128 ? 128 : 256;
   Maps maps;
@@ -472,15 +504,15 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
   const int M = int(m), N = int(n), Kk = int(k);
   if (BNsel == 128) {
     switch (precision) {
-      case 1: return launch<128, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
-      case 2: return launch<128, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
-      default: return launch<128, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+      case 1: return launch<128, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
+      case 2: return launch<128, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
+      default: return launch<128, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
     }
   }
   switch (precision) {
-    case 1: return launch<256, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
-    case 2: return launch<256, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
-    default: return launch<256, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, s);
+    case 1: return launch<256, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
+    case 2: return launch<256, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
+    default: return launch<256, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
   }
 }
 
@@ -489,7 +521,7 @@ extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, 
                        float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
                        int64_t n, int64_t k, int precision, void* stream) {
   return mr_gemm_batched(a_hi, a_lo, lda, 0, a_kmajor, b_hi, b_lo, ldb, 0, b_kmajor, c, ldc, 0,
-                         bias, accumulate, m, n, k, 1, precision, stream);
+                         bias, accumulate, m, n, k, 1, precision, 0, 0, stream);
 }
 
 // Device status word of the GEMM (0 ok, MR_ERR_TIMEOUT after a wait gave up).

@@ -239,10 +239,33 @@ def gemm(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, a_kmajor: bool, b
         GEMM_EVENTS.append((start, end, 2.0 * m * n * k, precision))
 
 
+def causal_fraction(causal: int, m: int, n: int, k: int, seq: int) -> float:
+    """Share of the dense tile work a causal mode of K3 actually computes
+    (mirrors the kernel's tile and K-tile predicates; BM = 128, BK = 64)."""
+    if not causal:
+        return 1.0
+    bm, bk = 128, 64
+    bn = 128 if n <= 128 else 256
+    m_tiles = -(-m // bm)
+    k_tiles = -(-k // bk)
+    n_tiles = -(-n // bn)
+    done = 0
+    for tm in range(m_tiles):
+        m0 = tm * bm
+        if causal == 1:
+            done += min(n_tiles, (m0 % seq + bm - 1) // bn + 1) * k_tiles
+        elif causal == 2:
+            done += min(k_tiles, (m0 % seq + bm + bk - 1) // bk) * n_tiles
+        else:
+            done += sum(1 for kt in range(k_tiles) if (kt * bk) % seq + bk - 1 >= m0) * n_tiles
+    return done / (m_tiles * n_tiles * k_tiles)
+
+
 def gemm_batched(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, batch: int, a_kmajor: bool,
                  b_kmajor: bool, lda: int, ldb: int, ldc: int, stride_a: int, stride_b: int,
-                 stride_c: int, precision: int, accumulate: bool = False) -> None:
-    """K3 over ``batch`` equally shaped problems in one launch."""
+                 stride_c: int, precision: int, accumulate: bool = False, causal: int = 0,
+                 seq: int = 0) -> None:
+    """K3 over ``batch`` equally shaped problems in one launch (``causal``: see the header)."""
     timing = GEMM_EVENTS is not None
     if timing:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -251,12 +274,13 @@ def gemm_batched(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, batch: in
         _ptr(a_hi, torch.bfloat16, "a_hi"), _ptr(a_lo, torch.bfloat16, "a_lo"), lda, stride_a,
         int(a_kmajor), _ptr(b_hi, torch.bfloat16, "b_hi"), _ptr(b_lo, torch.bfloat16, "b_lo"), ldb,
         stride_b, int(b_kmajor), _ptr(c, torch.float32, "c"), ldc, stride_c, None,
-        int(bool(accumulate)), m, n, k, batch, precision, _stream())
+        int(bool(accumulate)), m, n, k, batch, precision, int(causal), int(seq), _stream())
     check(status, "mr_gemm_batched")
     _count()
     if timing:
         end.record()
-        GEMM_EVENTS.append((start, end, 2.0 * m * n * k * batch, precision))
+        frac = causal_fraction(causal, m, n, k, seq)
+        GEMM_EVENTS.append((start, end, 2.0 * m * n * k * batch * frac, precision))
 
 
 # ---------------------------------------------------------------- block ops
@@ -344,21 +368,22 @@ def swiglu_bwd_split(dact, gu, t: int, i: int):
     return hi, lo
 
 
-def softmax_causal_split(scores, rows: int, s: int, scale: float):
+def softmax_causal_split(scores, rows: int, s: int, scale: float, band: bool = False):
     """Causal softmax in place (row r at position r % s); returns the hi/lo parts."""
     hi, lo = _pair(scores.shape, scores.device)
     st = lib().mr_softmax_causal_split(_ptr(scores, torch.float32, "scores", rows * s), rows, s,
-                                       float(scale), hi.data_ptr(), lo.data_ptr(), _stream())
+                                       float(scale), int(band), hi.data_ptr(), lo.data_ptr(),
+                                       _stream())
     check(st, "mr_softmax_causal_split")
     _count()
     return hi, lo
 
 
-def softmax_bwd_split(dp, p, rows: int, s: int, scale: float):
+def softmax_bwd_split(dp, p, rows: int, s: int, scale: float, band: bool = False):
     hi, lo = _pair(dp.shape, dp.device)
     st = lib().mr_softmax_bwd_split(_ptr(dp, torch.float32, "dp", rows * s),
                                     _ptr(p, torch.float32, "p", rows * s), rows, s, float(scale),
-                                    hi.data_ptr(), lo.data_ptr(), _stream())
+                                    int(band), hi.data_ptr(), lo.data_ptr(), _stream())
     check(st, "mr_softmax_bwd_split")
     _count()
     return hi, lo

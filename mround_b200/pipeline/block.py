@@ -248,10 +248,10 @@ def _mm(a, b, c, *, m, n, k, a_kmajor, b_kmajor, lda, ldb, prec, bias=None, accu
                  precision=prec, bias=bias, accumulate=accumulate)
 
 
-def _bmm(a, b, c, *, m, n, k, batch, a_kmajor, b_kmajor, lda, ldb, sa, sb, sc):
+def _bmm(a, b, c, *, m, n, k, batch, a_kmajor, b_kmajor, lda, ldb, sa, sb, sc, causal=0, seq=0):
     kernels.gemm_batched(a[0], a[1], b[0], b[1], c, m=m, n=n, k=k, batch=batch, a_kmajor=a_kmajor,
                          b_kmajor=b_kmajor, lda=lda, ldb=ldb, ldc=n, stride_a=sa, stride_b=sb,
-                         stride_c=sc, precision=3)
+                         stride_c=sc, precision=3, causal=causal, seq=seq)
 
 
 def _wprec(layer: FusedLinear, want: int) -> int:
@@ -276,13 +276,15 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     cos, sin = self._tables(s)
     q, k, v = kernels.rope_split(qkv, cos, sin, b, s, hq, hkv, d)
     del qkv
+    band = s % 128 == 0  # causal tile skipping needs 128-aligned heads
+    c1, c2 = (1, 2) if band else (0, 0)
     scores = torch.empty((nb, rep * s, s), dtype=torch.float32, device=x.device)
     _bmm(q, k, scores, m=rep * s, n=s, k=d, batch=nb, a_kmajor=True, b_kmajor=True, lda=d, ldb=d,
-         sa=rep * s * d, sb=s * d, sc=rep * s * s)
-    probs = kernels.softmax_causal_split(scores, nb * rep * s, s, scale)  # scores now holds P
+         sa=rep * s * d, sb=s * d, sc=rep * s * s, causal=c1, seq=s)
+    probs = kernels.softmax_causal_split(scores, nb * rep * s, s, scale, band)  # scores -> P
     o = torch.empty((b, hq, s, d), dtype=torch.float32, device=x.device)
     _bmm(probs, v, o, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,
-         sa=rep * s * s, sb=s * d, sc=rep * s * d)
+         sa=rep * s * s, sb=s * d, sc=rep * s * d, causal=c2, seq=s)
     att = kernels.heads_split(o, b, s, hq, d, merge=True)
     del o
     o_l = L["o"]
@@ -348,20 +350,22 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     g_o = kernels.heads_split(datt, b, s, hq, d, merge=False)
     del datt
     q, k, v, p, probs = saved["q"], saved["k"], saved["v"], saved["p"], saved["probs"]
+    band = s % 128 == 0
+    c1, c2, c3 = (1, 2, 3) if band else (0, 0, 0)
     dp = torch.empty((nb, rep * s, s), dtype=torch.float32, device=dout.device)
     _bmm(g_o, v, dp, m=rep * s, n=s, k=d, batch=nb, a_kmajor=True, b_kmajor=True, lda=d, ldb=d,
-         sa=rep * s * d, sb=s * d, sc=rep * s * s)
-    g_s = kernels.softmax_bwd_split(dp, p, nb * rep * s, s, scale)
+         sa=rep * s * d, sb=s * d, sc=rep * s * s, causal=c1, seq=s)
+    g_s = kernels.softmax_bwd_split(dp, p, nb * rep * s, s, scale, band)
     del dp
     dq = torch.empty((b, hq, s, d), dtype=torch.float32, device=dout.device)
     _bmm(g_s, k, dq, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,
-         sa=rep * s * s, sb=s * d, sc=rep * s * d)
+         sa=rep * s * s, sb=s * d, sc=rep * s * d, causal=c2, seq=s)
     dk = torch.empty((b, hkv, s, d), dtype=torch.float32, device=dout.device)
     _bmm(g_s, q, dk, m=s, n=d, k=rep * s, batch=nb, a_kmajor=False, b_kmajor=False, lda=s, ldb=d,
-         sa=rep * s * s, sb=rep * s * d, sc=s * d)
+         sa=rep * s * s, sb=rep * s * d, sc=s * d, causal=c3, seq=s)
     dv = torch.empty((b, hkv, s, d), dtype=torch.float32, device=dout.device)
     _bmm(probs, g_o, dv, m=s, n=d, k=rep * s, batch=nb, a_kmajor=False, b_kmajor=False, lda=s,
-         ldb=d, sa=rep * s * s, sb=rep * s * d, sc=s * d)
+         ldb=d, sa=rep * s * s, sb=rep * s * d, sc=s * d, causal=c3, seq=s)
     del g_s
     cos, sin = self._tables(s)
     g_qkv = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)

@@ -296,3 +296,24 @@ def test_cpu_tensor_is_refused(K):
     with pytest.raises(PlatformError):
         K.fq_forward(w, torch.zeros(8, 64), torch.ones(8, 1), torch.ones(8, 1), bits=2, group=64,
                      eps=1e-8, wq_f32=torch.zeros(8, 64))
+
+
+def test_division_matches_ieee_over_quantizer_range(K):
+    """The quantizer's reciprocal-plus-correction division equals IEEE a / b bit for bit."""
+    from mround_b200._native import lib
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    n = 1 << 24
+    mant = 1.0 + torch.rand(n, device="cuda", generator=g)
+    sign = torch.where(torch.rand(n, device="cuda", generator=g) < 0.5, -1.0, 1.0)
+    a = sign * mant * torch.exp2(torch.randint(-40, 4, (n,), device="cuda", generator=g).float())
+    b = (1.0 + torch.rand(n, device="cuda", generator=g)) * torch.exp2(
+        torch.randint(-27, 2, (n,), device="cuda", generator=g).float())
+    # bf16-valued weights against scales built like the quantizer's
+    a[: n // 2] = a[: n // 2].to(torch.bfloat16).float()
+    a[:1024] = 0.0
+    b[:2048] = 1e-8
+    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert lib().mr_selftest_division(a.data_ptr(), b.data_ptr(), n, bad.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    assert bad.item() == 0
