@@ -257,12 +257,23 @@ def cpu_sample(args, model, arch, budget_s: float = 25.0):
 
 
 # ----------------------------------------------------------------- main
+def _claim_stdout():
+    """Route everything written to fd 1 (NCCL's banner, library prints) to
+    stderr; the returned stream is the only writer of the real stdout, so the
+    run prints exactly one JSON line there."""
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+    return os.fdopen(saved, "w")
+
+
 def main():
     args = parse()
+    out_stream = _claim_stdout()
     from mround_b200.pipeline.dist import init_from_env
 
     if args.impl == "reference":
-        return reference_arm(args)
+        return reference_arm(args, out_stream)
 
     dist = init_from_env()
     device = torch.device("cuda", torch.cuda.current_device())
@@ -373,14 +384,14 @@ def main():
         except Exception as exc:  # noqa: BLE001 - the baseline is reported, not required
             out["cpu_baseline"] = {"value": None, "error": str(exc)}
     if dist.rank == 0:
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=out_stream, flush=True)
     if dist.world > 1:
         import torch.distributed as tdist
 
         tdist.destroy_process_group()
 
 
-def reference_arm(args):
+def reference_arm(args, out_stream):
     """The reference path's CPU implementation (the oracle restatement; the
     reference's MLX loop cannot run here), timed on this host's cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -403,7 +414,7 @@ def reference_arm(args):
                    "global_batch": BATCH, "seq_len": SEQ, "parallelism": "cpu"},
         "cpu_baseline": cpu,
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }), file=out_stream, flush=True)
 
 
 if __name__ == "__main__":

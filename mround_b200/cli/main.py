@@ -51,6 +51,12 @@ def build_parser() -> argparse.ArgumentParser:
     q.add_argument("--memory-budget", type=int, default=None)
     q.add_argument("--skip-memory-check", action="store_true")
     q.add_argument("--dry-run", action="store_true", help="Resolve and validate, then stop.")
+    q.add_argument("--scoring-samples", type=int, default=None,
+                   help="Sequences for the mixed-precision scoring pass (api scoring_samples).")
+    q.add_argument("--scoring-seq-len", type=int, default=None,
+                   help="Tokens per scoring sequence (api scoring_seq_len).")
+    q.add_argument("--sensitivity-gradients", default="auto",
+                   choices=["auto", "own_width", "widest"])
     return parser
 
 
@@ -74,6 +80,8 @@ def _quantize(args: argparse.Namespace) -> int:
                       candidate_bits=args.options, remainder_bits=args.remainder_bits,
                       tuning=tuning, calibration=args.calibration, export_format=args.format,
                       seed=args.seed, memory_budget=args.memory_budget,
+                      scoring_samples=args.scoring_samples, scoring_seq_len=args.scoring_seq_len,
+                      sensitivity_gradients=args.sensitivity_gradients,
                       memory_check=not args.skip_memory_check,
                       min_block_coverage=0.0 if args.allow_dense else MIN_BLOCK_COVERAGE)
     if result.summary is not None:

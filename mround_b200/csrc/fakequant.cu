@@ -288,6 +288,21 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
         biases[gi] = f32_to_bf16(__fmul_rn(-bf16_to_f32(sb), bf16_to_f32(zb)));
       }
     }
+    // Widths dividing 32 need no cross-lane assembly beyond a pair of lanes:
+    // 4 bits -> one word per lane, 8 bits -> two, 2 bits -> half a word.
+    if (bits == 4) {
+      if (in) packed[e / 8] = uint32_t(chunk);
+      continue;
+    }
+    if (bits == 8) {
+      if (in) *reinterpret_cast<uint2*>(packed + e / 4) = make_uint2(uint32_t(chunk), uint32_t(chunk >> 32));
+      continue;
+    }
+    if (bits == 2) {
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, uint32_t(chunk), 1);
+      if (in && (lane & 1) == 0) packed[e / 16] = (uint32_t(chunk) & 0xFFFFu) | (other << 16);
+      continue;
+    }
     // Word j of this tile takes its bits from lane j*32/chunk_bits and the
     // next one; a tile holds 8*bits words, so each lane forms up to two.
 #pragma unroll
@@ -386,7 +401,7 @@ extern "C" int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* 
   if (!alpha || !beta || !packed || !scales_bf16 || !biases_bf16) return MR_ERR_ARGUMENT;
   if (32 % bits == 0 ? (cols % (32 / bits)) : (cols % 32)) return MR_ERR_ARGUMENT;
   if (codes && (reinterpret_cast<uintptr_t>(codes) & 7u)) return MR_ERR_ALIGNMENT;
-  if (reinterpret_cast<uintptr_t>(packed) & 3u) return MR_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(packed) & (bits == 8 ? 7u : 3u)) return MR_ERR_ALIGNMENT;
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
   const float maxq = float((1 << bits) - 1);
