@@ -66,34 +66,85 @@ def parse():
 
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event reasons sampled every 10 ms during the timed region.
 
+    Reads NVML (found by the CUDA device's UUID, so it is the GPU this rank
+    drives); falls back to ``nvidia-smi -lms 200`` when NVML is unavailable.
+    Nothing here changes a GPU setting.  A timed region shorter than the first
+    sample still records one sample, taken when the region ends.
+    """
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int) -> None:
-        self.index = index
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.samples: list[tuple[float, float, set]] = []
         self.proc = None
-        self.lines: list[str] = []
+        self.handle = None
+        self.stop = threading.Event()
+        self.thread = None
+
+    def _nvml_handle(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(
+                uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:  # noqa: BLE001 -- any NVML failure selects the fallback
+            return None, None
+
+    def _nvml_sample(self):
+        nv = self.nvml
+        sm = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM))
+        mask = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+        self.samples.append((sm, mx, {n for n, bit in self.REASONS if mask & bit}))
+
+    def _nvml_loop(self):
+        while not self.stop.wait(0.01):
+            self._nvml_sample()
 
     def __enter__(self):
+        self.nvml, self.handle = self._nvml_handle()
+        if self.handle is not None:
+            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={self.device.index}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread = threading.Thread(target=self._smi_read, daemon=True)
             self.thread.start()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def _read(self):
+    def _smi_read(self):
+        names = [n for n, _ in self.REASONS]
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            self.samples.append((sm, mx, {n for n, f in zip(names, parts[5:9])
+                                          if f.lower().startswith("active")}))
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.handle is not None:
+            self.thread.join(timeout=1)
+            if not self.samples:
+                self._nvml_sample()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -103,23 +154,21 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
+        sm = [s[0] for s in self.samples]
+        reasons = set().union(*(s[2] for s in self.samples)) if self.samples else set()
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "sm_max_mhz": max(s[1] for s in self.samples) if sm else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.handle is not None else "nvidia-smi"}
+
+
+# DRAM bytes (read + write) per K3 launch, averaged over the 17 GEMM launches of
+# one 7B step (8 x 2048 tokens, N=1), from one ncu capture of this workload:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+#       --clock-control none -k regex:gemm_kernel -s 96 -c 36
+#       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-e2e
+# (58.2 GB read + 11.0 GB written per step).
+GEMM_TRAFFIC_7B = 4.07e9
 
 
 # ----------------------------------------------------------------- workload
@@ -292,7 +341,7 @@ def main():
     for i in range(args.warmup):
         step(i)
     launches0 = kernels.LAUNCHES[0]
-    with ClockSampler(device.index) as clocks:
+    with ClockSampler(device) as clocks:
         ms_steps = timed(lambda i: step(args.warmup + i), args.steps, dist, device)
     launches = kernels.LAUNCHES[0] - launches0
     t_step = ms_steps / args.steps
@@ -374,7 +423,8 @@ def main():
                      "executed_tflops": exe_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0,
                      "executed_frac": (exe_flops / (gemm_ms / 1e3) / 1e12) / peak if gemm_ms else 0.0,
                      "gemm_share_of_step": gemm_ms / t_step if t_step else None,
-                     "traffic": None},
+                     "traffic": GEMM_TRAFFIC_7B if args.arch == "qwen2.5-7b" and dist.world == 1 else None,
+                     "traffic_unit": "bytes per K3 launch (DRAM read + write), ncu capture"},
         "clocks": clocks.summary(),
         "e2e": e2e,
     }

@@ -59,58 +59,79 @@ int mr_device_check(void);
 const char* mr_last_cuda_error(void);
 
 /*
- * K1 -- fused asymmetric fake-quant forward.
- * Replaces fake_quantize (mround/core/quantizer.py:287-347, asym branch
- * 341-347) as called by _TunableLinear.__call__ (mround/pipeline/runner.py:364-366).
- *   scale = max((max(gmax,0)*alpha - min(gmin,0)*beta) / (2^bits-1), eps)
- *   zp    = rint(-w_min / scale)
- *   q     = clamp(rint(w/scale + v) + zp, 0, 2^bits-1)
- *   wq    = scale * (q - zp)
+ * Scheme arguments shared by K1, K2 and K5 (reference QuantScheme.symmetry and
+ * .scale_init, mround/schemes.py:74-200):
+ *   symmetric = 0, init_scale = NULL   asymmetric observed range: codes in
+ *       [0, 2^bits-1], scale and zero point from the clipped extremes;
+ *   symmetric = 1, init_scale = NULL   symmetric observed range: codes in
+ *       [-2^(bits-1), 2^(bits-1)-1], scale = s / 2^(bits-1) with s the
+ *       dominant clipped extreme negated (positive side: -max(gmax,0)*alpha,
+ *       else -min(gmin,0)*beta), then sign(s)*max(|s|, eps);
+ *   symmetric = 1, init_scale != NULL  searched (v2): scale =
+ *       sign*max(|init_scale*beta|, eps), alpha inert; init_scale is float32
+ *       (rows, cols/group), e.g. from mr_scale_search.
+ * symmetric = 0 with init_scale != NULL is refused (MR_ERR_ARGUMENT).
+ */
+
+/*
+ * K1 -- fused fake-quant forward.
+ * Replaces fake_quantize (mround/core/quantizer.py:287-347) as called by
+ * _TunableLinear.__call__ (mround/pipeline/runner.py:364-366).
+ *   asymmetric: scale = max((max(gmax,0)*alpha - min(gmin,0)*beta) / (2^bits-1), eps)
+ *               zp = rint(-w_min / scale); q = clamp(rint(w/scale + v) + zp, 0, 2^bits-1)
+ *               wq = scale * (q - zp)
+ *   symmetric:  q = clamp(rint(w/scale + v), -2^(bits-1), 2^(bits-1)-1); wq = scale * q
  * Outputs (any may be NULL): wq_hi = bf16(wq), wq_lo = bf16(wq - wq_hi) (the
  * split that lets two bf16 GEMM operands carry a float32 weight), wq_f32,
- * scale and zp per group (float32, (rows, cols/group)).
+ * scale and zp per group (float32, (rows, cols/group); zp is 0 under the
+ * symmetric schemes).
  * IEEE division and ties-to-even rounding: codes are bit-exact.
  */
 int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
                   const float* beta, int64_t rows, int64_t cols, int group, int bits,
-                  float eps, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_f32,
-                  float* scale, float* zp, void* stream);
+                  int symmetric, const float* init_scale, float eps, uint16_t* wq_hi,
+                  uint16_t* wq_lo, float* wq_f32, float* scale, float* zp, void* stream);
 
 /*
  * K2 -- straight-through backward fused with signSGD and projection.
  * Replaces the autodiff of fake_quantize (mround/core/quantizer.py:110-149,
- * 254-266, 341-345; hand form mround/reference/quantize.py:488-520) and
- * SignSGD.apply + project_params (mround/core/signsgd.py:125-145,
+ * 228-266, 319-345; hand form mround/reference/quantize.py:370-397, 465-520)
+ * and SignSGD.apply + project_params (mround/core/signsgd.py:125-145,
  * mround/core/quantizer.py:430-446; called at mround/pipeline/runner.py:926-931).
  * gq = dL/dwq, float32 (rows, cols).  With update != 0, V, alpha and beta are
  * updated in place:  p <- clip(p - lr*sign(g_p), lo, hi)  (V bounded by 0.5,
- * alpha and beta by [coef_lo, coef_hi]).
+ * alpha and beta by [coef_lo, coef_hi]).  Under the symmetric schemes only the
+ * dominant side's coefficient receives gradient; under the searched scheme
+ * alpha receives none.
  * Optional outputs (NULL to skip): the gradients gv (rows, cols), galpha and
  * gbeta (rows, cols/group); and, when update != 0, the NEXT step's operands
  * wq_hi/wq_lo recomputed from the updated parameters (fusing K1).
  */
 int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
                    float* beta, int64_t rows, int64_t cols, int group, int bits,
-                   float eps, float lr, float coef_lo, float coef_hi, int update,
-                   float* gv, float* galpha, float* gbeta, uint16_t* wq_hi,
-                   uint16_t* wq_lo, void* stream);
+                   int symmetric, const float* init_scale, float eps, float lr,
+                   float coef_lo, float coef_hi, int update, float* gv, float* galpha,
+                   float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, void* stream);
 
 /*
  * K5 -- commit and MLX packing in one pass.
- * Replaces quantize_codes (mround/core/quantizer.py:395-398), narrow_codes
- * (mround/formats/mlx_export.py:109-125), pack_codes
- * (mround/formats/packing.py:119-163) and to_affine
- * (mround/formats/mlx_export.py:159-195) for asymmetric schemes:
- *   packed (rows, cols*bits/32) uint32, element 0 in the least significant
- *   bits; 2/4/8 bits tile words, 3/5/6/7 form a little-endian bitstream;
- *   scales = bf16(scale), biases = bf16(-scales * bf16(zp)), (rows, cols/group).
- * codes (uint8, rows x cols) is optional.  Bit-exact.
+ * Replaces quantize_codes (mround/core/quantizer.py:350-398), narrow_codes
+ * (mround/formats/mlx_export.py:109-125), the symmetric offset and pack_codes
+ * (mlx_export.py:215-222, mround/formats/packing.py:119-163) and to_affine
+ * (mround/formats/mlx_export.py:159-195):
+ *   packed (rows, cols*bits/32) uint32 of the unsigned codes (the code, or
+ *   code + 2^(bits-1) under the symmetric schemes), element 0 in the least
+ *   significant bits; 2/4/8 bits tile words, 3/5/6/7 form a little-endian
+ *   bitstream; scales = bf16(scale), biases = bf16(-scales * zp) with zp the
+ *   bf16 zero point or the fixed 2^(bits-1), (rows, cols/group).
+ * codes (rows x cols, one byte each: uint8, or int8 under the symmetric
+ * schemes) is optional.  Bit-exact.
  * cols must be a multiple of 32 for 3/5/6/7 bits and of 32/bits otherwise.
  */
 int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* alpha,
                 const float* beta, int64_t rows, int64_t cols, int group, int bits,
-                float eps, uint32_t* packed, uint16_t* scales_bf16,
-                uint16_t* biases_bf16, uint8_t* codes, void* stream);
+                int symmetric, const float* init_scale, float eps, uint32_t* packed,
+                uint16_t* scales_bf16, uint16_t* biases_bf16, uint8_t* codes, void* stream);
 
 /*
  * K4 -- block-output loss, the exact global outlier threshold and dL/dpred.
@@ -177,12 +198,48 @@ int mr_loss_apply(const float* pred, const float* target, int64_t n, double deno
  * Replaces the per-layer term of _accumulate (mround/pipeline/scoring.py:262,
  * definition mround/planner/sensitivity.py:190-229):
  *   out[j] += sum |g * (RTN_{bits[j]}(w) - w)|   for j < n_bits,
- * RTN being the quantizer with v = 0 and unit coefficients.  Float64
- * accumulation.  out is device memory (n_bits doubles), accumulated into.
+ * RTN being the quantizer with v = 0 and unit coefficients (scoring.py:213-221)
+ * under the scheme given by symmetric / grids: grids NULL is the observed
+ * range; otherwise grids[j] is the searched scale of width bits[j] (float32,
+ * rows x cols/group, scoring.py:195-210) and symmetric must be 1.  grids is a
+ * host array of n_bits device pointers.  Float64 accumulation.  out is device
+ * memory (n_bits doubles), accumulated into.
  */
 int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t cols,
-                 int group, const int* bits, int n_bits, float eps, double* out,
-                 void* stream);
+                 int group, const int* bits, int n_bits, int symmetric,
+                 const float* const* grids, float eps, double* out, void* stream);
+
+/*
+ * K8 -- the v2 candidate scale grid search (symmetric schemes).
+ * Replaces search_scales (mround/core/scale_search.py:73-187; NumPy oracle
+ * mround/reference/scale_search.py:130-211), called by
+ * QuantizationRunner._search_scales (mround/pipeline/runner.py:712-760) and
+ * scoring's _grids (mround/pipeline/scoring.py:195-210).
+ * Per group of w_bf16 (rows, cols): anchor = the signed largest-magnitude
+ * element (first on ties); for each candidate c in order, eff = cands[c],
+ *   inverse = -eff * (1/anchor)  (0 when anchor is 0)
+ *   codes   = clamp(rint(inverse * w), -2^(bits-1), 2^(bits-1)-1)
+ *   scale   = 1/inverse          (0 when inverse is 0)
+ *   loss    = sum (scale*codes - w)^2 [* importance[col]]
+ * keeping the first candidate with the strictly smallest loss.  Float32, the
+ * sum of each group formed by 8-element runs combined pairwise.
+ * cands: host array of n_cands (1..256) float32 effective ranges, the anchor
+ * 2^(bits-1) first.  importance: float32 (cols) or NULL.
+ * out: float32 (rows, cols/group), a zero scale for an all-zero group.
+ */
+int mr_scale_search(const uint16_t* w_bf16, int64_t rows, int64_t cols, int group, int bits,
+                    const float* cands, int n_cands, const float* importance, float* out,
+                    void* stream);
+
+/*
+ * Importance statistics for the searched scale: out[c] += sum_r x[r, c]^2
+ * over rows of a float32 activation given as its bf16 parts (x = hi + lo;
+ * lo may be NULL).  Replaces the collection mode of _TunableLinear.__call__
+ * (mround/pipeline/runner.py:359-363).  Float32 accumulation; cols a multiple
+ * of 8, pointers 16-byte aligned.
+ */
+int mr_colsumsq_split(const uint16_t* hi, const uint16_t* lo, int64_t rows, int64_t cols,
+                      float* out, void* stream);
 
 /*
  * Self-test of the kernels' arithmetic (no reference counterpart): counts, into

@@ -41,10 +41,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_status_string": (ctypes.c_char_p, [_I]),
     "mr_device_check": (_I, []),
     "mr_last_cuda_error": (ctypes.c_char_p, []),
-    "mr_fq_forward": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _P, _P, _P, _P]),
-    "mr_ste_signsgd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I, _I, _F, _F, _F, _F, _I,
+    "mr_fq_forward": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _P, _P, _P, _P, _P,
+                           _P]),
+    "mr_ste_signsgd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _F, _F, _F, _I,
                             _P, _P, _P, _P, _P, _P]),
-    "mr_pack_mlx": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _P, _P, _P]),
+    "mr_pack_mlx": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _P, _P, _P, _P, _P]),
     "mr_loss_workspace_bytes": (ctypes.c_size_t, []),
     "mr_loss_outlier": (_I, [_P, _P, _I64, _I64, _I, _D, _F, _P, _P, _P, _P, _P]),
     "mr_loss_noalloc_scratch_bytes": (ctypes.c_size_t, []),
@@ -52,7 +53,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_loss_hist_pass": (_I, [_P, _P, _I64, _I, _P, _P, _P]),
     "mr_loss_select_digit": (_I, [_P, _I64, _I, _P, _P, _P]),
     "mr_loss_apply": (_I, [_P, _P, _I64, _D, _P, _I, _P, _P, _P, _P]),
-    "mr_deltaloss": (_I, [_P, _P, _I64, _I64, _I, _P, _I, _F, _P, _P]),
+    "mr_deltaloss": (_I, [_P, _P, _I64, _I64, _I, _P, _I, _I, _P, _F, _P, _P]),
+    "mr_scale_search": (_I, [_P, _I64, _I64, _I, _I, _P, _I, _P, _P, _P]),
+    "mr_colsumsq_split": (_I, [_P, _P, _I64, _I64, _P, _P]),
     "mr_split_bf16": (_I, [_P, _I64, _P, _P, _P]),
     "mr_selftest_division": (_I, [_P, _P, _I64, _P, _P]),
     "mr_gemm": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _P, _I64, _P, _I, _I64, _I64, _I64,

@@ -11,8 +11,9 @@ precision, run the block loop, round the remainder to nearest, export, write
   mround/pipeline/loader.py) is not on this path;
 - calibration ``"auto"`` is Zipf(1.1) token ids over the vocabulary (the
   reference's pile-10k is not available offline);
-- the device quantizer implements asymmetric observed-range schemes; a
-  symmetric or searched scheme raises ``UnsupportedSchemeError``;
+- every scheme the reference defines runs on the device (asymmetric and
+  symmetric observed range, and the searched v2 scale below 4 bits on
+  symmetric runs, ``default_scale_init``);
 - ``memory_budget``/``memory_check`` are accepted and recorded, the Mac
   memory and time rules (mround/planner/memory.py, timing.py) are not applied.
 """
@@ -126,10 +127,6 @@ def _resolve_scheme(*, bits, group_size, symmetry, average_bits, candidate_bits,
         widths = set(cands)
         if remainder_bits is not None:
             widths.add(int(remainder_bits))
-    if resolved.symmetry is not Symmetry.ASYMMETRIC or resolved.scale_init is not ScaleInit.OBSERVED_RANGE:
-        raise UnsupportedSchemeError(
-            "the B200 tuning path implements asymmetric observed-range schemes "
-            "(pass symmetry='asym'); symmetric schemes and the v2 scale search are not on it")
     return resolved, widths
 
 
@@ -153,15 +150,23 @@ def _calibration(model: SyntheticModel, tuning: TuningConfig, seed: int | None,
 
 
 def _rtn_layer(weight: torch.Tensor, scheme: QuantScheme, device) -> QuantizedLayer:
+    """Round-to-nearest with nothing learned (reference _round_to_nearest_layers,
+    mround/api.py:1877-1937): a searched scheme searches unweighted first."""
     from mround_b200 import kernels
+    from mround_b200.core.scale_search import search_scales
 
-    w = weight.to(device).contiguous()
+    w = weight.to(device).to(torch.bfloat16).contiguous()
     rows, cols = w.shape
     ng = cols // scheme.group_size
     zeros = torch.zeros((rows, cols), dtype=torch.float32, device=device)
     ones = torch.ones((rows, ng), dtype=torch.float32, device=device)
-    packed, scales, biases, _ = kernels.pack_mlx(w, zeros, ones, ones, bits=scheme.bits,
-                                                 group=scheme.group_size, eps=1e-8)
+    init = None
+    if scheme.scale_init is ScaleInit.SEARCHED:
+        init = torch.empty((rows, ng), dtype=torch.float32, device=device)
+        search_scales(w, scheme, out=init)
+    packed, scales, biases, _ = kernels.pack_mlx(
+        w, zeros, ones, ones, bits=scheme.bits, group=scheme.group_size, eps=1e-8,
+        symmetric=scheme.symmetry is Symmetry.SYMMETRIC, init_scale=init)
     return QuantizedLayer(packed.cpu(), scales.cpu(), biases.cpu(), scheme, (rows, cols))
 
 
@@ -365,7 +370,7 @@ def quantize(model: str | Path | SyntheticModel, *, output_dir: str | Path, bits
 
 def quantize_round_to_nearest(model: str | Path | SyntheticModel, *, output_dir: str | Path,
                               bits: int = 4, group_size: int = 64,
-                              symmetry: Symmetry = Symmetry.ASYMMETRIC) -> QuantizeResult:
+                              symmetry: Symmetry = Symmetry.SYMMETRIC) -> QuantizeResult:
     """Every eligible module rounded to nearest, nothing learned (reference api.py:841)."""
     scheme = QuantScheme(bits=bits, group_size=group_size, symmetry=symmetry)
     _resolve_scheme(bits=bits, group_size=group_size, symmetry=symmetry, average_bits=None,

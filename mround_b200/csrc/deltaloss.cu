@@ -9,6 +9,10 @@
 // (mround/pipeline/scoring.py:262) forms it; accumulation is float64
 // (mround/planner/sensitivity.py:190-229).  Same warp-tile layout as the
 // quantizer kernels: 8 elements per lane, a group over group/8 lanes.
+// Symmetric schemes: the observed-range scale opposite to the dominant extreme
+// over 2^(b-1), or the searched grid of each width; codes in
+// [-2^(b-1), 2^(b-1)-1], reconstruction scale * code (mround/core/quantizer.py:
+// 216-251, 319-339).
 
 #include "common.cuh"
 
@@ -22,10 +26,17 @@ constexpr int kMaxWidths = 8;
 
 struct Widths {
   int n;
-  float maxq[kMaxWidths];
+  float maxq[kMaxWidths];          // 2^b - 1 (asymmetric) or 2^(b-1) (symmetric)
+  const float* grid[kMaxWidths];   // searched scale per group, or NULL
 };
 
-template <int LPG>
+// sign(s) * max(|s|, eps), sign(0) = +1
+__device__ __forceinline__ float clamp_mag(float s, float eps) {
+  const float m = fmaxf(fabsf(s), eps);
+  return s < 0.f ? -m : m;
+}
+
+template <int LPG, int SYM>
 __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __restrict__ g,
                                                              const uint16_t* __restrict__ w,
                                                              int64_t n, Widths widths, float eps,
@@ -64,19 +75,40 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
     if (!in) continue;
     const float w_max = gmax > 0.f ? gmax : 0.f;
     const float w_min = gmin < 0.f ? gmin : 0.f;
+    const int64_t gi = e / (LPG * 8);
 #pragma unroll
     for (int j = 0; j < kMaxWidths; ++j) {
       if (j >= widths.n) break;
       const float maxq = widths.maxq[j];
-      const float scale = fmaxf(__fdiv_rn(__fsub_rn(w_max, w_min), maxq), eps);
-      const float zp = rintf(__fdiv_rn(-w_min, scale));
-      const float rcp = __frcp_rn(scale);
       float part = 0.f;
+      if constexpr (SYM) {
+        float scale;
+        if (widths.grid[j]) {
+          scale = clamp_mag(widths.grid[j][gi], eps);
+        } else {
+          const float neg = -w_min;
+          const bool pos = w_max >= neg;
+          const float dom = pos ? w_max : neg;
+          scale = clamp_mag(__fdiv_rn(pos ? -dom : dom, maxq), eps);
+        }
+        const float rcp = __frcp_rn(scale);
+        const float hi = __fsub_rn(maxq, 1.f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float x = __fadd_rn(rintf(div_rcp(wf[i], scale, rcp)), zp);
-        const float q = __fmul_rn(scale, __fsub_rn(fminf(fmaxf(x, 0.f), maxq), zp));
-        part = __fadd_rn(part, fabsf(__fmul_rn(gf[i], __fsub_rn(q, wf[i]))));
+        for (int i = 0; i < 8; ++i) {
+          const float c = fminf(fmaxf(rintf(div_rcp(wf[i], scale, rcp)), -maxq), hi);
+          const float q = __fmul_rn(scale, c);
+          part = __fadd_rn(part, fabsf(__fmul_rn(gf[i], __fsub_rn(q, wf[i]))));
+        }
+      } else {
+        const float scale = fmaxf(__fdiv_rn(__fsub_rn(w_max, w_min), maxq), eps);
+        const float zp = rintf(__fdiv_rn(-w_min, scale));
+        const float rcp = __frcp_rn(scale);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float x = __fadd_rn(rintf(div_rcp(wf[i], scale, rcp)), zp);
+          const float q = __fmul_rn(scale, __fsub_rn(fminf(fmaxf(x, 0.f), maxq), zp));
+          part = __fadd_rn(part, fabsf(__fmul_rn(gf[i], __fsub_rn(q, wf[i]))));
+        }
       }
       acc[j] += double(part);
     }
@@ -102,31 +134,41 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
 using namespace mr;
 
 extern "C" int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows, int64_t cols,
-                            int group, const int* bits, int n_bits, float eps, double* out,
-                            void* stream) {
+                            int group, const int* bits, int n_bits, int symmetric,
+                            const float* const* grids, float eps, double* out, void* stream) {
   if (!g || !w_bf16 || !bits || !out || rows <= 0 || cols <= 0) return MR_ERR_ARGUMENT;
   if (n_bits < 1 || n_bits > kMaxWidths) return MR_ERR_ARGUMENT;
   if (group != 8 && group != 16 && group != 32 && group != 64 && group != 128 && group != 256)
     return MR_ERR_ARGUMENT;
   if (cols % group) return MR_ERR_ARGUMENT;
+  if (grids && !symmetric) return MR_ERR_ARGUMENT;
   if (!aligned16(g) || !aligned16(w_bf16)) return MR_ERR_ALIGNMENT;
   Widths widths{};
   widths.n = n_bits;
   for (int j = 0; j < n_bits; ++j) {
     if (bits[j] < 2 || bits[j] > 8) return MR_ERR_ARGUMENT;
-    widths.maxq[j] = float((1 << bits[j]) - 1);
+    widths.maxq[j] = symmetric ? float(1 << (bits[j] - 1)) : float((1 << bits[j]) - 1);
+    widths.grid[j] = grids ? grids[j] : nullptr;
+    if (grids && !grids[j]) return MR_ERR_ARGUMENT;
   }
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (group / 8) {
-    case 1: deltaloss_kernel<1><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
-    case 2: deltaloss_kernel<2><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
-    case 4: deltaloss_kernel<4><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
-    case 8: deltaloss_kernel<8><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
-    case 16: deltaloss_kernel<16><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
-    case 32: deltaloss_kernel<32><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;
-    default: return MR_ERR_ARGUMENT;
+#define MR_DL_LAUNCH(SYM)                                                                       \
+  switch (group / 8) {                                                                          \
+    case 1: deltaloss_kernel<1, SYM><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;   \
+    case 2: deltaloss_kernel<2, SYM><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;   \
+    case 4: deltaloss_kernel<4, SYM><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;   \
+    case 8: deltaloss_kernel<8, SYM><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break;   \
+    case 16: deltaloss_kernel<16, SYM><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break; \
+    case 32: deltaloss_kernel<32, SYM><<<grid, kThreads, 0, s>>>(g, w_bf16, n, widths, eps, out); break; \
+    default: return MR_ERR_ARGUMENT;                                                             \
   }
+  if (symmetric) {
+    MR_DL_LAUNCH(1)
+  } else {
+    MR_DL_LAUNCH(0)
+  }
+#undef MR_DL_LAUNCH
   return launch_status();
 }

@@ -25,9 +25,20 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kTile = 256;  // elements per warp tile
 
+// Scheme of a launch, fixed at compile time:
+//   kAsym      codes in [0, 2^b - 1], scale from the clipped extremes, zero point
+//              (reference asymmetric_scale, mround/core/quantizer.py:254-266);
+//   kSym       codes in [-2^(b-1), 2^(b-1) - 1], signed scale opposite to the
+//              dominant clipped extreme (symmetric_scale, quantizer.py:228-251);
+//   kSearched  symmetric codes, scale = searched per-group value times beta,
+//              alpha inert (the searched branch, quantizer.py:319-331).
+// ``maxq`` is 2^b - 1 under kAsym and 2^(b-1) otherwise.
+enum Mode { kAsym = 0, kSym = 1, kSearched = 2 };
+
 struct GroupQ {
-  float scale, rcp, zp, w_min, wmax_raw, wmin_raw;
+  float scale, rcp, zp, w_min, wmax_raw, wmin_raw, base;
   bool live;  // scale above the eps floor, i.e. a function of alpha/beta
+  bool pos;   // kSym: the positive side dominates (alpha carries the gradient)
 };
 
 template <int LPG>
@@ -53,20 +64,45 @@ __device__ __forceinline__ float group_sum(float x) {
   return x;
 }
 
-// scale and zero point of one group (reference asymmetric_scale).
+// sign(s) * max(|s|, eps) with sign(0) = +1 (reference _clamp_magnitude,
+// quantizer.py:216-225).
+__device__ __forceinline__ float clamp_magnitude(float s, float eps, bool& live) {
+  const float mag = fabsf(s);
+  live = mag > eps;
+  const float m = fmaxf(mag, eps);
+  return s < 0.f ? -m : m;
+}
+
+// Scale (and zero point under kAsym) of one group.  ``base`` is the searched
+// scale (kSearched only).
+template <int MODE>
 __device__ __forceinline__ GroupQ group_params(float gmax, float gmin, float alpha, float beta,
-                                               float maxq, float eps) {
+                                               float base, float maxq, float eps) {
   GroupQ q;
   q.wmax_raw = gmax > 0.f ? gmax : 0.f;
   q.wmin_raw = gmin < 0.f ? gmin : 0.f;
-  const float w_max = __fmul_rn(q.wmax_raw, alpha);
-  const float w_min = __fmul_rn(q.wmin_raw, beta);
-  const float span = __fdiv_rn(__fsub_rn(w_max, w_min), maxq);
-  q.live = span > eps;
-  q.scale = fmaxf(span, eps);
-  q.zp = rintf(__fdiv_rn(-w_min, q.scale));
+  q.base = base;
+  q.pos = false;
+  q.zp = 0.f;
+  q.w_min = 0.f;
+  if constexpr (MODE == kAsym) {
+    const float w_max = __fmul_rn(q.wmax_raw, alpha);
+    const float w_min = __fmul_rn(q.wmin_raw, beta);
+    const float span = __fdiv_rn(__fsub_rn(w_max, w_min), maxq);
+    q.live = span > eps;
+    q.scale = fmaxf(span, eps);
+    q.zp = rintf(__fdiv_rn(-w_min, q.scale));
+    q.w_min = w_min;
+  } else if constexpr (MODE == kSym) {
+    const float w_max = __fmul_rn(q.wmax_raw, alpha);
+    const float neg = -__fmul_rn(q.wmin_raw, beta);
+    q.pos = w_max >= neg;
+    const float dominant = q.pos ? w_max : neg;
+    q.scale = clamp_magnitude(__fdiv_rn(q.pos ? -dominant : dominant, maxq), eps, q.live);
+  } else {
+    q.scale = clamp_magnitude(__fmul_rn(base, beta), eps, q.live);
+  }
   q.rcp = __frcp_rn(q.scale);
-  q.w_min = w_min;
   return q;
 }
 
@@ -75,21 +111,38 @@ __device__ __forceinline__ float over_scale(float w, const GroupQ& q) {
   return div_rcp(w, q.scale, q.rcp);
 }
 
-// x = rint(w/scale + v) + zp, before the clamp; ws = w/scale.
+// The code before the clamp from ws = w/scale: rint(ws + v) (+ zp under kAsym).
+template <int MODE>
 __device__ __forceinline__ float code_from(float ws, float v, const GroupQ& q) {
-  return __fadd_rn(rintf(__fadd_rn(ws, v)), q.zp);
+  const float r = rintf(__fadd_rn(ws, v));
+  if constexpr (MODE == kAsym) return __fadd_rn(r, q.zp);
+  return r;
 }
 
+template <int MODE>
 __device__ __forceinline__ float unclamped_code(float w, float v, const GroupQ& q) {
-  return code_from(over_scale(w, q), v, q);
+  return code_from<MODE>(over_scale(w, q), v, q);
 }
 
+template <int MODE>
+__device__ __forceinline__ float code_lo(float maxq) {
+  return MODE == kAsym ? 0.f : -maxq;
+}
+
+template <int MODE>
+__device__ __forceinline__ float code_hi(float maxq) {
+  return MODE == kAsym ? maxq : __fsub_rn(maxq, 1.f);
+}
+
+template <int MODE>
 __device__ __forceinline__ float clamp_code(float x, float maxq) {
-  return fminf(fmaxf(x, 0.f), maxq);
+  return fminf(fmaxf(x, code_lo<MODE>(maxq)), code_hi<MODE>(maxq));
 }
 
+template <int MODE>
 __device__ __forceinline__ float dequant(float code, const GroupQ& q) {
-  return __fmul_rn(q.scale, __fsub_rn(code, q.zp));
+  if constexpr (MODE == kAsym) return __fmul_rn(q.scale, __fsub_rn(code, q.zp));
+  return __fmul_rn(q.scale, code);
 }
 
 __device__ __forceinline__ float signf(float x) {
@@ -120,13 +173,23 @@ __device__ __forceinline__ void store_split(const float (&wq)[8], int64_t e, uin
   if (lo) *reinterpret_cast<uint4*>(lo + e) = pack8(l);
 }
 
+// Group extremes (not needed under kSearched) and the per-group inputs.
+template <int LPG, int MODE>
+__device__ __forceinline__ void extremes_for(const float (&wf)[8], float& gmax, float& gmin) {
+  if constexpr (MODE != kSearched) {
+    group_extremes<LPG>(wf, gmax, gmin);
+  } else {
+    gmax = gmin = 0.f;
+  }
+}
+
 // ---------------------------------------------------------------- K1
-template <int LPG>
+template <int LPG, int MODE>
 __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
     const uint16_t* __restrict__ w, const float* __restrict__ v, const float* __restrict__ alpha,
-    const float* __restrict__ beta, int64_t n, int group, float maxq, float eps,
-    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo, float* __restrict__ wq_f32,
-    float* __restrict__ scale_out, float* __restrict__ zp_out) {
+    const float* __restrict__ beta, const float* __restrict__ init_scale, int64_t n, int group,
+    float maxq, float eps, uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo,
+    float* __restrict__ wq_f32, float* __restrict__ scale_out, float* __restrict__ zp_out) {
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
@@ -142,13 +205,15 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
       for (int i = 0; i < 8; ++i) wf[i] = vf[i] = 0.f;
     }
     float gmax, gmin;
-    group_extremes<LPG>(wf, gmax, gmin);
+    extremes_for<LPG, MODE>(wf, gmax, gmin);
     if (!in) continue;  // whole groups lie past the end together
     const int64_t gi = e / group;
-    const GroupQ q = group_params(gmax, gmin, alpha[gi], beta[gi], maxq, eps);
+    const GroupQ q = group_params<MODE>(gmax, gmin, alpha[gi], beta[gi],
+                                        MODE == kSearched ? init_scale[gi] : 0.f, maxq, eps);
     float wq[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) wq[i] = dequant(clamp_code(unclamped_code(wf[i], vf[i], q), maxq), q);
+    for (int i = 0; i < 8; ++i)
+      wq[i] = dequant<MODE>(clamp_code<MODE>(unclamped_code<MODE>(wf[i], vf[i], q), maxq), q);
     store_split(wq, e, wq_hi, wq_lo);
     if (wq_f32) store_f8(wq_f32 + e, wq);
     if ((lane & (LPG - 1)) == 0) {
@@ -159,13 +224,24 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
 }
 
 // ---------------------------------------------------------------- K2
-template <int LPG>
+// Straight-through gradients per group (reference hand derivation
+// mround/reference/quantize.py:370-397, 465-520; the chain MLX autodiff forms):
+//   gV = g * scale * inside
+//   kAsym:     d(wq)/d(scale) = (code - zp) - w/scale inside the clamp,
+//              (code - zp) - w_min/scale outside; galpha = gs * w_max_raw,
+//              gbeta = (sum_out g - gs) * w_min_raw, gs = sum g*d / maxq
+//   kSym:      d(wq)/d(scale) = code - inside * w/scale; only the dominant
+//              side's coefficient moves the scale: galpha = -gs * w_max_raw or
+//              gbeta = -gs * w_min_raw, gs = sum g*d / 2^(b-1)
+//   kSearched: same d; galpha = 0, gbeta = sum g*d * searched scale
+// with gs zeroed where the eps floor holds the scale.
+template <int LPG, int MODE>
 __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
     const float* __restrict__ gq, const uint16_t* __restrict__ w, float* __restrict__ v,
-    float* __restrict__ alpha, float* __restrict__ beta, int64_t n, int group, float maxq,
-    float eps, float lr, float lo, float hi, int update, float* __restrict__ gv_out,
-    float* __restrict__ ga_out, float* __restrict__ gb_out, uint16_t* __restrict__ wq_hi,
-    uint16_t* __restrict__ wq_lo) {
+    float* __restrict__ alpha, float* __restrict__ beta, const float* __restrict__ init_scale,
+    int64_t n, int group, float maxq, float eps, float lr, float lo, float hi, int update,
+    float* __restrict__ gv_out, float* __restrict__ ga_out, float* __restrict__ gb_out,
+    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo) {
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
@@ -182,34 +258,49 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
       for (int i = 0; i < 8; ++i) wf[i] = vf[i] = g[i] = 0.f;
     }
     float gmax, gmin;
-    group_extremes<LPG>(wf, gmax, gmin);
+    extremes_for<LPG, MODE>(wf, gmax, gmin);
     const int64_t gi = in ? e / group : 0;
     const float a = in ? alpha[gi] : 1.f;
     const float b = in ? beta[gi] : 1.f;
-    const GroupQ q = group_params(gmax, gmin, a, b, maxq, eps);
+    const float base = (MODE == kSearched && in) ? init_scale[gi] : 1.f;
+    const GroupQ q = group_params<MODE>(gmax, gmin, a, b, base, maxq, eps);
 
     float gv[8];
     float sum_t = 0.f, sum_out = 0.f;
-    const float wmin_s = __fdiv_rn(q.w_min, q.scale);  // per group
+    const float wmin_s = MODE == kAsym ? __fdiv_rn(q.w_min, q.scale) : 0.f;  // per group
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float ws = over_scale(wf[i], q);
-      const float x = code_from(ws, vf[i], q);
-      const bool inside = (x >= 0.f) && (x <= maxq);
-      const float code = clamp_code(x, maxq);
-      const float cz = __fsub_rn(code, q.zp);
-      // d(wq)/d(scale): (code - zp) - w/scale inside the clamp, (code - zp) - w_min/scale outside
-      const float d = inside ? __fsub_rn(cz, ws) : __fsub_rn(cz, wmin_s);
+      const float x = code_from<MODE>(ws, vf[i], q);
+      const bool inside = (x >= code_lo<MODE>(maxq)) && (x <= code_hi<MODE>(maxq));
+      const float code = clamp_code<MODE>(x, maxq);
+      float d;
+      if constexpr (MODE == kAsym) {
+        const float cz = __fsub_rn(code, q.zp);
+        d = inside ? __fsub_rn(cz, ws) : __fsub_rn(cz, wmin_s);
+        if (!inside) sum_out = __fadd_rn(sum_out, g[i]);
+      } else {
+        d = inside ? __fsub_rn(code, ws) : code;
+      }
       sum_t = __fadd_rn(sum_t, __fmul_rn(g[i], d));
-      if (!inside) sum_out = __fadd_rn(sum_out, g[i]);
       gv[i] = inside ? __fmul_rn(g[i], q.scale) : 0.f;
     }
     sum_t = group_sum<LPG>(sum_t);
-    sum_out = group_sum<LPG>(sum_out);
+    if constexpr (MODE == kAsym) sum_out = group_sum<LPG>(sum_out);
     if (!in) continue;
-    const float gs = q.live ? __fdiv_rn(sum_t, maxq) : 0.f;
-    const float ga = __fmul_rn(gs, q.wmax_raw);
-    const float gb = __fmul_rn(__fsub_rn(sum_out, gs), q.wmin_raw);
+    float ga, gb;
+    if constexpr (MODE == kAsym) {
+      const float gs = q.live ? __fdiv_rn(sum_t, maxq) : 0.f;
+      ga = __fmul_rn(gs, q.wmax_raw);
+      gb = __fmul_rn(__fsub_rn(sum_out, gs), q.wmin_raw);
+    } else if constexpr (MODE == kSym) {
+      const float gs = q.live ? __fdiv_rn(sum_t, maxq) : 0.f;  // maxq = 2^(b-1): exact
+      ga = q.pos ? -__fmul_rn(gs, q.wmax_raw) : 0.f;
+      gb = q.pos ? 0.f : -__fmul_rn(gs, q.wmin_raw);
+    } else {
+      ga = 0.f;
+      gb = q.live ? __fmul_rn(sum_t, q.base) : 0.f;
+    }
     const bool leader = (lane & (LPG - 1)) == 0;
     if (gv_out) store_f8(gv_out + e, gv);
     if (leader) {
@@ -229,27 +320,34 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
       beta[gi] = bn;
     }
     if (wq_hi || wq_lo) {
-      const GroupQ qn = group_params(gmax, gmin, an, bn, maxq, eps);
+      const GroupQ qn = group_params<MODE>(gmax, gmin, an, bn, base, maxq, eps);
       float wq[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        wq[i] = dequant(clamp_code(unclamped_code(wf[i], vn[i], qn), maxq), qn);
+        wq[i] = dequant<MODE>(clamp_code<MODE>(unclamped_code<MODE>(wf[i], vn[i], qn), maxq), qn);
       store_split(wq, e, wq_hi, wq_lo);
     }
   }
 }
 
 // ---------------------------------------------------------------- K5
-template <int LPG>
+// Stored codes are unsigned: the code itself under kAsym, code + 2^(b-1) under
+// the symmetric schemes (reference mround/formats/mlx_export.py:215-222).
+// Affine form W = scales * q_u + biases with scales = bf16(scale) and
+// biases = bf16(-scales * zp), zp the zero point or the fixed 2^(b-1)
+// (mlx_export.py:159-195).  ``codes_out`` receives the codes one byte each:
+// uint8 under kAsym, int8 (two's complement) under the symmetric schemes.
+template <int LPG, int MODE>
 __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
     const uint16_t* __restrict__ w, const float* __restrict__ v, const float* __restrict__ alpha,
-    const float* __restrict__ beta, int64_t n, int group, int bits, float maxq, float eps,
-    uint32_t* __restrict__ packed, uint16_t* __restrict__ scales, uint16_t* __restrict__ biases,
-    uint8_t* __restrict__ codes_out) {
+    const float* __restrict__ beta, const float* __restrict__ init_scale, int64_t n, int group,
+    int bits, float maxq, float eps, uint32_t* __restrict__ packed, uint16_t* __restrict__ scales,
+    uint16_t* __restrict__ biases, uint8_t* __restrict__ codes_out) {
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   const int64_t total_words = n * bits / 32;
   const int chunk_bits = 8 * bits;  // bits one lane contributes, 16..64
+  const float offset = MODE == kAsym ? 0.f : maxq;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
        t += int64_t(gridDim.x) * kWarps) {
     const int64_t e = t * kTile + lane * 8;
@@ -263,17 +361,18 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
       for (int i = 0; i < 8; ++i) wf[i] = vf[i] = 0.f;
     }
     float gmax, gmin;
-    group_extremes<LPG>(wf, gmax, gmin);
+    extremes_for<LPG, MODE>(wf, gmax, gmin);
     uint64_t chunk = 0;
     if (in) {
       const int64_t gi = e / group;
-      const GroupQ q = group_params(gmax, gmin, alpha[gi], beta[gi], maxq, eps);
+      const GroupQ q = group_params<MODE>(gmax, gmin, alpha[gi], beta[gi],
+                                          MODE == kSearched ? init_scale[gi] : 0.f, maxq, eps);
       uint8_t c8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint32_t c = uint32_t(clamp_code(unclamped_code(wf[i], vf[i], q), maxq));
-        c8[i] = uint8_t(c);
-        chunk |= uint64_t(c) << (i * bits);
+        const float code = clamp_code<MODE>(unclamped_code<MODE>(wf[i], vf[i], q), maxq);
+        c8[i] = uint8_t(int(code));
+        chunk |= uint64_t(uint32_t(__fadd_rn(code, offset))) << (i * bits);
       }
       if (codes_out) {
         uint2 u;
@@ -283,9 +382,9 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
       }
       if ((lane & (LPG - 1)) == 0) {
         const uint16_t sb = f32_to_bf16(q.scale);
-        const uint16_t zb = f32_to_bf16(q.zp);
+        const float zb = MODE == kAsym ? bf16_to_f32(f32_to_bf16(q.zp)) : offset;
         scales[gi] = sb;
-        biases[gi] = f32_to_bf16(__fmul_rn(-bf16_to_f32(sb), bf16_to_f32(zb)));
+        biases[gi] = f32_to_bf16(__fmul_rn(-bf16_to_f32(sb), zb));
       }
     }
     // Widths dividing 32 need no cross-lane assembly beyond a pair of lanes:
@@ -343,70 +442,97 @@ int check_common(const void* w, const void* v, int64_t rows, int64_t cols, int g
 
 using namespace mr;
 
-#define MR_DISPATCH_LPG(group, KERNEL, GRID, STREAM, ...)                             \
-  switch ((group) / 8) {                                                             \
-    case 1: KERNEL<1><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
-    case 2: KERNEL<2><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
-    case 4: KERNEL<4><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
-    case 8: KERNEL<8><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;            \
-    case 16: KERNEL<16><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
-    case 32: KERNEL<32><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
-    default: return MR_ERR_ARGUMENT;                                                 \
+#define MR_LAUNCH_LPG(MODE, group, KERNEL, GRID, STREAM, ...)                            \
+  switch ((group) / 8) {                                                                 \
+    case 1: KERNEL<1, MODE><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
+    case 2: KERNEL<2, MODE><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
+    case 4: KERNEL<4, MODE><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
+    case 8: KERNEL<8, MODE><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;          \
+    case 16: KERNEL<16, MODE><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;        \
+    case 32: KERNEL<32, MODE><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;        \
+    default: return MR_ERR_ARGUMENT;                                                     \
   }
+
+#define MR_DISPATCH(mode, group, KERNEL, GRID, STREAM, ...)                                \
+  switch (mode) {                                                                        \
+    case kAsym: MR_LAUNCH_LPG(kAsym, group, KERNEL, GRID, STREAM, __VA_ARGS__) break;    \
+    case kSym: MR_LAUNCH_LPG(kSym, group, KERNEL, GRID, STREAM, __VA_ARGS__) break;      \
+    default: MR_LAUNCH_LPG(kSearched, group, KERNEL, GRID, STREAM, __VA_ARGS__) break;   \
+  }
+
+namespace {
+
+// Scheme mode from the ABI arguments; -1 for an invalid combination.
+int scheme_mode(int symmetric, const float* init_scale) {
+  if (init_scale) return symmetric ? kSearched : -1;
+  return symmetric ? kSym : kAsym;
+}
+
+float mode_maxq(int mode, int bits) {
+  return mode == kAsym ? float((1 << bits) - 1) : float(1 << (bits - 1));
+}
+
+}  // namespace
 
 extern "C" int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
                              const float* beta, int64_t rows, int64_t cols, int group, int bits,
-                             float eps, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_f32,
-                             float* scale, float* zp, void* stream) {
+                             int symmetric, const float* init_scale, float eps, uint16_t* wq_hi,
+                             uint16_t* wq_lo, float* wq_f32, float* scale, float* zp,
+                             void* stream) {
   int st = check_common(w_bf16, v, rows, cols, group, bits);
   if (st) return st;
-  if (!alpha || !beta) return MR_ERR_ARGUMENT;
+  const int mode = scheme_mode(symmetric, init_scale);
+  if (!alpha || !beta || mode < 0) return MR_ERR_ARGUMENT;
   if ((wq_hi && !aligned16(wq_hi)) || (wq_lo && !aligned16(wq_lo)) || (wq_f32 && !aligned16(wq_f32)))
     return MR_ERR_ALIGNMENT;
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
-  const float maxq = float((1 << bits) - 1);
+  const float maxq = mode_maxq(mode, bits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  MR_DISPATCH_LPG(group, fq_forward_kernel, grid, s, w_bf16, v, alpha, beta, n, group, maxq, eps,
-                  wq_hi, wq_lo, wq_f32, scale, zp);
+  MR_DISPATCH(mode, group, fq_forward_kernel, grid, s, w_bf16, v, alpha, beta, init_scale, n,
+              group, maxq, eps, wq_hi, wq_lo, wq_f32, scale, zp);
   return launch_status();
 }
 
 extern "C" int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
                               float* beta, int64_t rows, int64_t cols, int group, int bits,
-                              float eps, float lr, float coef_lo, float coef_hi, int update,
-                              float* gv, float* galpha, float* gbeta, uint16_t* wq_hi,
-                              uint16_t* wq_lo, void* stream) {
+                              int symmetric, const float* init_scale, float eps, float lr,
+                              float coef_lo, float coef_hi, int update, float* gv, float* galpha,
+                              float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, void* stream) {
   int st = check_common(w_bf16, v, rows, cols, group, bits);
   if (st) return st;
-  if (!gq || !alpha || !beta) return MR_ERR_ARGUMENT;
+  const int mode = scheme_mode(symmetric, init_scale);
+  if (!gq || !alpha || !beta || mode < 0) return MR_ERR_ARGUMENT;
   if (!aligned16(gq) || (gv && !aligned16(gv)) || (wq_hi && !aligned16(wq_hi)) ||
       (wq_lo && !aligned16(wq_lo)))
     return MR_ERR_ALIGNMENT;
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
-  const float maxq = float((1 << bits) - 1);
+  const float maxq = mode_maxq(mode, bits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  MR_DISPATCH_LPG(group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, n, group, maxq,
-                  eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo);
+  MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, init_scale, n,
+              group, maxq, eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo);
   return launch_status();
 }
 
 extern "C" int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* alpha,
                            const float* beta, int64_t rows, int64_t cols, int group, int bits,
-                           float eps, uint32_t* packed, uint16_t* scales_bf16,
-                           uint16_t* biases_bf16, uint8_t* codes, void* stream) {
+                           int symmetric, const float* init_scale, float eps, uint32_t* packed,
+                           uint16_t* scales_bf16, uint16_t* biases_bf16, uint8_t* codes,
+                           void* stream) {
   int st = check_common(w_bf16, v, rows, cols, group, bits);
   if (st) return st;
-  if (!alpha || !beta || !packed || !scales_bf16 || !biases_bf16) return MR_ERR_ARGUMENT;
+  const int mode = scheme_mode(symmetric, init_scale);
+  if (!alpha || !beta || !packed || !scales_bf16 || !biases_bf16 || mode < 0)
+    return MR_ERR_ARGUMENT;
   if (32 % bits == 0 ? (cols % (32 / bits)) : (cols % 32)) return MR_ERR_ARGUMENT;
   if (codes && (reinterpret_cast<uintptr_t>(codes) & 7u)) return MR_ERR_ALIGNMENT;
   if (reinterpret_cast<uintptr_t>(packed) & (bits == 8 ? 7u : 3u)) return MR_ERR_ALIGNMENT;
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
-  const float maxq = float((1 << bits) - 1);
+  const float maxq = mode_maxq(mode, bits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  MR_DISPATCH_LPG(group, pack_mlx_kernel, grid, s, w_bf16, v, alpha, beta, n, group, bits, maxq,
-                  eps, packed, scales_bf16, biases_bf16, codes);
+  MR_DISPATCH(mode, group, pack_mlx_kernel, grid, s, w_bf16, v, alpha, beta, init_scale, n, group,
+              bits, maxq, eps, packed, scales_bf16, biases_bf16, codes);
   return launch_status();
 }

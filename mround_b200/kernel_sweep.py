@@ -12,6 +12,11 @@ Algorithmic bytes per launch (per weight, plus per group):
   K5 pack_mlx          read W 2 + V 4, write bits/8                 (+12 B/group)
   K6 deltaloss (3 w.)  read g 4 + W 2                               = 6 B
 
+K8 (the scale search) is bound by float32 issue, not HBM: every weight is
+read once (2 B) but evaluated against ~200 candidates at ~8 float32 operations
+each; it is reported as candidate-element evaluations per second beside its
+bandwidth.
+
 Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick]
 Prints one JSON line per case, then a summary line.
 """
@@ -95,6 +100,13 @@ def run(reps: int = 5, quick: bool = False) -> list[dict]:
                                                                eps=1e-8, out=out),
                                      6 * n),
                 }
+                from mround_b200.core.scale_search import candidates
+
+                cands = candidates(bits)
+                cases["K8_scale_search"] = (
+                    lambda: kernels.scale_search(w, bits=bits, group=group, candidates=cands,
+                                                 out=a),
+                    2 * n + 4 * ng)
                 for name, (fn, nbytes) in cases.items():
                     if name == "K6_deltaloss" and bits != 2:
                         continue  # one pass scores every width; timed once per shape/group
@@ -105,15 +117,23 @@ def run(reps: int = 5, quick: bool = False) -> list[dict]:
                     rec = {"kernel": name, "rows": rows, "cols": cols, "bits": bits, "group": group,
                            "ms": ms, "bytes": nbytes, "gbs": gbs, "frac": gbs / peak,
                            "peak_gbs": peak, "peak_source": src}
+                    if name == "K8_scale_search":
+                        rec["candidates"] = len(cands)
+                        rec["evals_per_s"] = n * len(cands) / (ms * 1e-3)
                     results.append(rec)
                     print(json.dumps(rec), flush=True)
     big = [r for r in results if r["rows"] * r["cols"] >= 3584 * 3584]
     summary = {}
-    for name in sorted({r["kernel"] for r in results}):
+    for name in sorted({r["kernel"] for r in results} - {"K8_scale_search"}):
         sel = [r["frac"] for r in big if r["kernel"] == name]
         if sel:
             summary[name] = {"median_frac_large": statistics.median(sel), "min_frac_large": min(sel),
                              "max_frac_large": max(sel)}
+    k8 = [r for r in big if r["kernel"] == "K8_scale_search"]
+    if k8:
+        summary["K8_scale_search"] = {"median_ms_large": statistics.median(r["ms"] for r in k8),
+                                      "median_evals_per_s": statistics.median(r["evals_per_s"]
+                                                                              for r in k8)}
     print(json.dumps({"summary": summary, "peak_gbs": peak, "peak_source": src}), flush=True)
     return results
 

@@ -15,6 +15,7 @@ from mround_b200.exceptions import PlatformError, SchemeError
 
 __all__ = [
     "LossWorkspace",
+    "colsumsq_split",
     "deltaloss",
     "fq_forward",
     "gemm",
@@ -24,6 +25,7 @@ __all__ = [
     "loss_outlier",
     "loss_select_digit",
     "pack_mlx",
+    "scale_search",
     "split_bf16",
     "ste_signsgd",
 ]
@@ -76,13 +78,24 @@ def _weight_args(w, v, alpha, beta, group):
     )
 
 
+def _scheme_args(symmetric: bool, init_scale, ng: int):
+    if init_scale is not None and not symmetric:
+        raise SchemeError("a searched scale belongs to a symmetric scheme")
+    return int(bool(symmetric)), _ptr(init_scale, torch.float32, "init_scale", ng)
+
+
 def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=None, wq_lo=None,
-               wq_f32=None, scale=None, zp=None) -> None:
-    """K1: write the fake-quantized weight (bf16 hi/lo split and/or float32)."""
+               wq_f32=None, scale=None, zp=None, symmetric: bool = False, init_scale=None) -> None:
+    """K1: write the fake-quantized weight (bf16 hi/lo split and/or float32).
+
+    ``symmetric`` selects the symmetric code range; ``init_scale`` (float32,
+    one per group) the searched scale.
+    """
     rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
     n, ng = rows * cols, rows * (cols // group)
+    sym, pinit = _scheme_args(symmetric, init_scale, ng)
     status = lib().mr_fq_forward(
-        pw, pv, pa, pb, rows, cols, group, bits, eps,
+        pw, pv, pa, pb, rows, cols, group, bits, sym, pinit, eps,
         _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
         _ptr(wq_f32, torch.float32, "wq_f32", n), _ptr(scale, torch.float32, "scale", ng),
         _ptr(zp, torch.float32, "zp", ng), _stream())
@@ -92,12 +105,14 @@ def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=No
 
 def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr: float,
                 lo: float, hi: float, update: bool = True, gv=None, galpha=None, gbeta=None,
-                wq_hi=None, wq_lo=None) -> None:
+                wq_hi=None, wq_lo=None, symmetric: bool = False, init_scale=None) -> None:
     """K2: straight-through gradients, then (if ``update``) the signed step in place."""
     rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
     n, ng = rows * cols, rows * (cols // group)
+    sym, pinit = _scheme_args(symmetric, init_scale, ng)
     status = lib().mr_ste_signsgd(
-        _ptr(gq, torch.float32, "gq", n), pw, pv, pa, pb, rows, cols, group, bits, eps, lr, lo,
+        _ptr(gq, torch.float32, "gq", n), pw, pv, pa, pb, rows, cols, group, bits, sym, pinit,
+        eps, lr, lo,
         hi, int(bool(update)), _ptr(gv, torch.float32, "gv", n),
         _ptr(galpha, torch.float32, "galpha", ng), _ptr(gbeta, torch.float32, "gbeta", ng),
         _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
@@ -106,9 +121,14 @@ def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr:
     _count()
 
 
-def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes: bool = False):
-    """K5: ``(packed uint32 as int32, scales bf16, biases bf16, codes uint8 or None)``."""
+def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes: bool = False,
+             symmetric: bool = False, init_scale=None):
+    """K5: ``(packed uint32 as int32, scales bf16, biases bf16, codes or None)``.
+
+    Codes are uint8, or int8 under a symmetric scheme.
+    """
     rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
+    sym, pinit = _scheme_args(symmetric, init_scale, rows * (cols // group))
     if 32 % bits == 0:
         if cols % (32 // bits):
             raise SchemeError(f"cols={cols} does not tile {bits}-bit words")
@@ -121,9 +141,10 @@ def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes
     packed = torch.empty((rows, words), dtype=torch.int32, device=dev)
     scales = torch.empty((rows, cols // group), dtype=torch.bfloat16, device=dev)
     biases = torch.empty_like(scales)
-    codes = torch.empty((rows, cols), dtype=torch.uint8, device=dev) if want_codes else None
+    code_dtype = torch.int8 if sym else torch.uint8
+    codes = torch.empty((rows, cols), dtype=code_dtype, device=dev) if want_codes else None
     status = lib().mr_pack_mlx(
-        pw, pv, pa, pb, rows, cols, group, bits, eps, packed.data_ptr(), scales.data_ptr(),
+        pw, pv, pa, pb, rows, cols, group, bits, sym, pinit, eps, packed.data_ptr(), scales.data_ptr(),
         biases.data_ptr(), None if codes is None else codes.data_ptr(), _stream())
     check(status, "mr_pack_mlx")
     _count()
@@ -189,19 +210,75 @@ def loss_apply(pred, target, ws: LossWorkspace, *, suppress: bool, denom: float,
     _count(2)
 
 
-def deltaloss(g, w, *, bits: list[int] | tuple[int, ...], group: int, eps: float, out) -> None:
-    """K6: ``out[j] += sum |g * (RTN_bits[j](w) - w)|`` (``out`` float64, on device)."""
+def deltaloss(g, w, *, bits: list[int] | tuple[int, ...], group: int, eps: float, out,
+              symmetric: bool = False, grids=None) -> None:
+    """K6: ``out[j] += sum |g * (RTN_bits[j](w) - w)|`` (``out`` float64, on device).
+
+    ``grids``: one searched scale tensor per width (float32, one per group) for
+    a searched scheme, else None.
+    """
     import ctypes
 
     if w.dim() != 2:
         raise SchemeError("expected a 2-D weight")
     rows, cols = w.shape
+    if grids is not None and not symmetric:
+        raise SchemeError("searched grids belong to a symmetric scheme")
     widths = (ctypes.c_int * len(bits))(*[int(b) for b in bits])
+    grid_arr = None
+    if grids is not None:
+        if len(grids) != len(bits):
+            raise SchemeError("one searched grid per width")
+        ptrs = [_ptr(gr, torch.float32, "grid", rows * (cols // group)) for gr in grids]
+        grid_arr = ctypes.cast((ctypes.c_void_p * len(ptrs))(*ptrs), ctypes.c_void_p)
     status = lib().mr_deltaloss(
         _ptr(g, torch.float32, "g", rows * cols), _ptr(w, torch.bfloat16, "w", rows * cols),
-        rows, cols, group, ctypes.cast(widths, ctypes.c_void_p), len(bits), eps,
-        _ptr(out, torch.float64, "out", len(bits)), _stream())
+        rows, cols, group, ctypes.cast(widths, ctypes.c_void_p), len(bits), int(bool(symmetric)),
+        grid_arr, eps, _ptr(out, torch.float64, "out", len(bits)), _stream())
     check(status, "mr_deltaloss")
+    _count()
+
+
+def scale_search(w, *, bits: int, group: int, candidates, importance=None, out=None):
+    """K8: the searched scale of every group of ``w`` (bf16 (rows, cols)).
+
+    ``candidates``: effective ranges in evaluation order (anchor first), any
+    sequence of floats, converted to float32.  ``importance``: float32 (cols,)
+    or None.  Returns float32 (rows, cols // group).
+    """
+    import ctypes
+
+    if w.dim() != 2:
+        raise SchemeError("expected a 2-D weight")
+    rows, cols = w.shape
+    if group not in DEVICE_GROUPS or cols % group:
+        raise SchemeError(f"group {group} is not supported on the device for {cols} columns")
+    cands = [float(c) for c in candidates]
+    if not 1 <= len(cands) <= 256:
+        raise SchemeError("1 to 256 candidates")
+    arr = (ctypes.c_float * len(cands))(*cands)
+    if out is None:
+        out = torch.empty((rows, cols // group), dtype=torch.float32, device=w.device)
+    status = lib().mr_scale_search(
+        _ptr(w, torch.bfloat16, "w", rows * cols), rows, cols, group, bits,
+        ctypes.cast(arr, ctypes.c_void_p), len(cands),
+        _ptr(importance, torch.float32, "importance", cols),
+        _ptr(out, torch.float32, "out", rows * (cols // group)), _stream())
+    check(status, "mr_scale_search")
+    _count()
+    return out
+
+
+def colsumsq_split(hi, lo, out) -> None:
+    """``out[c] += sum_r (hi + lo)[r, c]^2`` for a float32 activation in bf16 parts."""
+    if hi.dim() != 2:
+        raise SchemeError("expected a 2-D activation")
+    rows, cols = hi.shape
+    status = lib().mr_colsumsq_split(
+        _ptr(hi, torch.bfloat16, "hi", rows * cols),
+        _ptr(lo, torch.bfloat16, "lo", rows * cols) if lo is not None else None, rows, cols,
+        _ptr(out, torch.float32, "out", cols), _stream())
+    check(status, "mr_colsumsq_split")
     _count()
 
 

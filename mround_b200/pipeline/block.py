@@ -258,8 +258,17 @@ def _wprec(layer: FusedLinear, want: int) -> int:
     return want if layer.wq_lo is not None else min(want, 2)
 
 
-def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bool):
+def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bool,
+                   collect: dict[str, torch.Tensor] | None = None):
+    """Block forward.  ``collect`` maps fused-layer names to float32 (in_features,)
+    accumulators: each receives the summed squared input its GEMM sees (the
+    importance statistics of the searched scale)."""
     a = self.arch
+
+    def stats(name, op):
+        if collect is not None and name in collect:
+            kernels.colsumsq_split(op[0], op[1], collect[name])
+
     b, s, h = x.shape
     t = b * s
     hq, hkv, d, inter = a.heads, a.kv_heads, a.head_dim, a.intermediate
@@ -269,6 +278,7 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     L = self.layers
     h1 = kernels.rmsnorm_split(x2, self.input_norm, a.rms_eps)
     qkv_l = L["qkv"]
+    stats("qkv", h1)
     qkv = torch.empty((t, qkv_l.out_features), dtype=torch.float32, device=x.device)
     p = _wprec(qkv_l, prec.forward)
     _mm(h1, (qkv_l.wq_hi, qkv_l.wq_lo), qkv, m=t, n=qkv_l.out_features, k=h, a_kmajor=True,
@@ -288,16 +298,19 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     att = kernels.heads_split(o, b, s, hq, d, merge=True)
     del o
     o_l = L["o"]
+    stats("o", att)
     hres = x2.clone()
     _mm(att, (o_l.wq_hi, o_l.wq_lo), hres, m=t, n=h, k=hq * d, a_kmajor=True, b_kmajor=True,
         lda=hq * d, ldb=hq * d, prec=_wprec(o_l, prec.forward), accumulate=True)
     h2_hi, h2_lo, rstd2 = kernels.rmsnorm_split(hres, self.post_norm, a.rms_eps)
     gu_l = L["gate_up"]
+    stats("gate_up", (h2_hi, h2_lo))
     gu = torch.empty((t, 2 * inter), dtype=torch.float32, device=x.device)
     _mm((h2_hi, h2_lo), (gu_l.wq_hi, gu_l.wq_lo), gu, m=t, n=2 * inter, k=h, a_kmajor=True,
         b_kmajor=True, lda=h, ldb=h, prec=_wprec(gu_l, prec.forward))
     act = kernels.swiglu_split(gu, t, inter)
     dn_l = L["down"]
+    stats("down", act)
     out = hres.clone()
     _mm(act, (dn_l.wq_hi, dn_l.wq_lo), out, m=t, n=h, k=inter, a_kmajor=True, b_kmajor=True,
         lda=inter, ldb=inter, prec=_wprec(dn_l, prec.forward), accumulate=True)

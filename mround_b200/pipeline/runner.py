@@ -297,6 +297,8 @@ class QuantizationRunner:
         if not tuner.tunables:
             reasons = "; ".join(f"{p}: {why}" for p, why in tuner.skipped)
             raise ArchitectureError(f"nothing in {name!r} can be quantized at this group size. {reasons}")
+        with meter.stage("search"):
+            search_seconds = tuner.search(inputs)
         outcome = self._tune(tuner, inputs, targets, meter)
         with meter.stage("commit"):
             layers = tuner.commit(self.keep_codes)
@@ -309,7 +311,8 @@ class QuantizationRunner:
             stage_peaks=dict(meter.stages),
             tuned=tuple(sorted(m.path for t in tuner.tunables for m in t.members)),
             skipped=tuple(tuner.skipped), reverted=outcome["reverted"],
-            generalization_gap=outcome["gap"], step_seconds=outcome["step_seconds"])
+            generalization_gap=outcome["gap"], step_seconds=outcome["step_seconds"],
+            search_seconds=search_seconds)
         return result, exported
 
     def _tune(self, tuner: BlockTuner, inputs, targets, meter: _Meter) -> dict[str, Any]:

@@ -31,7 +31,8 @@ from mround_b200 import kernels
 from mround_b200.exceptions import SchemeError
 from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision, rms_norm
 from mround_b200.pipeline.model import SyntheticModel
-from mround_b200.schemes import DEFAULT_EPS_FP32, QuantScheme
+from mround_b200.core.scale_search import search_scales
+from mround_b200.schemes import DEFAULT_EPS_FP32, QuantScheme, ScaleInit, Symmetry
 
 __all__ = ["SensitivityScores", "score_widths"]
 
@@ -119,13 +120,31 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
             layer.grad = grad_pool[key]
     acc = {p: torch.zeros(len(widths), dtype=torch.float64, device=dev) for p in shapes}
     active: dict[str, list[int]] = {}
+    symmetric = base_scheme.symmetry is Symmetry.SYMMETRIC
+    searched = base_scheme.scale_init is ScaleInit.SEARCHED
+    # searched schemes: each layer's unweighted searched scale at every width,
+    # kept (a few numbers per group) to rebuild that width's quantize-dequantize
+    # (reference _grids, mround/pipeline/scoring.py:195-210)
+    grids: dict[tuple[int, int], torch.Tensor] = {}
+    if searched:
+        for blk in blocks:
+            for layer in blk.layers.values():
+                if layer.in_features % group:
+                    continue
+                for bits in widths:
+                    scheme = dataclasses.replace(base_scheme, bits=bits)
+                    out = torch.empty((layer.out_features, layer.in_features // group),
+                                      dtype=torch.float32, device=dev)
+                    search_scales(layer.w, scheme, out=out)
+                    grids[(id(layer), bits)] = out
 
     def on_grad(layer: FusedLinear) -> None:
         for full, r0, r1 in paths_by_layer[id(layer)]:
             bits = active["bits"]
             out = torch.zeros(len(bits), dtype=torch.float64, device=dev)
+            g = [grids[(id(layer), b)][r0:r1] for b in bits] if searched else None
             kernels.deltaloss(layer.grad[r0:r1], layer.w[r0:r1], bits=bits, group=group, eps=eps,
-                              out=out)
+                              out=out, symmetric=symmetric, grids=g)
             idx = [widths.index(b) for b in bits]
             acc[full][idx] += out
 
@@ -147,7 +166,8 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
                 zeros = torch.zeros((o, i), dtype=torch.float32, device=dev)
                 hi, lo = torch.empty_like(layer.w), torch.empty_like(layer.w)
                 kernels.fq_forward(layer.w, zeros, ones[key], ones[key], bits=bits, group=group,
-                                   eps=eps, wq_hi=hi, wq_lo=lo)
+                                   eps=eps, wq_hi=hi, wq_lo=lo, symmetric=symmetric,
+                                   init_scale=grids.get((id(layer), bits)))
                 layer.wq_hi, layer.wq_lo = hi, lo
 
     embed = model.embed_tokens().to(dev)

@@ -19,14 +19,16 @@ device and are read once per block.
 from __future__ import annotations
 
 import dataclasses
+import time
 
 import torch
 
 from mround_b200 import kernels
 from mround_b200.core.quantizer import require_device_scheme
+from mround_b200.core.scale_search import search_scales
 from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision
 from mround_b200.pipeline.dist import DistContext
-from mround_b200.schemes import QuantScheme
+from mround_b200.schemes import QuantScheme, ScaleInit, Symmetry
 
 __all__ = ["BlockTuner", "Member", "QuantizedLayer", "TunableLayer", "piece_bounds"]
 
@@ -50,7 +52,8 @@ class QuantizedLayer:
     """One committed layer, already in MLX's stored form.
 
     ``packed`` uint32 words (held as int32) (out, in*bits/32), ``scales`` and
-    ``biases`` bf16 (out, n_groups), ``codes`` uint8 (out, in) when kept.
+    ``biases`` bf16 (out, n_groups), ``codes`` (out, in) when kept: uint8, or
+    int8 under a symmetric scheme.
     """
 
     packed: torch.Tensor
@@ -71,7 +74,13 @@ class Member:
 
 
 class TunableLayer:
-    """V / alpha / beta of one fused weight and the operands derived from them."""
+    """V / alpha / beta of one fused weight and the operands derived from them.
+
+    Members of one fused weight share the run's symmetry and scale
+    initialisation; their widths may differ.  Under a searched scheme
+    ``init_scale`` holds each group's searched scale (set by
+    ``BlockTuner.search``) and the operand is formed only once it is set.
+    """
 
     def __init__(self, layer: FusedLinear, members: list[Member], eps: float) -> None:
         self.layer = layer
@@ -82,10 +91,17 @@ class TunableLayer:
         if len(groups) != 1:
             raise ValueError("members of one fused weight must share a group size")
         self.group = groups.pop()
+        kinds = {(m.scheme.symmetry, m.scheme.scale_init) for m in members}
+        if len(kinds) != 1:
+            raise ValueError("members of one fused weight must share symmetry and scale_init")
+        symmetry, scale_init = kinds.pop()
+        self.symmetric = symmetry is Symmetry.SYMMETRIC
+        self.searched = scale_init is ScaleInit.SEARCHED
         dev = layer.w.device
         self.v = torch.zeros((out, inn), dtype=torch.float32, device=dev)
         self.alpha = torch.ones((out, inn // self.group), dtype=torch.float32, device=dev)
         self.beta = torch.ones_like(self.alpha)
+        self.init_scale = torch.zeros_like(self.alpha) if self.searched else None
         tuned_rows = sum(m.rows[1] - m.rows[0] for m in members)
         if tuned_rows == out:
             layer.wq_hi = torch.empty_like(layer.w)
@@ -94,11 +110,17 @@ class TunableLayer:
             layer.wq_hi = layer.w.clone()
             layer.wq_lo = torch.zeros_like(layer.w)
         layer.grad = torch.empty((out, inn), dtype=torch.float32, device=dev)
-        self.requantize()
+        if not self.searched:
+            self.requantize()
 
     def _slices(self, m: Member):
         r0, r1 = m.rows
         return (self.layer.w[r0:r1], self.v[r0:r1], self.alpha[r0:r1], self.beta[r0:r1])
+
+    def _scheme_kw(self, m: Member) -> dict:
+        r0, r1 = m.rows
+        return {"symmetric": self.symmetric,
+                "init_scale": None if self.init_scale is None else self.init_scale[r0:r1]}
 
     def requantize(self) -> None:
         """K1 on every member: refresh the operand from the current parameters."""
@@ -106,7 +128,8 @@ class TunableLayer:
             w, v, a, b = self._slices(m)
             r0, r1 = m.rows
             kernels.fq_forward(w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps,
-                               wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1])
+                               wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1],
+                               **self._scheme_kw(m))
 
     def update(self, step: int, iters: int) -> None:
         """K2 on every member with the linearly decayed rate of this step."""
@@ -117,7 +140,8 @@ class TunableLayer:
             lo, hi = m.scheme.coefficient_bounds
             kernels.ste_signsgd(self.layer.grad[r0:r1], w, v, a, b, bits=m.scheme.bits,
                                 group=m.group, eps=self.eps, lr=lr, lo=lo, hi=hi, update=True,
-                                wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1])
+                                wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1],
+                                **self._scheme_kw(m))
 
     def gradients(self) -> dict[str, tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         """K2 without the update: (gV, galpha, gbeta) per member, from ``layer.grad``."""
@@ -128,11 +152,12 @@ class TunableLayer:
             gv, ga, gb = torch.empty_like(v), torch.empty_like(a), torch.empty_like(b)
             kernels.ste_signsgd(self.layer.grad[r0:r1], w, v, a, b, bits=m.scheme.bits,
                                 group=m.group, eps=self.eps, lr=0.0, lo=0.0, hi=1.0, update=False,
-                                gv=gv, galpha=ga, gbeta=gb)
+                                gv=gv, galpha=ga, gbeta=gb, **self._scheme_kw(m))
             out[m.path] = (gv, ga, gb)
         return out
 
-    def load(self, path: str, v: torch.Tensor, alpha: torch.Tensor, beta: torch.Tensor) -> None:
+    def load(self, path: str, v: torch.Tensor, alpha: torch.Tensor, beta: torch.Tensor,
+             init_scale: torch.Tensor | None = None) -> None:
         """Set one member's parameters (used by parity tests and resume)."""
         for m in self.members:
             if m.path == path:
@@ -140,6 +165,10 @@ class TunableLayer:
                 self.v[r0:r1].copy_(v)
                 self.alpha[r0:r1].copy_(alpha)
                 self.beta[r0:r1].copy_(beta)
+                if init_scale is not None:
+                    if self.init_scale is None:
+                        raise ValueError(f"{path} does not use a searched scale")
+                    self.init_scale[r0:r1].copy_(init_scale)
         self.requantize()
 
     def reset(self) -> None:
@@ -156,10 +185,12 @@ class TunableLayer:
         for m in self.members:
             w, v, a, b = self._slices(m)
             r0, r1 = m.rows
+            kw = self._scheme_kw(m)
             packed, scales, biases, codes = kernels.pack_mlx(
-                w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps, want_codes=keep_codes)
+                w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps, want_codes=keep_codes,
+                **kw)
             kernels.fq_forward(w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps,
-                               wq_hi=committed[r0:r1])
+                               wq_hi=committed[r0:r1], **kw)
             out[m.path] = QuantizedLayer(packed.cpu(), scales.cpu(), biases.cpu(), m.scheme,
                                          (r1 - r0, w.shape[1]),
                                          None if codes is None else codes.cpu())
@@ -197,8 +228,53 @@ class BlockTuner:
                 if dist.world > 1:
                     layer.grad_ready.append(self._reduce_hook)
         self.ws = kernels.LossWorkspace(block.device)
+        self.importance: dict[str, torch.Tensor] = {}  # per fused layer, after search()
         self._pending: dict[int, object] = {}
         self._last_piece = True
+
+    # ------------------------------------------------------------ search
+    def search(self, inputs: list[torch.Tensor]) -> float:
+        """The v2 scale search for every searched member (reference
+        ``QuantizationRunner._search_scales``, mround/pipeline/runner.py:712-760).
+
+        One forward per calibration batch through the ORIGINAL weights collects
+        each fused weight's importance (summed squared input per channel,
+        runner.py:346-363, summed over all ranks' shards), then K8 searches every
+        searched member at its own width.  Returns the seconds spent (0.0 when
+        nothing searches).
+        """
+        searching = [t for t in self.tunables if t.searched]
+        if not searching:
+            return 0.0
+        torch.cuda.synchronize(self.block.device)
+        started = time.perf_counter()
+        stash = {}
+        collect = {}
+        for t in self.tunables:
+            layer = t.layer
+            stash[layer.name] = (layer.wq_hi, layer.wq_lo)
+            layer.use_dense()
+        for t in searching:
+            collect[t.layer.name] = torch.zeros(t.layer.in_features, dtype=torch.float32,
+                                                device=self.block.device)
+        try:
+            with torch.no_grad():
+                for x in inputs:
+                    self.block.forward_fused(x, self.precision, False, collect)
+        finally:
+            for t in self.tunables:
+                t.layer.wq_hi, t.layer.wq_lo = stash[t.layer.name]
+        for name in sorted(collect):
+            self.dist.all_reduce_(collect[name])
+        self.importance = collect
+        for t in searching:
+            for m in t.members:
+                r0, r1 = m.rows
+                search_scales(t.layer.w[r0:r1], m.scheme, importance=collect[t.layer.name],
+                              out=t.init_scale[r0:r1])
+            t.requantize()
+        torch.cuda.synchronize(self.block.device)
+        return time.perf_counter() - started
 
     # ------------------------------------------------------------ pieces
     def _reduce_hook(self, layer: FusedLinear) -> None:

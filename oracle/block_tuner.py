@@ -45,12 +45,40 @@ def _clip_ste(x, lo, hi):
     return through + (torch.clamp(x, lo, hi) - through).detach()
 
 
-def fake_quant_ste(w, v, alpha, beta, bits, group, eps=1e-8):
-    """Differentiable asymmetric fake quantization of w (out, in) float32."""
+def _clamp_magnitude(s, eps):
+    """sign(s) * max(|s|, eps), sign(0) = +1 (mround/core/quantizer.py:216-225)."""
+    sign = torch.sign(s).detach()
+    sign = torch.where(sign == 0, torch.ones_like(sign), sign)
+    return sign * torch.clamp(s.abs(), min=eps)
+
+
+def fake_quant_ste(w, v, alpha, beta, bits, group, eps=1e-8, *, symmetric=False, init_scale=None):
+    """Differentiable fake quantization of w (out, in) float32.
+
+    Asymmetric (default), symmetric observed range (``symmetric``) or
+    searched (``init_scale``, (out, in/group)): mround/core/quantizer.py:
+    228-266, 319-347.
+    """
     rows, cols = w.shape
     g = w.view(rows, cols // group, group)
     a = alpha.view(rows, cols // group, 1)
     b = beta.view(rows, cols // group, 1)
+    if symmetric or init_scale is not None:
+        maxq = float(2 ** (bits - 1))
+        if init_scale is not None:
+            s = init_scale.view(rows, cols // group, 1) * b
+        else:
+            gmax = g.amax(-1, keepdim=True)
+            gmin = g.amin(-1, keepdim=True)
+            pos_mag = torch.where(gmax > 0, gmax, torch.zeros_like(gmax)) * a
+            neg_mag = -(torch.where(gmin < 0, gmin, torch.zeros_like(gmin)) * b)
+            pos = (pos_mag >= neg_mag).detach()
+            dominant = torch.where(pos, pos_mag, neg_mag)
+            s = torch.where(pos, -dominant, dominant) / maxq
+        scale = _clamp_magnitude(s, eps)
+        raw = g / scale + v.view(g.shape)
+        codes = _clip_ste(_round_ste(raw), -maxq, maxq - 1.0)
+        return (scale * codes).view(rows, cols)
     maxq = float(2**bits - 1)
     gmax = g.amax(-1, keepdim=True)
     gmin = g.amin(-1, keepdim=True)
@@ -101,8 +129,11 @@ class OracleBlock:
     ``committed[path]`` (if set) replaces the weight by a given tensor.
     """
 
-    def __init__(self, arch, block_params, bits: dict[str, int], group: int):
+    def __init__(self, arch, block_params, bits: dict[str, int], group: int, *,
+                 symmetric: bool = False, init_scales: dict[str, torch.Tensor] | None = None):
         self.arch = arch
+        self.symmetric = symmetric
+        self.init_scales = init_scales
         self.w = {p: t.float() for p, t in block_params.linears.items()}
         self.b = {p: t.float() for p, t in block_params.biases.items()}
         self.n_in = block_params.input_norm.float()
@@ -125,7 +156,9 @@ class OracleBlock:
         if params is None:
             return self.w[p]
         v, a, b = params[p]
-        return fake_quant_ste(self.w[p], v, a, b, self.bits[p], self.group)
+        init = None if self.init_scales is None else self.init_scales[p]
+        return fake_quant_ste(self.w[p], v, a, b, self.bits[p], self.group,
+                              symmetric=self.symmetric, init_scale=init)
 
     def forward(self, x, params=None):
         ar = self.arch
@@ -179,21 +212,26 @@ def tune_block(block: OracleBlock, inputs, targets, *, iters: int, lr0: float, s
     step_losses, recorded = [], None
     t0 = time.perf_counter()
     ran = 0
+    def grad_of(t):
+        # a parameter that does not reach the loss (alpha under a searched
+        # scale) has no gradient: sign(0) = 0 leaves it in place
+        return t.grad if t.grad is not None else torch.zeros_like(t)
+
     for step in range(iters):
         leaves = {p: tuple(t.clone().requires_grad_(True) for t in params[p]) for p in params}
         loss, _ = loss_fn(block.forward(inputs[step % nb], leaves), targets[step % nb], suppress)
         loss.backward()
-        step_losses.append(float(loss))
+        step_losses.append(float(loss.detach()))
         if record_grads_at == step:
-            recorded = {p: tuple(t.grad.clone() for t in leaves[p]) for p in leaves}
+            recorded = {p: tuple(grad_of(t).clone() for t in leaves[p]) for p in leaves}
             recorded["__loss__"] = float(loss)
         lr = lr0 * (1.0 - step / iters)
         lr32 = torch.tensor(lr, dtype=torch.float32)
         new = {}
         for p, (v, a, b) in leaves.items():
-            nv = torch.clamp(v.detach() - lr32 * torch.sign(v.grad), -V_BOUND, V_BOUND)
-            na = torch.clamp(a.detach() - lr32 * torch.sign(a.grad), lo, hi)
-            nb_ = torch.clamp(b.detach() - lr32 * torch.sign(b.grad), lo, hi)
+            nv = torch.clamp(v.detach() - lr32 * torch.sign(grad_of(v)), -V_BOUND, V_BOUND)
+            na = torch.clamp(a.detach() - lr32 * torch.sign(grad_of(a)), lo, hi)
+            nb_ = torch.clamp(b.detach() - lr32 * torch.sign(grad_of(b)), lo, hi)
             new[p] = (nv, na, nb_)
         params = new
         ran += 1

@@ -74,10 +74,17 @@ def bf16_to_f32(bits16: np.ndarray) -> np.ndarray:
     return (np.asarray(bits16, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
 
 
-def to_affine(scale: np.ndarray, zp: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
-    """Asymmetric MLX affine parameters as bf16 bit patterns ``(scales, biases)``."""
+def to_affine(scale: np.ndarray, zp, bits: int | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """MLX affine parameters as bf16 bit patterns ``(scales, biases)``.
+
+    ``zp`` None means a symmetric scheme: the fixed offset ``2**(bits-1)``
+    (reference ``mround/formats/mlx_export.py:186-194``).
+    """
     s_bits = bf16_bits(scale)
     s = bf16_to_f32(s_bits)
-    z = bf16_to_f32(bf16_bits(zp))
+    if zp is None:
+        z = np.float32(2 ** (bits - 1))
+    else:
+        z = bf16_to_f32(bf16_bits(zp))
     prod = ((-s) * z).astype(np.float32)  # exact: two 8-bit significands
     return s_bits, bf16_bits(prod)

@@ -27,7 +27,8 @@ from mround.reference import losses as ref_losses
 from mround.reference import optimizer as ref_opt
 from mround.reference import packing as ref_pack
 from mround.reference import quantize as ref_quant
-from mround.schemes import QuantScheme, Symmetry
+from mround.reference import scale_search as ref_search
+from mround.schemes import QuantScheme, ScaleInit, Symmetry
 
 HERE = Path(__file__).resolve().parent
 
@@ -80,6 +81,83 @@ def quant_cases(out: dict) -> list[str]:
             out[f"{key}_galpha"] = grads.alpha.reshape(rows, ng)
             out[f"{key}_gbeta"] = grads.beta.reshape(rows, ng)
             names.append(key)
+    return names
+
+
+def sym_cases(out: dict) -> list[str]:
+    """Symmetric observed-range and searched fake-quant with gradients."""
+    names = []
+    rng = np.random.default_rng(4321)
+    for init in ("observed", "searched"):
+        for bits in (2, 3, 4, 8):
+            for group in (32, 64, 128):
+                rows, cols = 12, 256
+                w = sweep_weight(rng, rows, cols)
+                ng = cols // group
+                v = rng.uniform(-0.5, 0.5, size=(rows, cols)).astype(np.float32)
+                lo, hi = (0.5, 1.0) if init == "observed" else (0.5, 1.5)
+                a = rng.uniform(lo, hi, size=(rows, ng)).astype(np.float32)
+                b = rng.uniform(lo, hi, size=(rows, ng)).astype(np.float32)
+                gq = rng.normal(0.0, 1e-3, size=(rows, cols)).astype(np.float32)
+                scale_init = ScaleInit.SEARCHED if init == "searched" else ScaleInit.OBSERVED_RANGE
+                scheme = QuantScheme(bits=bits, group_size=group, symmetry=Symmetry.SYMMETRIC,
+                                     scale_init=scale_init)
+                init_scale = None
+                if init == "searched":
+                    # float32 search result, as the MLX pipeline hands it over
+                    init_scale = ref_search.search_scales(w.astype(np.float64), scheme).astype(np.float32)
+                params = ref_quant.QuantParams(
+                    v.astype(np.float64).reshape(rows, ng, group),
+                    a.astype(np.float64).reshape(rows, ng, 1),
+                    b.astype(np.float64).reshape(rows, ng, 1),
+                )
+                base = None if init_scale is None else init_scale.astype(np.float64)
+                res = ref_quant.fake_quantize(w.astype(np.float64), params, scheme, init_scale=base)
+                grads = ref_quant.quantize_grad(w.astype(np.float64), params, scheme,
+                                                gq.astype(np.float64), init_scale=base)
+                key = f"s{init[0]}_b{bits}_g{group}"
+                out[f"{key}_w"] = w
+                out[f"{key}_v"] = v
+                out[f"{key}_alpha"] = a
+                out[f"{key}_beta"] = b
+                out[f"{key}_gq"] = gq
+                if init_scale is not None:
+                    out[f"{key}_init"] = init_scale.reshape(rows, ng)
+                out[f"{key}_qdq"] = res.qdq
+                out[f"{key}_codes"] = res.codes.reshape(rows, cols).astype(np.int16)
+                out[f"{key}_scale"] = res.scale.reshape(rows, ng)
+                out[f"{key}_gv"] = grads.v.reshape(rows, cols)
+                out[f"{key}_galpha"] = grads.alpha.reshape(rows, ng)
+                out[f"{key}_gbeta"] = grads.beta.reshape(rows, ng)
+                names.append(key)
+    return names
+
+
+def search_cases(out: dict) -> list[str]:
+    """The scale search, unweighted and importance-weighted, plus edge groups."""
+    names = []
+    rng = np.random.default_rng(2468)
+    for bits in (2, 3, 4, 8):
+        for group in (32, 64):
+            w = bf16_round(rng.normal(size=(64, 256)).astype(np.float32) * 0.02)
+            scheme = QuantScheme(bits=bits, group_size=group)
+            key = f"srch_b{bits}_g{group}"
+            out[f"{key}_w"] = w
+            out[f"{key}_scale"] = ref_search.search_scales(w.astype(np.float64), scheme)
+            names.append(key)
+    w = bf16_round(rng.normal(size=(32, 64)).astype(np.float32))
+    imp = rng.uniform(0.1, 10.0, size=64).astype(np.float32)
+    out["srch_imp_w"], out["srch_imp_importance"] = w, imp
+    out["srch_imp_scale"] = ref_search.search_scales(
+        w.astype(np.float64), QuantScheme(bits=3, group_size=16), importance=imp.astype(np.float64))
+    edge = np.zeros((3, 16), dtype=np.float32)
+    edge[1, :] = np.linspace(-1.0, 1.0, 16, dtype=np.float32) * 0.01
+    edge[2, 3], edge[2, 9] = 0.5, -0.5  # |anchor| tie of opposite signs: first wins
+    edge = bf16_round(edge)
+    out["srch_edge_w"] = edge
+    for bits in (2, 4):
+        out[f"srch_edge_b{bits}_scale"] = ref_search.search_scales(
+            edge.astype(np.float64), QuantScheme(bits=bits, group_size=16))
     return names
 
 
@@ -236,6 +314,8 @@ def main() -> None:
     out: dict[str, np.ndarray] = {}
     names = quant_cases(out)
     out["quant_case_names"] = np.array(names)
+    out["sym_case_names"] = np.array(sym_cases(out))
+    out["search_case_names"] = np.array(search_cases(out))
     edge_cases(out)
     optimizer_case(out)
     loss_cases(out)

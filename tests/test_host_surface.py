@@ -77,12 +77,24 @@ def test_block_recipe_and_pieces():
     assert piece_bounds(2, 4) == [(0, 1), (1, 2)]
 
 
-def test_api_refuses_symmetric_and_bad_format():
+def test_api_resolves_every_scheme_and_refuses_bad_format():
     from mround_b200.api import _resolve_scheme, quantize
+    from mround_b200.schemes import ScaleInit, Symmetry
 
-    with pytest.raises(UnsupportedSchemeError):
-        _resolve_scheme(bits=4, group_size=64, symmetry="sym", average_bits=None,
-                        candidate_bits=(), remainder_bits=None, scheme=None, scale_init=None)
+    # the reference's defaults: symmetric, searched below 4 bits (api.py:116-153)
+    s4, _ = _resolve_scheme(bits=4, group_size=64, symmetry="sym", average_bits=None,
+                            candidate_bits=(), remainder_bits=None, scheme=None, scale_init=None)
+    assert s4.symmetry is Symmetry.SYMMETRIC and s4.scale_init is ScaleInit.OBSERVED_RANGE
+    s2, _ = _resolve_scheme(bits=2, group_size=64, symmetry="sym", average_bits=None,
+                            candidate_bits=(), remainder_bits=None, scheme=None, scale_init=None)
+    assert s2.scale_init is ScaleInit.SEARCHED and s2.coefficient_bounds == (0.5, 1.5)
+    mixed, widths = _resolve_scheme(bits=4, group_size=64, symmetry="sym", average_bits=2.5,
+                                    candidate_bits=(2, 3, 4), remainder_bits=None, scheme=None,
+                                    scale_init=None)
+    assert mixed.scale_init is ScaleInit.SEARCHED and widths == {2, 3, 4}
+    asym, _ = _resolve_scheme(bits=2, group_size=64, symmetry="asym", average_bits=None,
+                              candidate_bits=(), remainder_bits=None, scheme=None, scale_init=None)
+    assert asym.scale_init is ScaleInit.OBSERVED_RANGE
     with pytest.raises(UnsupportedSchemeError):
         quantize("synthetic:tiny-qwen2", output_dir="/tmp/x", export_format="gguf")
     with pytest.raises(SchemeError):
@@ -104,7 +116,12 @@ def test_cli_dry_run(capsys):
     assert main(["quantize", "synthetic:tiny-qwen2", "-o", "/tmp/x", "--bits", "2", "--asym",
                  "--dry-run"]) == 0
     assert "asym" in capsys.readouterr().out
-    assert main(["quantize", "synthetic:tiny-qwen2", "-o", "/tmp/x", "--dry-run"]) == 2
+    # the reference's default scheme: symmetric, and searched below 4 bits
+    assert main(["quantize", "synthetic:tiny-qwen2", "-o", "/tmp/x", "--dry-run"]) == 0
+    assert "observed_range" in capsys.readouterr().out
+    assert main(["quantize", "synthetic:tiny-qwen2", "-o", "/tmp/x", "--bits", "2",
+                 "--dry-run"]) == 0
+    assert "searched" in capsys.readouterr().out
 
 
 def _fake_layer(rows, cols, bits, group, seed):

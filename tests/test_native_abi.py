@@ -51,8 +51,20 @@ def test_status_maps_to_exceptions():
 def test_argument_errors_are_refused_before_any_launch():
     lib = _native.lib()
     # group 12 is not a device group: refused on the host side of the ABI
-    st = lib.mr_fq_forward(None, None, None, None, 4, 48, 12, 2, 1e-8, None, None, None, None,
-                           None, None)
+    st = lib.mr_fq_forward(None, None, None, None, 4, 48, 12, 2, 0, None, 1e-8, None, None, None,
+                           None, None, None)
     assert st == -1
-    st = lib.mr_pack_mlx(None, None, None, None, 4, 64, 64, 9, 1e-8, None, None, None, None, None)
+    st = lib.mr_pack_mlx(None, None, None, None, 4, 64, 64, 9, 0, None, 1e-8, None, None, None,
+                         None, None)
+    assert st == -1
+    # a searched scale without the symmetric flag is refused before any launch
+    buf = (ctypes.c_uint8 * 4096)()
+    p = ctypes.addressof(buf)
+    st = lib.mr_fq_forward(p, p, p, p, 4, 64, 64, 2, 0, p, 1e-8, None, None, None, None, None,
+                           None)
+    assert st == -1
+    cands = (ctypes.c_float * 1)(2.0)
+    st = lib.mr_scale_search(p, 4, 64, 12, 2, cands, 1, None, p, None)
+    assert st == -1
+    st = lib.mr_scale_search(p, 4, 64, 64, 2, cands, 0, None, p, None)
     assert st == -1
