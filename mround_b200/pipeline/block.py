@@ -79,6 +79,7 @@ class FusedLinear:
         self.grad: torch.Tensor | None = None
         self.accumulate_grad = False
         self.grad_ready: list = []  # callbacks run right after this layer's weight gradient
+        self.pending: list = []  # collectives that must finish before wq_hi/wq_lo are read
 
     @property
     def out_features(self) -> int:
@@ -89,7 +90,14 @@ class FusedLinear:
         return self.w.shape[1]
 
     def use_dense(self) -> None:
+        self.ready()
         self.wq_hi, self.wq_lo = self.w, None
+
+    def ready(self) -> None:
+        """Order the current stream after the collectives still writing the operands."""
+        for work in self.pending:
+            work.wait()
+        self.pending.clear()
 
 
 def _split(x2: torch.Tensor, want_lo: bool):
@@ -101,6 +109,7 @@ class _LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, anchor, layer: FusedLinear, prec: Precision):
+        layer.ready()
         lead = x.shape[:-1]
         x2 = x.reshape(-1, layer.in_features)
         if not x2.is_contiguous():
@@ -279,6 +288,7 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     h1 = kernels.rmsnorm_split(x2, self.input_norm, a.rms_eps)
     qkv_l = L["qkv"]
     stats("qkv", h1)
+    L["qkv"].ready()
     qkv = torch.empty((t, qkv_l.out_features), dtype=torch.float32, device=x.device)
     p = _wprec(qkv_l, prec.forward)
     _mm(h1, (qkv_l.wq_hi, qkv_l.wq_lo), qkv, m=t, n=qkv_l.out_features, k=h, a_kmajor=True,
@@ -299,18 +309,21 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     del o
     o_l = L["o"]
     stats("o", att)
+    o_l.ready()
     hres = x2.clone()
     _mm(att, (o_l.wq_hi, o_l.wq_lo), hres, m=t, n=h, k=hq * d, a_kmajor=True, b_kmajor=True,
         lda=hq * d, ldb=hq * d, prec=_wprec(o_l, prec.forward), accumulate=True)
     h2_hi, h2_lo, rstd2 = kernels.rmsnorm_split(hres, self.post_norm, a.rms_eps)
     gu_l = L["gate_up"]
     stats("gate_up", (h2_hi, h2_lo))
+    gu_l.ready()
     gu = torch.empty((t, 2 * inter), dtype=torch.float32, device=x.device)
     _mm((h2_hi, h2_lo), (gu_l.wq_hi, gu_l.wq_lo), gu, m=t, n=2 * inter, k=h, a_kmajor=True,
         b_kmajor=True, lda=h, ldb=h, prec=_wprec(gu_l, prec.forward))
     act = kernels.swiglu_split(gu, t, inter)
     dn_l = L["down"]
     stats("down", act)
+    dn_l.ready()
     out = hres.clone()
     _mm(act, (dn_l.wq_hi, dn_l.wq_lo), out, m=t, n=h, k=inter, a_kmajor=True, b_kmajor=True,
         lda=inter, ldb=inter, prec=_wprec(dn_l, prec.forward), accumulate=True)

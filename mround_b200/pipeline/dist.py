@@ -4,8 +4,10 @@ The tuning loop shards naturally over calibration sequences (the reference's
 micro-batch contract, mround/pipeline/runner.py:984-1044): rank ``r`` of ``N``
 holds sequences ``j`` with ``j % N == r`` of every batch, for both activation
 streams.  Per step the ranks exchange only (a) three 2048-bin histograms for
-the exact global outlier threshold and (b) the float32 weight gradients,
-summed so that every rank applies the same signed step.
+the exact global outlier threshold and (b) the float32 weight gradients:
+reduce-scattered by rows, each rank applying the signed step to its own rows
+and all-gathering the updated bf16 operands (or, where a weight's rows do not
+divide by the rank count, all-reduced and applied on every rank).
 
 ``DistContext`` wraps ``torch.distributed`` with a bounded timeout; with one
 rank every call is a no-op.
@@ -44,6 +46,20 @@ class DistContext:
     def all_reduce_async(self, t: torch.Tensor):
         if self.world > 1:
             return tdist.all_reduce(t, group=self.group, async_op=True)
+        return None
+
+    def reduce_scatter_async(self, out: torch.Tensor, full: torch.Tensor):
+        """Sum ``full`` over ranks; this rank receives its contiguous 1/N in ``out``."""
+        if self.world > 1:
+            return tdist.reduce_scatter_tensor(out, full, group=self.group, async_op=True)
+        out.copy_(full)
+        return None
+
+    def all_gather_async(self, full: torch.Tensor, part: torch.Tensor):
+        """Concatenate every rank's ``part`` (rank order) into ``full``."""
+        if self.world > 1:
+            return tdist.all_gather_into_tensor(full, part, group=self.group, async_op=True)
+        full.copy_(part)
         return None
 
     def barrier(self) -> None:

@@ -124,6 +124,7 @@ class TunableLayer:
 
     def requantize(self) -> None:
         """K1 on every member: refresh the operand from the current parameters."""
+        self.layer.ready()
         for m in self.members:
             w, v, a, b = self._slices(m)
             r0, r1 = m.rows
@@ -142,6 +143,24 @@ class TunableLayer:
                                 group=m.group, eps=self.eps, lr=lr, lo=lo, hi=hi, update=True,
                                 wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1],
                                 **self._scheme_kw(m))
+
+    def update_rows(self, step: int, iters: int, s0: int, s1: int, grad: torch.Tensor,
+                    hi: torch.Tensor, lo: torch.Tensor) -> None:
+        """K2 on rows [s0, s1) only: ``grad`` holds the summed gradient of those
+        rows, and the next step's operand rows go to ``hi``/``lo`` (this rank's
+        part of the all-gather).  V/alpha/beta of other rows are left as they are."""
+        for m in self.members:
+            r0, r1 = max(m.rows[0], s0), min(m.rows[1], s1)
+            if r0 >= r1:
+                continue
+            lr = m.lr0 * (1.0 - step / iters) if step < iters else 0.0
+            lo_b, hi_b = m.scheme.coefficient_bounds
+            init = None if self.init_scale is None else self.init_scale[r0:r1]
+            kernels.ste_signsgd(grad[r0 - s0:r1 - s0], self.layer.w[r0:r1], self.v[r0:r1],
+                                self.alpha[r0:r1], self.beta[r0:r1], bits=m.scheme.bits,
+                                group=m.group, eps=self.eps, lr=lr, lo=lo_b, hi=hi_b, update=True,
+                                wq_hi=hi[r0 - s0:r1 - s0], wq_lo=lo[r0 - s0:r1 - s0],
+                                symmetric=self.symmetric, init_scale=init)
 
     def gradients(self) -> dict[str, tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         """K2 without the update: (gV, galpha, gbeta) per member, from ``layer.grad``."""
@@ -172,6 +191,7 @@ class TunableLayer:
         self.requantize()
 
     def reset(self) -> None:
+        self.layer.ready()
         self.v.zero_()
         self.alpha.fill_(1.0)
         self.beta.fill_(1.0)
@@ -181,6 +201,7 @@ class TunableLayer:
         """K5 per member, then make the layer's weight bf16(reconstruction)
         (reference mround/pipeline/runner.py:775-787)."""
         out: dict[str, QuantizedLayer] = {}
+        self.layer.ready()
         committed = self.layer.w.clone()
         for m in self.members:
             w, v, a, b = self._slices(m)
@@ -231,6 +252,23 @@ class BlockTuner:
         self.importance: dict[str, torch.Tensor] = {}  # per fused layer, after search()
         self._pending: dict[int, object] = {}
         self._last_piece = True
+        # Row-sharded update: every fused weight's rows divide by the rank count,
+        # so rank r reduce-scatters the gradient, steps rows [r*R/N, (r+1)*R/N)
+        # and all-gathers the operands; otherwise all-reduce and step everywhere.
+        self.sharded = dist.world > 1 and all(t.layer.out_features % dist.world == 0
+                                              for t in self.tunables)
+        self._sharded_step = False
+        self._dirty = False  # V/alpha/beta rows of other ranks are stale
+        self._shards: dict[int, tuple[int, int, torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+        if self.sharded:
+            for t in self.tunables:
+                out, inn = t.layer.w.shape
+                per = out // dist.world
+                s0, s1 = dist.rank * per, (dist.rank + 1) * per
+                grad = torch.empty((per, inn), dtype=torch.float32, device=block.device)
+                # untuned rows of a partly tuned fused weight keep their exact operand
+                self._shards[id(t.layer)] = (s0, s1, grad, t.layer.wq_hi[s0:s1].clone(),
+                                             t.layer.wq_lo[s0:s1].clone())
 
     # ------------------------------------------------------------ search
     def search(self, inputs: list[torch.Tensor]) -> float:
@@ -278,8 +316,44 @@ class BlockTuner:
 
     # ------------------------------------------------------------ pieces
     def _reduce_hook(self, layer: FusedLinear) -> None:
-        if self._last_piece:
+        if not self._last_piece:
+            return
+        if self._sharded_step:
+            _, _, grad, _, _ = self._shards[id(layer)]
+            self._pending[id(layer)] = self.dist.reduce_scatter_async(grad, layer.grad)
+        else:
             self._pending[id(layer)] = self.dist.all_reduce_async(layer.grad)
+
+    def _update(self, step: int, iters: int) -> None:
+        """The signed step of every tunable after the backward."""
+        if not self._sharded_step:
+            for t in self.tunables:
+                self._wait(t.layer)
+                t.update(step, iters)
+            return
+        # rows of this rank, then the operands' all-gather; qkv first, so the
+        # next forward's first GEMM waits on the smallest gather only
+        for t in self.tunables:
+            self._wait(t.layer)
+            s0, s1, grad, hi, lo = self._shards[id(t.layer)]
+            t.update_rows(step, iters, s0, s1, grad, hi, lo)
+            t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_hi, hi))
+            t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_lo, lo))
+        self._dirty = True
+
+    def sync_params(self) -> None:
+        """Make V/alpha/beta whole on every rank after row-sharded steps."""
+        if not self._dirty:
+            return
+        for t in self.tunables:
+            t.layer.ready()
+            s0, s1, _, _, _ = self._shards[id(t.layer)]
+            works = [self.dist.all_gather_async(buf, buf[s0:s1].clone())
+                     for buf in (t.v, t.alpha, t.beta)]
+            for w in works:
+                if w is not None:
+                    w.wait()
+        self._dirty = False
 
     def _wait(self, layer: FusedLinear) -> None:
         work = self._pending.pop(id(layer), None)
@@ -330,6 +404,7 @@ class BlockTuner:
 
     def step(self, x: torch.Tensor, target: torch.Tensor, step: int, iters: int) -> torch.Tensor:
         """One signed-gradient step on one batch; returns this rank's loss share."""
+        self._sharded_step = self.sharded
         bounds = piece_bounds(x.shape[0], self.pieces)
         if len(bounds) == 1:
             self._last_piece = True
@@ -358,13 +433,13 @@ class BlockTuner:
                 del out
                 self.block.backward_fused(saved, grad, self.precision)
                 del saved
-        for t in self.tunables:
-            self._wait(t.layer)
-            t.update(step, iters)
+        self._update(step, iters)
+        self._sharded_step = False
         return loss
 
     def gradient_only(self, x: torch.Tensor, target: torch.Tensor):
         """Forward, loss and backward without a step; returns (loss, grads by path)."""
+        self.sync_params()
         self._last_piece = True
         for t in self.tunables:
             t.layer.accumulate_grad = False
@@ -381,11 +456,14 @@ class BlockTuner:
     def reset(self) -> None:
         for t in self.tunables:
             t.reset()
+        self._dirty = False
 
     def snapshot(self) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+        self.sync_params()
         return [(t.v.clone(), t.alpha.clone(), t.beta.clone()) for t in self.tunables]
 
     def commit(self, keep_codes: bool = False) -> dict[str, QuantizedLayer]:
+        self.sync_params()
         out: dict[str, QuantizedLayer] = {}
         for t in self.tunables:
             out.update(t.commit(keep_codes))

@@ -5,6 +5,8 @@
 - Per-rank weight gradients summed by an all-reduce give every rank the same
   signed step, equal to the single-process step on the whole batch.
 - Loss shares divided by the global element count sum to the batch loss.
+- The row-sharded exchange (reduce-scatter of the gradient by rows, each rank
+  stepping its own rows, all-gather of the result) equals the replicated step.
 """
 
 from __future__ import annotations
@@ -61,7 +63,18 @@ def _worker(rank, world, port, q):
         ones = np.ones((8, 1), np.float32)
         gv, ga, gb = Q.ste_grads(w, np.zeros_like(w), ones, ones, g_local.numpy(), 2, 64)
         v1, a1, b1 = Q.signsgd_step(np.zeros_like(w), ones, ones, gv, ga, gb, 0.005, 0.1, 1.0)
-        q.put((rank, float(thr), float(t.item()), v1, a1, b1))
+        # (4) row-sharded: reduce-scatter rows, step own rows, all-gather V
+        per = w.shape[0] // world
+        r0, r1 = rank * per, (rank + 1) * per
+        g_rows = torch.empty((per, w.shape[1]), dtype=torch.float32)
+        work = ctx.reduce_scatter_async(g_rows, torch.from_numpy(np.ascontiguousarray(g_full[ctx.shard(4)].sum(0))))
+        work.wait()
+        o = ones[r0:r1]
+        gvr, gar, gbr = Q.ste_grads(w[r0:r1], np.zeros_like(w[r0:r1]), o, o, g_rows.numpy(), 2, 64)
+        vr, _, _ = Q.signsgd_step(np.zeros_like(w[r0:r1]), o, o, gvr, gar, gbr, 0.005, 0.1, 1.0)
+        v_sharded = torch.empty(w.shape, dtype=torch.float32)
+        ctx.all_gather_async(v_sharded, torch.from_numpy(np.ascontiguousarray(vr))).wait()
+        q.put((rank, float(thr), float(t.item()), v1, a1, b1, v_sharded.numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -88,10 +101,11 @@ def test_two_rank_exchange_matches_single_process():
     ones = np.ones((8, 1), np.float32)
     gv, ga, gb = Q.ste_grads(w, np.zeros_like(w), ones, ones, g_full.sum(0), 2, 64)
     v_want, _, _ = Q.signsgd_step(np.zeros_like(w), ones, ones, gv, ga, gb, 0.005, 0.1, 1.0)
-    for rank, thr, loss, v1, a1, b1 in results:
+    for rank, thr, loss, v1, a1, b1, v_sharded in results:
         assert thr == want_thr, "histogram exchange gives the exact global order statistic"
         assert loss == pytest.approx(want_loss, rel=1e-12)
         assert np.array_equal(v1, v_want)
+        assert np.array_equal(v_sharded, v_want), "row-sharded step equals the replicated one"
     assert np.array_equal(results[0][3], results[1][3])
     assert np.array_equal(results[0][4], results[1][4])
 

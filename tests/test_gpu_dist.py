@@ -1,12 +1,13 @@
 """Data-parallel step on 2 GPUs (NCCL) against one process on the whole batch.
 
 Each rank holds half the sequences of the batch; the threshold comes from
-all-reduced histograms, the weight gradients from an all-reduce, and every
-rank applies the same K2 step.  Against a single-process step on the whole
+all-reduced histograms, the weight gradients are reduce-scattered by rows,
+each rank steps its rows and the operands are all-gathered for the next step
+(two steps run).  Against a single-process step on the whole
 batch: the loss agrees to float64 summation order and the exact outlier
-threshold is identical; V after the step agrees except where a gradient's
+threshold is identical; V after the steps agrees except where a gradient's
 sign flips between two summation orders (bounded here at 0.1 % of entries);
-and the two ranks hold bitwise identical parameters.  Skipped with fewer
+and the two ranks hold bitwise identical parameters once gathered.  Skipped with fewer
 than two GPUs.
 """
 
@@ -73,11 +74,15 @@ def _rank(rank, world, port, q):
         _, block, x, tgt = _setup(dev)
         rows = ctx.shard(SHAPE[0])
         tuner = _tuner(block, ctx)
+        assert tuner.sharded, "tiny-qwen2's fused rows divide by 2: the row-sharded update runs"
         loss = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 0, 10)
-        total = loss.clone()
+        # a second step runs on the all-gathered operands of the first
+        loss2 = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 1, 10)
+        tuner.sync_params()
+        total = torch.stack([loss, loss2])
         ctx.all_reduce_(total)
         torch.cuda.synchronize(dev)
-        q.put((rank, float(total.item()), float(tuner.ws.thr.item()),
+        q.put((rank, total.tolist(), float(tuner.ws.thr.item()),
                [t.v.cpu().numpy() for t in tuner.tunables],
                [t.alpha.cpu().numpy() for t in tuner.tunables]))
         tdist.barrier()
@@ -105,9 +110,11 @@ def test_two_gpu_step_matches_single_process():
     _, block, x, tgt = _setup(dev)
     tuner = _tuner(block, DistContext())
     loss = tuner.step(x.to(dev), tgt.to(dev), 0, 10)
+    loss2 = tuner.step(x.to(dev), tgt.to(dev), 1, 10)
     torch.cuda.synchronize(dev)
     want_v = [t.v.cpu().numpy() for t in tuner.tunables]
-    assert res[0][1] == pytest.approx(loss.item(), rel=1e-6)
+    assert res[0][1][0] == pytest.approx(loss.item(), rel=1e-6)
+    assert res[0][1][1] == pytest.approx(loss2.item(), rel=1e-4)
     assert res[0][2] == tuner.ws.thr.item()
     for a, b in zip(res[0][3], res[1][3]):
         assert np.array_equal(a, b), "ranks must hold identical parameters"
