@@ -235,7 +235,8 @@ int mr_scale_search(const uint16_t* w_bf16, int64_t rows, int64_t cols, int grou
  * Importance statistics for the searched scale: out[c] += sum_r x[r, c]^2
  * over rows of a float32 activation given as its bf16 parts (x = hi + lo;
  * lo may be NULL).  Replaces the collection mode of _TunableLinear.__call__
- * (mround/pipeline/runner.py:359-363).  Float32 accumulation; cols a multiple
+ * (mround/pipeline/runner.py:359-363).  Float32 accumulation in a fixed order
+ * (no atomics: the result is reproducible); cols a multiple
  * of 8, pointers 16-byte aligned.
  */
 int mr_colsumsq_split(const uint16_t* hi, const uint16_t* lo, int64_t rows, int64_t cols,

@@ -8,18 +8,23 @@
 // lo*hi into one TMEM accumulator, precision 2 hi*hi + lo*hi (B exact in
 // bf16), precision 1 hi*hi.
 //
-// Structure (one 128 x BN output tile per CTA, 128 threads):
+// Structure: a persistent kernel, one CTA (192 threads) per SM, walking the
+// flattened (batch, M-tile, N-tile) list of 128 x BN output tiles with stride
+// gridDim.x (grouped rasterization: 16 M-tiles share each sweep over N):
 //   warp 0, one lane : TMA producer.  Loads 64-wide K slices of A and B (hi
 //                      and lo parts) into a ring of shared-memory stages with
-//                      128-byte swizzle; completion is tracked by the
-//                      stage's "full" mbarrier (transaction bytes).
-//   warp 1           : allocates the TMEM accumulator (BN columns); one lane
-//                      issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K
-//                      step and per product, then tcgen05.commit to the
-//                      stage's "empty" mbarrier so the producer can refill it.
-//   warps 0-3        : epilogue.  After the final commit, each warp reads its
-//                      32 TMEM lanes (rows) with tcgen05.ld 32x32b.x32, adds
-//                      bias / the previous C, and stores float32 rows.
+//                      128-byte swizzle, continuing across tiles; completion is
+//                      tracked by the stage's "full" mbarrier (transaction bytes).
+//   warp 1           : allocates two TMEM accumulators (2 x BN columns); one
+//                      lane issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K
+//                      step and per product into accumulator (tile & 1),
+//                      tcgen05.commit to the stage's "empty" mbarrier so the
+//                      producer can refill it, and to "tmem_full" at tile end.
+//   warps 2-5        : epilogue.  Each warp reads the 32 TMEM lanes (rows) it
+//                      may access with tcgen05.ld 32x32b.x32, adds bias / the
+//                      previous C, stores float32 rows, and arrives on
+//                      "tmem_empty" -- while the MMAs of the next tile run in
+//                      the other accumulator.
 // Operand majorness: K-major tiles are TMA boxes {64 (K), rows}; MN-major
 // tiles are boxes {64 (M or N), 64 (K)}, one per 64-wide MN chunk.  The UMMA
 // shared-memory descriptors describe the canonical SWIZZLE_128B layouts of
@@ -40,7 +45,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
 __device__ int g_gemm_status = 0;
@@ -188,6 +193,7 @@ struct Cfg {
   static constexpr int kStage = kA * kAParts + kB * kBParts;
   static constexpr int kStages = (200 * 1024) / kStage > 4 ? 4 : (200 * 1024) / kStage;
   static constexpr int kSmem = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+  static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
 };
 
 struct Maps {
@@ -215,179 +221,258 @@ __device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int ro
                 : smem_desc(base + kstep * 2048, 64 * BK * 2, 1024);
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One output tile of the flattened (batch, M-tile, N-tile) space and its K range.
+struct Tile {
+  int m0, n0, z;
+  int kt_end;    // K-tiles [0, kt_end) are visited (fewer under causal mode 2)
+  int n_active;  // K-tiles that issue MMAs (0: the tile is written as zeros)
+  bool skip;     // causal mode 1: the tile lies wholly above the diagonal, not written
+};
+
+struct Shape {
+  int m, n, k, m_tiles, n_tiles, k_tiles, causal, clen;
+};
+
+// Causal attention products (rows of a batch entry stack heads of clen
+// positions; a 128-row tile lies within one head because clen % 128 == 0):
+//  1: C = Q K^T or dO V^T -- tiles wholly above the diagonal are skipped;
+//  2: C = P V or dS K     -- K (key positions) stops after the tile's last row;
+//  3: C = dS^T Q or P^T dO -- K-tiles whose rows all precede the tile's first
+//     key are skipped.
+__device__ __forceinline__ bool k_active(const Shape& sh, int m0, int kt) {
+  return sh.causal != 3 || ((kt * BK) % sh.clen) + BK - 1 >= m0;
+}
+
+// Grouped rasterization inside each batch entry: 16 M-tiles share a sweep over N.
+template <int BN>
+__device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
+  constexpr int G = 16;
+  const int per_batch = sh.m_tiles * sh.n_tiles;
+  Tile tl;
+  tl.z = t / per_batch;
+  const int tt = t - tl.z * per_batch;
+  const int group = tt / (G * sh.n_tiles);
+  const int first_m = group * G;
+  const int gm = min(G, sh.m_tiles - first_m);
+  const int r = tt - group * G * sh.n_tiles;
+  tl.m0 = (first_m + r % gm) * BM;
+  tl.n0 = (r / gm) * BN;
+  tl.kt_end = sh.k_tiles;
+  tl.skip = sh.causal == 1 && tl.n0 > (tl.m0 % sh.clen) + BM - 1;
+  if (sh.causal == 2) tl.kt_end = min(sh.k_tiles, ((tl.m0 % sh.clen) + BM + BK - 1) / BK);
+  if (tl.skip) tl.kt_end = 0;
+  tl.n_active = tl.kt_end;
+  if (sh.causal == 3) {
+    tl.n_active = 0;
+    for (int kt = 0; kt < tl.kt_end; ++kt) tl.n_active += k_active(sh, tl.m0, kt) ? 1 : 0;
+  }
+  return tl;
+}
+
+// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
+// Roles (192 threads):
+//   warp 0, one lane : TMA producer over the shared-memory ring, continuing
+//                      across tiles.
+//   warp 1           : allocates 2 x BN TMEM columns (two accumulators); one
+//                      lane issues the tile's MMAs into accumulator (j & 1)
+//                      and commits to tmem_full[j & 1].
+//   warps 2-5        : epilogue of tile j from accumulator (j & 1) while the
+//                      MMAs of tile j + 1 run in the other; each warp reads the
+//                      32 TMEM lanes (warp % 4) it may access, stores float32
+//                      rows, then arrives on tmem_empty[j & 1].
 template <int BN, int PREC>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
                 int64_t stride_c, const float* __restrict__ bias, int accumulate, int m, int n,
-                int k, int a_kmajor, int b_kmajor, int causal, int clen) {
+                int k, int a_kmajor, int b_kmajor, int causal, int clen, int total_tiles) {
   using C = Cfg<BN, PREC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStage);
   uint64_t* empty = full + C::kStages;
-  uint64_t* done = empty + C::kStages;
+  uint64_t* tmem_full = empty + C::kStages;  // [2]
+  uint64_t* tmem_empty = tmem_full + 2;      // [2]
+  uint64_t* done = tmem_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // grouped rasterization: 16 M-tiles share each sweep over N
-  const int m_tiles = (m + BM - 1) / BM;
-  const int n_tiles = (n + BN - 1) / BN;
-  constexpr int G = 16;
-  const int tile = blockIdx.x;
-  const int group = tile / (G * n_tiles);
-  const int first_m = group * G;
-  const int gm = min(G, m_tiles - first_m);
-  const int tm = first_m + (tile % (G * n_tiles)) % gm;
-  const int tn = (tile % (G * n_tiles)) / gm;
-  const int m0 = tm * BM;
-  const int n0 = tn * BN;
-  const int k_tiles = (k + BK - 1) / BK;
-  const int z = blockIdx.y;  // batch index
-  c += int64_t(z) * stride_c;
-
-  // Causal attention products (rows of a batch entry stack heads of clen
-  // positions; a 128-row tile lies within one head because clen % 128 == 0):
-  //  1: C = Q K^T or dO V^T -- tiles wholly above the diagonal are skipped;
-  //  2: C = P V or dS K     -- K (key positions) stops after the tile's last row;
-  //  3: C = dS^T Q or P^T dO -- K-tiles whose rows all precede the tile's first
-  //     key are skipped.
-  int kt_end = k_tiles;
-  bool skip_tile = false;
-  if (causal == 1) skip_tile = n0 > (m0 % clen) + BM - 1;
-  if (causal == 2) kt_end = min(k_tiles, ((m0 % clen) + BM + BK - 1) / BK);
-  if (skip_tile) kt_end = 0;
-  auto active = [&](int kt) { return causal != 3 || ((kt * BK) % clen) + BK - 1 >= m0; };
-  int n_active = 0;
-  for (int kt = 0; kt < kt_end; ++kt) n_active += active(kt) ? 1 : 0;
+  Shape sh;
+  sh.m = m; sh.n = n; sh.k = k;
+  sh.m_tiles = (m + BM - 1) / BM;
+  sh.n_tiles = (n + BN - 1) / BN;
+  sh.k_tiles = (k + BK - 1) / BK;
+  sh.causal = causal;
+  sh.clen = clen;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 4);  // one arrival per epilogue warp
+    }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a_hi)));
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b_hi)));
   }
-  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------ producer
-    int it = 0;
-    for (int kt = 0; kt < kt_end && ok; ++kt) {
-      if (!active(kt)) continue;
-      const int s = it % C::kStages;
-      const uint32_t round = it / C::kStages;
-      if (it >= C::kStages) ok = mbar_wait(&empty[s], (round - 1) & 1);
-      ++it;
-      if (!ok) break;
-      uint8_t* st = smem + s * C::kStage;
-      mbar_expect_tx(&full[s], C::kStage);
-      const int k0 = kt * BK;
-      load_part<BM>(st, &maps.a_hi, &full[s], a_kmajor, m0, k0, z);
-      if (C::kAParts == 2) load_part<BM>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, m0, k0, z);
-      uint8_t* sb = st + C::kA * C::kAParts;
-      load_part<BN>(sb, &maps.b_hi, &full[s], b_kmajor, n0, k0, z);
-      if (C::kBParts == 2) load_part<BN>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, n0, k0, z);
-    }
-    if (!ok) {
-      // let issued copies land before the CTA exits (bounded)
-      for (int s = 0; s < C::kStages; ++s) {
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(&full[s], 0) && !mbar_try_wait(&full[s], 1) &&
-               globaltimer() - t0 < kWaitLimitNs / 4) {
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ producer
+      bool ok = true;
+      int it = 0;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const Tile tl = tile_at<BN>(sh, t);
+        for (int kt = 0; kt < tl.kt_end; ++kt) {
+          if (!k_active(sh, tl.m0, kt)) continue;
+          const int s = it % C::kStages;
+          const uint32_t round = it / C::kStages;
+          if (it >= C::kStages) ok = mbar_wait(&empty[s], (round - 1) & 1);
+          if (!ok) break;
+          ++it;
+          uint8_t* st = smem + s * C::kStage;
+          mbar_expect_tx(&full[s], C::kStage);
+          const int k0 = kt * BK;
+          load_part<BM>(st, &maps.a_hi, &full[s], a_kmajor, tl.m0, k0, tl.z);
+          if (C::kAParts == 2)
+            load_part<BM>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, tl.m0, k0, tl.z);
+          uint8_t* sb = st + C::kA * C::kAParts;
+          load_part<BN>(sb, &maps.b_hi, &full[s], b_kmajor, tl.n0, k0, tl.z);
+          if (C::kBParts == 2)
+            load_part<BN>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, tl.n0, k0, tl.z);
+        }
+      }
+      if (!ok) {
+        // let issued copies land before the CTA exits (bounded)
+        for (int s = 0; s < C::kStages; ++s) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full[s], 0) && !mbar_try_wait(&full[s], 1) &&
+                 globaltimer() - t0 < kWaitLimitNs / 4) {
+          }
         }
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------------------------ MMA issuer
-    const uint32_t idesc = instr_desc(BN, !a_kmajor, !b_kmajor);
-    int it = 0;
-    for (int kt = 0; kt < kt_end; ++kt) {
-      if (!active(kt)) continue;
-      const int s = it % C::kStages;
-      ok = mbar_wait(&full[s], (it / C::kStages) & 1);
-      if (!ok) break;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      const uint32_t idesc = instr_desc(BN, !a_kmajor, !b_kmajor);
+      bool ok = true;
+      int it = 0, j = 0;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++j) {
+        const Tile tl = tile_at<BN>(sh, t);
+        const int b = j & 1;
+        if (j >= 2) ok = mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(b * BN);
+        bool first = true;
+        for (int kt = 0; kt < tl.kt_end; ++kt) {
+          if (!k_active(sh, tl.m0, kt)) continue;
+          const int s = it % C::kStages;
+          ok = mbar_wait(&full[s], (it / C::kStages) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * C::kStage);
+          const uint32_t a_hi = st;
+          const uint32_t a_lo = st + C::kA;
+          const uint32_t b_hi = st + C::kA * C::kAParts;
+          const uint32_t b_lo = b_hi + C::kB;
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint32_t acc0 = (!first || ks > 0) ? 1u : 0u;
+            const uint64_t dah = part_desc(a_hi, a_kmajor, BM, ks);
+            const uint64_t dbh = part_desc(b_hi, b_kmajor, BN, ks);
+            umma_bf16(d, dah, dbh, idesc, acc0);
+            if (PREC == 3) umma_bf16(d, dah, part_desc(b_lo, b_kmajor, BN, ks), idesc, 1u);
+            if (PREC >= 2) umma_bf16(d, part_desc(a_lo, a_kmajor, BM, ks), dbh, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
+          ++it;
+          first = false;
+        }
+        if (!ok) break;
+        umma_commit(&tmem_full[b]);  // fires when this tile's MMAs have completed
+      }
+      // every MMA issued above has completed before TMEM is released
+      umma_commit(done);
+      mbar_wait(done, 0);
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2-5)
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    bool ok = true;
+    int j = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
+      const Tile tl = tile_at<BN>(sh, t);
+      const int b = j & 1;
+      ok = mbar_wait(&tmem_full[b], (j >> 1) & 1);
       tc_fence_after();
-      const uint32_t st = smem_u32(smem + s * C::kStage);
-      const uint32_t a_hi = st;
-      const uint32_t a_lo = st + C::kA;
-      const uint32_t b_hi = st + C::kA * C::kAParts;
-      const uint32_t b_lo = b_hi + C::kB;
-#pragma unroll
-      for (int ks = 0; ks < BK / 16; ++ks) {
-        const uint32_t acc0 = (it > 0 || ks > 0) ? 1u : 0u;
-        const uint64_t dah = part_desc(a_hi, a_kmajor, BM, ks);
-        const uint64_t dbh = part_desc(b_hi, b_kmajor, BN, ks);
-        umma_bf16(tmem, dah, dbh, idesc, acc0);
-        if (PREC == 3) umma_bf16(tmem, dah, part_desc(b_lo, b_kmajor, BN, ks), idesc, 1u);
-        if (PREC >= 2) umma_bf16(tmem, part_desc(a_lo, a_kmajor, BM, ks), dbh, idesc, 1u);
-      }
-      umma_commit(&empty[s]);
-      ++it;
-    }
-    umma_commit(done);  // fires when every MMA issued above has completed
-  }
-  __syncwarp();
-
-  // ------------------------------------------------ epilogue (all 4 warps)
-  ok = mbar_wait(done, 0);
-  tc_fence_after();
-  const bool run_epilogue =
-      __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(&g_gemm_status) == 0);
-  if (run_epilogue && !skip_tile) {
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+      ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(&g_gemm_status) == 0);
+      if (!ok) break;
+      if (!tl.skip) {
+        float* cz = c + int64_t(tl.z) * stride_c;
+        const int row = tl.m0 + quarter * 32 + lane;
+        const uint32_t lane_base = tmem + uint32_t(b * BN) + (uint32_t(quarter * 32) << 16);
 #pragma unroll 1
-    for (int col = 0; col < BN; col += 32) {
-      float v[32];
-      tmem_ld32(lane_base + col, v);
-      if (n_active == 0) {
+        for (int col = 0; col < BN; col += 32) {
+          float v[32];
+          tmem_ld32(lane_base + col, v);
+          if (tl.n_active == 0) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-      }
-      const int gc = n0 + col;
-      if (row < m && gc < n) {
-        float* dst = c + int64_t(row) * ldc + gc;
-        const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
-        if (full_chunk) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            if (bias) {
-              o.x += bias[gc + j]; o.y += bias[gc + j + 1];
-              o.z += bias[gc + j + 2]; o.w += bias[gc + j + 3];
-            }
-            if (accumulate) {
-              const float4 p = *reinterpret_cast<const float4*>(dst + j);
-              o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
-            }
-            *reinterpret_cast<float4*>(dst + j) = o;
+            for (int q = 0; q < 32; ++q) v[q] = 0.f;
           }
-        } else {
-          for (int j = 0; j < 32 && gc + j < n; ++j) {
-            float o = v[j];
-            if (bias) o += bias[gc + j];
-            if (accumulate) o += dst[j];
-            dst[j] = o;
+          const int gc = tl.n0 + col;
+          if (row < m && gc < n) {
+            float* dst = cz + int64_t(row) * ldc + gc;
+            const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+            if (full_chunk) {
+#pragma unroll
+              for (int q = 0; q < 32; q += 4) {
+                float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+                if (bias) {
+                  o.x += bias[gc + q]; o.y += bias[gc + q + 1];
+                  o.z += bias[gc + q + 2]; o.w += bias[gc + q + 3];
+                }
+                if (accumulate) {
+                  const float4 p = *reinterpret_cast<const float4*>(dst + q);
+                  o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+                }
+                *reinterpret_cast<float4*>(dst + q) = o;
+              }
+            } else {
+              for (int q = 0; q < 32 && gc + q < n; ++q) {
+                float o = v[q];
+                if (bias) o += bias[gc + q];
+                if (accumulate) o += dst[q];
+                dst[q] = o;
+              }
+            }
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[b]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
@@ -435,6 +520,18 @@ bool operand_map(CUtensorMap* map, const void* p, bool kmajor, int64_t rows, int
   return make_map(map, p, rows, k, ld, batch, batch_stride, 64, BK);
 }
 
+int sm_count() {
+  static int count = 0;
+  if (!count) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        count <= 0)
+      count = kSMs;
+  }
+  return count;
+}
+
 template <int BN, int PREC>
 int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const float* bias,
            int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
@@ -450,9 +547,12 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
     }
     configured = true;
   }
-  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-  gemm_kernel<BN, PREC><<<dim3(tiles, batch), kThreads, C::kSmem, stream>>>(
-      maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor, causal, clen);
+  const int64_t tiles = int64_t((m + BM - 1) / BM) * ((n + BN - 1) / BN) * batch;
+  if (tiles > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
+  const int grid = int(tiles < sm_count() ? tiles : sm_count());
+  gemm_kernel<BN, PREC><<<grid, kThreads, C::kSmem, stream>>>(
+      maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor, causal, clen,
+      int(tiles));
   return launch_status();
 }
 

@@ -18,11 +18,11 @@
 // with recip(0) = 0, each one correctly rounded and none contracted into FMA.
 //
 // colsumsq_kernel: out[c] += sum_r (hi + lo)[r, c]^2 -- the summed squared
-// activation each input channel sees (runner.py:359-363).  A block covers 256
-// consecutive columns and a slab of rows: 32 threads span a row (8 columns
-// each, one 16-byte load per part) and 8 such row lanes stride the slab; the
-// partial column sums meet in shared memory, one atomicAdd per column and
-// block.
+// activation each input channel sees (runner.py:359-363).  A block owns 64
+// consecutive columns over all rows: 8 threads span a row (8 columns each, one
+// 16-byte load per part) and 32 such row lanes stride the rows; the row lanes'
+// partial sums are combined in shared memory in a fixed order and each column
+// is written by one thread, so the result does not depend on scheduling.
 
 #include "common.cuh"
 
@@ -118,25 +118,22 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const uint16_t* __rest
   }
 }
 
-constexpr int kColThreads = 256;  // 32 column chunks of 8 x 8 row lanes
-constexpr int kColsPerBlock = 256;
-constexpr int kRowLanes = kColThreads / (kColsPerBlock / 8);
+constexpr int kColThreads = 256;
+constexpr int kColsPerBlock = 64;
+constexpr int kRowLanes = kColThreads / (kColsPerBlock / 8);  // 32
 
 __global__ void __launch_bounds__(kColThreads) colsumsq_kernel(const uint16_t* __restrict__ hi,
                                                                const uint16_t* __restrict__ lo,
                                                                int64_t rows, int64_t cols,
-                                                               int64_t rows_per_block,
                                                                float* __restrict__ out) {
   const int chunk = threadIdx.x % (kColsPerBlock / 8);
   const int rlane = threadIdx.x / (kColsPerBlock / 8);
   const int64_t c0 = int64_t(blockIdx.x) * kColsPerBlock + chunk * 8;
-  const int64_t r0 = int64_t(blockIdx.y) * rows_per_block;
-  const int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   if (c0 < cols) {
-    for (int64_t r = r0 + rlane; r < r1; r += kRowLanes) {
+    for (int64_t r = rlane; r < rows; r += kRowLanes) {
       float h[8];
       unpack8(__ldcs(reinterpret_cast<const uint4*>(hi + r * cols + c0)), h);
       if (lo) {
@@ -149,15 +146,17 @@ __global__ void __launch_bounds__(kColThreads) colsumsq_kernel(const uint16_t* _
       for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(h[i], h[i]));
     }
   }
-  __shared__ float sh[kRowLanes][kColsPerBlock];
+  __shared__ float sh[kRowLanes][kColsPerBlock + 1];
 #pragma unroll
   for (int i = 0; i < 8; ++i) sh[rlane][chunk * 8 + i] = acc[i];
   __syncthreads();
-  const int col = threadIdx.x;  // kColThreads == kColsPerBlock
-  float s = 0.f;
-  for (int k = 0; k < kRowLanes; ++k) s = __fadd_rn(s, sh[k][col]);
-  const int64_t c = int64_t(blockIdx.x) * kColsPerBlock + col;
-  if (c < cols) atomicAdd(out + c, s);
+  if (threadIdx.x < kColsPerBlock) {
+    const int col = threadIdx.x;
+    float s = 0.f;
+    for (int q = 0; q < kRowLanes; ++q) s = __fadd_rn(s, sh[q][col]);
+    const int64_t c = int64_t(blockIdx.x) * kColsPerBlock + col;
+    if (c < cols) out[c] = __fadd_rn(out[c], s);
+  }
 }
 
 }  // namespace
@@ -208,14 +207,8 @@ extern "C" int mr_colsumsq_split(const uint16_t* hi, const uint16_t* lo, int64_t
   if (cols % 8) return MR_ERR_ARGUMENT;
   if (!aligned16(hi) || (lo && !aligned16(lo))) return MR_ERR_ALIGNMENT;
   const int64_t col_blocks = (cols + kColsPerBlock - 1) / kColsPerBlock;
-  // enough row slabs to put about four blocks on every SM
-  int64_t slabs = (int64_t(kSMs) * 4 + col_blocks - 1) / col_blocks;
-  if (slabs > rows) slabs = rows;
-  if (slabs > 65535) slabs = 65535;
-  const int64_t per = (rows + slabs - 1) / slabs;
-  slabs = (rows + per - 1) / per;
-  const dim3 grid{unsigned(col_blocks), unsigned(slabs), 1u};
-  colsumsq_kernel<<<grid, kColThreads, 0, static_cast<cudaStream_t>(stream)>>>(hi, lo, rows, cols,
-                                                                               per, out);
+  if (col_blocks > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
+  colsumsq_kernel<<<unsigned(col_blocks), kColThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      hi, lo, rows, cols, out);
   return launch_status();
 }
