@@ -11,9 +11,9 @@
 // Structure: a persistent kernel, one CTA (192 threads) per SM, walking the
 // flattened (batch, M-tile, N-tile) list of 128 x BN output tiles with stride
 // gridDim.x (grouped rasterization: 16 M-tiles share each sweep over N):
-//   warp 0, one lane : TMA producer.  Loads 64-wide K slices of A and B (hi
-//                      and lo parts) into a ring of shared-memory stages with
-//                      128-byte swizzle, continuing across tiles; completion is
+//   warp 0, one lane : TMA producer.  Loads 32- or 64-wide K slices of A and B (hi
+//                      and lo parts) into a ring of up to 8 swizzled
+//                      shared-memory stages, continuing across tiles; completion is
 //                      tracked by the stage's "full" mbarrier (transaction bytes).
 //   warp 1           : allocates two TMEM accumulators (2 x BN columns); one
 //                      lane issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K
@@ -25,11 +25,15 @@
 //                      previous C, stores float32 rows, and arrives on
 //                      "tmem_empty" -- while the MMAs of the next tile run in
 //                      the other accumulator.
-// Operand majorness: K-major tiles are TMA boxes {64 (K), rows}; MN-major
-// tiles are boxes {64 (M or N), 64 (K)}, one per 64-wide MN chunk.  The UMMA
-// shared-memory descriptors describe the canonical SWIZZLE_128B layouts of
-// both (K-major: 8-row groups 1024 B apart; MN-major: 8-K-row groups 1024 B
-// apart, 64-wide MN chunks one box apart).
+// Operand majorness: K-major tiles are TMA boxes {BK (K), rows} with BK*2-byte
+// swizzle; MN-major tiles are boxes {64 (M or N), BK (K)} with 128-byte
+// swizzle, one per 64-wide MN chunk.  The UMMA shared-memory descriptors
+// describe the canonical layouts of both (K-major: 8-row groups BK*16 B apart;
+// MN-major: 8-K-row groups 1024 B apart, 64-wide MN chunks one box apart).
+// K slices are 32 wide (64-byte rows) when an operand is K-major: a stage is
+// then 48 KB for three products at BN = 256, four stages fit, and the loads
+// run several MMA groups ahead.  With both operands MN-major the slices are 64
+// wide (128-byte rows), keeping each TMA box at 8 KB.
 // Every mbarrier wait is bounded in time: a wait that exceeds the limit sets
 // the device status word (read with mr_gemm_status), and all roles skip their
 // remaining work, wait (bounded) for their own issued copies and MMAs, and
@@ -44,7 +48,8 @@ namespace mr {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
+// K per stage (BK): 32 (K-major rows of 64 B, SWIZZLE_64B) or 64 (128 B rows,
+// SWIZZLE_128B); MN-major tiles always have 128-byte rows (64 M or N values).
 constexpr int kThreads = 192;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
@@ -162,14 +167,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
 }
 
 // ---------------------------------------------------------------- descriptors
-// UMMA shared-memory descriptor for a SWIZZLE_128B canonical layout.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptor for a swizzled canonical layout
+// (layout type 2 = SWIZZLE_128B, 4 = SWIZZLE_64B).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= uint64_t((addr >> 4) & 0x3FFFu);
   d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
   d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
   d |= uint64_t(1) << 46;  // descriptor version (sm_100)
-  d |= uint64_t(2) << 61;  // SWIZZLE_128B
+  d |= uint64_t(layout) << 61;
   return d;
 }
 
@@ -184,14 +191,14 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn) {
          | (uint32_t(BM >> 4) << 24);    // M
 }
 
-template <int BN, int PREC>
+template <int BN, int BK, int PREC>
 struct Cfg {
   static constexpr int kA = BM * BK * 2;                  // bytes of one A part per stage
   static constexpr int kB = BN * BK * 2;                  // bytes of one B part per stage
   static constexpr int kAParts = PREC >= 2 ? 2 : 1;
   static constexpr int kBParts = PREC == 3 ? 2 : 1;
   static constexpr int kStage = kA * kAParts + kB * kBParts;
-  static constexpr int kStages = (200 * 1024) / kStage > 4 ? 4 : (200 * 1024) / kStage;
+  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
   static constexpr int kSmem = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
   static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
 };
@@ -200,9 +207,9 @@ struct Maps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;
 };
 
-// Load one operand part (rows x 64 K) of a stage.  K-major: one box {64, rows}.
-// MN-major: rows/64 boxes {64, 64} at 8 KB spacing.
-template <int ROWS>
+// Load one operand part (rows x BK) of a stage.  K-major: one box {BK, rows}.
+// MN-major: rows/64 boxes {64, BK} at 64 * BK * 2 bytes spacing.
+template <int ROWS, int BK>
 __device__ __forceinline__ void load_part(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                           bool kmajor, int row0, int k0, int z) {
   if (kmajor) {
@@ -214,11 +221,14 @@ __device__ __forceinline__ void load_part(uint8_t* dst, const CUtensorMap* map, 
   }
 }
 
-__device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int rows, int kstep) {
-  // K-major: +32 B per 16-wide K step inside the 128 B swizzle row; SBO 1024.
-  // MN-major: +2048 B (two 8-row K groups) per K step; LBO = one 64-wide box.
-  return kmajor ? smem_desc(base + kstep * 32, 16, 1024)
-                : smem_desc(base + kstep * 2048, 64 * BK * 2, 1024);
+template <int BK>
+__device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int kstep) {
+  // K-major: +32 B per 16-wide K step inside the swizzle row (BK * 2 bytes);
+  // 8-row groups 8 * BK * 2 bytes apart (SBO); SWIZZLE_64B or SWIZZLE_128B.
+  // MN-major: +2048 B (two 8-row K groups of 1024 B) per K step; LBO = one
+  // 64-wide MN box.
+  return kmajor ? smem_desc(base + kstep * 32, 16, 8 * BK * 2, BK == 32 ? 4 : 2)
+                : smem_desc(base + kstep * 2048, 64 * BK * 2, 1024, 2);
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -243,12 +253,13 @@ struct Shape {
 //  2: C = P V or dS K     -- K (key positions) stops after the tile's last row;
 //  3: C = dS^T Q or P^T dO -- K-tiles whose rows all precede the tile's first
 //     key are skipped.
+template <int BK>
 __device__ __forceinline__ bool k_active(const Shape& sh, int m0, int kt) {
   return sh.causal != 3 || ((kt * BK) % sh.clen) + BK - 1 >= m0;
 }
 
 // Grouped rasterization inside each batch entry: 16 M-tiles share a sweep over N.
-template <int BN>
+template <int BN, int BK>
 __device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
   constexpr int G = 16;
   const int per_batch = sh.m_tiles * sh.n_tiles;
@@ -268,7 +279,7 @@ __device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
   tl.n_active = tl.kt_end;
   if (sh.causal == 3) {
     tl.n_active = 0;
-    for (int kt = 0; kt < tl.kt_end; ++kt) tl.n_active += k_active(sh, tl.m0, kt) ? 1 : 0;
+    for (int kt = 0; kt < tl.kt_end; ++kt) tl.n_active += k_active<BK>(sh, tl.m0, kt) ? 1 : 0;
   }
   return tl;
 }
@@ -284,12 +295,12 @@ __device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
 //                      MMAs of tile j + 1 run in the other; each warp reads the
 //                      32 TMEM lanes (warp % 4) it may access, stores float32
 //                      rows, then arrives on tmem_empty[j & 1].
-template <int BN, int PREC>
+template <int BN, int BK, int PREC>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
                 int64_t stride_c, const float* __restrict__ bias, int accumulate, int m, int n,
                 int k, int a_kmajor, int b_kmajor, int causal, int clen, int total_tiles) {
-  using C = Cfg<BN, PREC>;
+  using C = Cfg<BN, BK, PREC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStage);
@@ -335,9 +346,9 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int it = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const Tile tl = tile_at<BN>(sh, t);
+        const Tile tl = tile_at<BN, BK>(sh, t);
         for (int kt = 0; kt < tl.kt_end; ++kt) {
-          if (!k_active(sh, tl.m0, kt)) continue;
+          if (!k_active<BK>(sh, tl.m0, kt)) continue;
           const int s = it % C::kStages;
           const uint32_t round = it / C::kStages;
           if (it >= C::kStages) ok = mbar_wait(&empty[s], (round - 1) & 1);
@@ -346,13 +357,13 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* st = smem + s * C::kStage;
           mbar_expect_tx(&full[s], C::kStage);
           const int k0 = kt * BK;
-          load_part<BM>(st, &maps.a_hi, &full[s], a_kmajor, tl.m0, k0, tl.z);
+          load_part<BM, BK>(st, &maps.a_hi, &full[s], a_kmajor, tl.m0, k0, tl.z);
           if (C::kAParts == 2)
-            load_part<BM>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, tl.m0, k0, tl.z);
+            load_part<BM, BK>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, tl.m0, k0, tl.z);
           uint8_t* sb = st + C::kA * C::kAParts;
-          load_part<BN>(sb, &maps.b_hi, &full[s], b_kmajor, tl.n0, k0, tl.z);
+          load_part<BN, BK>(sb, &maps.b_hi, &full[s], b_kmajor, tl.n0, k0, tl.z);
           if (C::kBParts == 2)
-            load_part<BN>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, tl.n0, k0, tl.z);
+            load_part<BN, BK>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, tl.n0, k0, tl.z);
         }
       }
       if (!ok) {
@@ -372,7 +383,7 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int it = 0, j = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++j) {
-        const Tile tl = tile_at<BN>(sh, t);
+        const Tile tl = tile_at<BN, BK>(sh, t);
         const int b = j & 1;
         if (j >= 2) ok = mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1);
         if (!ok) break;
@@ -380,7 +391,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t d = tmem + uint32_t(b * BN);
         bool first = true;
         for (int kt = 0; kt < tl.kt_end; ++kt) {
-          if (!k_active(sh, tl.m0, kt)) continue;
+          if (!k_active<BK>(sh, tl.m0, kt)) continue;
           const int s = it % C::kStages;
           ok = mbar_wait(&full[s], (it / C::kStages) & 1);
           if (!ok) break;
@@ -393,11 +404,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
             const uint32_t acc0 = (!first || ks > 0) ? 1u : 0u;
-            const uint64_t dah = part_desc(a_hi, a_kmajor, BM, ks);
-            const uint64_t dbh = part_desc(b_hi, b_kmajor, BN, ks);
+            const uint64_t dah = part_desc<BK>(a_hi, a_kmajor, ks);
+            const uint64_t dbh = part_desc<BK>(b_hi, b_kmajor, ks);
             umma_bf16(d, dah, dbh, idesc, acc0);
-            if (PREC == 3) umma_bf16(d, dah, part_desc(b_lo, b_kmajor, BN, ks), idesc, 1u);
-            if (PREC >= 2) umma_bf16(d, part_desc(a_lo, a_kmajor, BM, ks), dbh, idesc, 1u);
+            if (PREC == 3) umma_bf16(d, dah, part_desc<BK>(b_lo, b_kmajor, ks), idesc, 1u);
+            if (PREC >= 2) umma_bf16(d, part_desc<BK>(a_lo, a_kmajor, ks), dbh, idesc, 1u);
           }
           umma_commit(&empty[s]);
           ++it;
@@ -416,7 +427,7 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
-      const Tile tl = tile_at<BN>(sh, t);
+      const Tile tl = tile_at<BN, BK>(sh, t);
       const int b = j & 1;
       ok = mbar_wait(&tmem_full[b], (j >> 1) & 1);
       tc_fence_after();
@@ -498,7 +509,8 @@ EncodeTiledFn encode_fn() {
 }
 
 bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
-              int64_t batch, int64_t batch_stride, uint32_t box_inner, uint32_t box_outer) {
+              int64_t batch, int64_t batch_stride, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle) {
   EncodeTiledFn encode = encode_fn();
   if (!encode) return false;
   const cuuint64_t dims[3] = {cuuint64_t(inner), cuuint64_t(outer), cuuint64_t(batch)};
@@ -508,16 +520,19 @@ bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
   const cuuint32_t elem_strides[3] = {1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
                       strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
 // Map for an operand with `rows` logical rows (M or N) and K columns.
 bool operand_map(CUtensorMap* map, const void* p, bool kmajor, int64_t rows, int64_t k,
-                 int64_t ld, int64_t batch, int64_t batch_stride, int tile_rows) {
-  if (kmajor) return make_map(map, p, k, rows, ld, batch, batch_stride, BK, uint32_t(tile_rows));
-  return make_map(map, p, rows, k, ld, batch, batch_stride, 64, BK);
+                 int64_t ld, int64_t batch, int64_t batch_stride, int tile_rows, int bk) {
+  if (kmajor)
+    return make_map(map, p, k, rows, ld, batch, batch_stride, uint32_t(bk), uint32_t(tile_rows),
+                    bk == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_map(map, p, rows, k, ld, batch, batch_stride, 64, uint32_t(bk),
+                  CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int sm_count() {
@@ -532,14 +547,14 @@ int sm_count() {
   return count;
 }
 
-template <int BN, int PREC>
+template <int BN, int BK, int PREC>
 int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const float* bias,
            int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
            int causal, int clen, cudaStream_t stream) {
-  using C = Cfg<BN, PREC>;
+  using C = Cfg<BN, BK, PREC>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, PREC>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BK, PREC>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) {
       set_cuda_error(e);
@@ -550,7 +565,7 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
   const int64_t tiles = int64_t((m + BM - 1) / BM) * ((n + BN - 1) / BN) * batch;
   if (tiles > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
   const int grid = int(tiles < sm_count() ? tiles : sm_count());
-  gemm_kernel<BN, PREC><<<grid, kThreads, C::kSmem, stream>>>(
+  gemm_kernel<BN, BK, PREC><<<grid, kThreads, C::kSmem, stream>>>(
       maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor, causal, clen,
       int(tiles));
   return launch_status();
@@ -588,32 +603,39 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
     if (causal == 2 && k != seq) return MR_ERR_ARGUMENT;
     if (causal == 3 && (m != seq || k % seq)) return MR_ERR_ARGUMENT;
   }
-  // narrow outputs (attention's head dimension) use 128-wide tiles
+  // narrow outputs (attention's head dimension) use 128-wide tiles; 32-wide K
+  // slices (deeper pipelines) unless both operands are MN-major, whose 64-wide
+  // boxes would then be split into many small TMA copies
   const int BNsel = n <= 128 ? 128 : 256;
+  const int BKsel = (!a_kmajor && !b_kmajor) ? 64 : 32;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
-  bool good = operand_map(&maps.a_hi, a_hi, a_kmajor, m, k, lda, batch, stride_a, BM) &&
-              operand_map(&maps.b_hi, b_hi, b_kmajor, n, k, ldb, batch, stride_b, BNsel);
+  bool good = operand_map(&maps.a_hi, a_hi, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel) &&
+              operand_map(&maps.b_hi, b_hi, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
   if (good && precision >= 2)
-    good = operand_map(&maps.a_lo, a_lo, a_kmajor, m, k, lda, batch, stride_a, BM);
+    good = operand_map(&maps.a_lo, a_lo, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel);
   if (good && precision == 3)
-    good = operand_map(&maps.b_lo, b_lo, b_kmajor, n, k, ldb, batch, stride_b, BNsel);
+    good = operand_map(&maps.b_lo, b_lo, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
   if (!good) return MR_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bt = int(batch);
   const int M = int(m), N = int(n), Kk = int(k);
+#define MR_GEMM_LAUNCH(BN_, BK_)                                                               \
+  switch (precision) {                                                                         \
+    case 1: return launch<BN_, BK_, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,     \
+                                       a_kmajor, b_kmajor, bt, causal, int(seq), s);           \
+    case 2: return launch<BN_, BK_, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,     \
+                                       a_kmajor, b_kmajor, bt, causal, int(seq), s);           \
+    default: return launch<BN_, BK_, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,    \
+                                        a_kmajor, b_kmajor, bt, causal, int(seq), s);          \
+  }
   if (BNsel == 128) {
-    switch (precision) {
-      case 1: return launch<128, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
-      case 2: return launch<128, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
-      default: return launch<128, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
-    }
+    if (BKsel == 64) { MR_GEMM_LAUNCH(128, 64) }
+    MR_GEMM_LAUNCH(128, 32)
   }
-  switch (precision) {
-    case 1: return launch<256, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
-    case 2: return launch<256, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
-    default: return launch<256, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor, b_kmajor, bt, causal, int(seq), s);
-  }
+  if (BKsel == 64) { MR_GEMM_LAUNCH(256, 64) }
+  MR_GEMM_LAUNCH(256, 32)
+#undef MR_GEMM_LAUNCH
 }
 
 extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
