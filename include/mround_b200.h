@@ -264,7 +264,8 @@ int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* s
  * Each reads float32 activations and writes the next GEMM operand directly as
  * a bf16 hi/lo pair.  Token t = b*S + s; attention operands are (B, H, S, D).
  *   mr_rmsnorm_split:     y = x * rsqrt(mean(x^2) + eps) * w; rstd per row
- *   mr_rmsnorm_bwd_split: dx = resid + rstd * (g - xhat * mean(g * xhat)), g = dy * w
+ *   mr_rmsnorm_bwd_split: dx = resid + rstd * (g - xhat * mean(g * xhat)), g = dy * w;
+ *                         resid may be NULL; written as hi/lo and/or float32 (out)
  *   mr_rope_split:        qkv (T, (Hq+2Hkv)*D) -> rope(q), rope(k), v as (B,H,S,D)
  *   mr_rope_bwd_split:    dq, dk, dv (B,H,S,D) -> dqkv (T, (Hq+2Hkv)*D)
  *   mr_heads_split:       merge=1: (B,H,S,D) -> (T, H*D); merge=0: the reverse
@@ -281,7 +282,7 @@ int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows, int h, flo
                      uint16_t* hi, uint16_t* lo, float* rstd, void* stream);
 int mr_rmsnorm_bwd_split(const float* dy, const float* x, const uint16_t* w, const float* rstd,
                          const float* resid, int64_t rows, int h, uint16_t* hi, uint16_t* lo,
-                         void* stream);
+                         float* out, void* stream);
 int mr_rope_split(const float* qkv, const float* cosv, const float* sinv, int b, int s, int hq,
                   int hkv, int d, uint16_t* q_hi, uint16_t* q_lo, uint16_t* k_hi, uint16_t* k_lo,
                   uint16_t* v_hi, uint16_t* v_lo, void* stream);

@@ -64,7 +64,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
                              _I, _I64, _I64, _I64, _I64, _I, _I, _I64, _P]),
     "mr_gemm_status": (_I, [_I]),
     "mr_rmsnorm_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P, _P]),
-    "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P]),
+    "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P, _P]),
     "mr_rope_split": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "mr_rope_bwd_split": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "mr_heads_split": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),

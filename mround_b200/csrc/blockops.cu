@@ -104,10 +104,12 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_split_kernel(
 }
 
 // dx = resid + rstd * (g - xhat * mean(g * xhat)),  g = dy * w,  xhat = x * rstd.
+// Written as hi/lo (when hi is given) and/or float32 (when out is given);
+// resid may be NULL (no residual term).
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_split_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const uint16_t* __restrict__ w,
     const float* __restrict__ rstd, const float* __restrict__ resid, int h,
-    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ out) {
   __shared__ float sh[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const float r = rstd[row];
@@ -134,13 +136,14 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_split_kernel(
   for (int i = 0; i < kMaxVec; ++i) {
     const int c = threadIdx.x + i * kRowThreads;
     if (c < n4) {
-      const float4 q = rr[c];
+      const float4 q = resid ? rr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
       float4 d;
       d.x = q.x + r * (g[i].x - xh[i].x * dot);
       d.y = q.y + r * (g[i].y - xh[i].y * dot);
       d.z = q.z + r * (g[i].z - xh[i].z * dot);
       d.w = q.w + r * (g[i].w - xh[i].w * dot);
-      put_split4(hi, lo, row * h + c * 4, d);
+      if (hi) put_split4(hi, lo, row * h + c * 4, d);
+      if (out) reinterpret_cast<float4*>(out + row * h)[c] = d;
     }
   }
 }
@@ -364,13 +367,15 @@ extern "C" int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows,
 
 extern "C" int mr_rmsnorm_bwd_split(const float* dy, const float* x, const uint16_t* w,
                                     const float* rstd, const float* resid, int64_t rows, int h,
-                                    uint16_t* hi, uint16_t* lo, void* stream) {
-  if (!dy || !x || !w || !rstd || !resid || !hi || !lo || rows <= 0 || h <= 0 || h % 4 ||
+                                    uint16_t* hi, uint16_t* lo, float* out, void* stream) {
+  if (!dy || !x || !w || !rstd || rows <= 0 || h <= 0 || h % 4 ||
       h > 4 * kMaxVec * kRowThreads)
     return MR_ERR_ARGUMENT;
-  if (!aligned16(dy) || !aligned16(x) || !aligned16(resid)) return MR_ERR_ALIGNMENT;
+  if ((hi == nullptr) != (lo == nullptr) || (!hi && !out)) return MR_ERR_ARGUMENT;
+  if (!aligned16(dy) || !aligned16(x) || (resid && !aligned16(resid)) || (out && !aligned16(out)))
+    return MR_ERR_ALIGNMENT;
   rmsnorm_bwd_split_kernel<<<unsigned(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      dy, x, w, rstd, resid, h, hi, lo);
+      dy, x, w, rstd, resid, h, hi, lo, out);
   return launch_status();
 }
 

@@ -378,13 +378,17 @@ def rmsnorm_split(x, w, eps: float):
     return hi, lo, rstd
 
 
-def rmsnorm_bwd_split(dy, x, w, rstd, resid):
+def rmsnorm_bwd_split(dy, x, w, rstd, resid, *, split: bool = True, out=None):
+    """RMSNorm backward plus ``resid`` (or None): ``(hi, lo)`` when ``split``,
+    and the float32 gradient written to ``out`` when given.  Returns (hi, lo)
+    or (None, None)."""
     t, h = x.shape
-    hi, lo = _pair((t, h), x.device)
-    st = lib().mr_rmsnorm_bwd_split(_ptr(dy, torch.float32, "dy", t * h), _ptr(x, torch.float32, "x"),
-                                    _ptr(w, torch.bfloat16, "w", h), _ptr(rstd, torch.float32, "rstd", t),
-                                    _ptr(resid, torch.float32, "resid", t * h), t, h, hi.data_ptr(),
-                                    lo.data_ptr(), _stream())
+    hi, lo = _pair((t, h), x.device) if split else (None, None)
+    st = lib().mr_rmsnorm_bwd_split(
+        _ptr(dy, torch.float32, "dy", t * h), _ptr(x, torch.float32, "x"),
+        _ptr(w, torch.bfloat16, "w", h), _ptr(rstd, torch.float32, "rstd", t),
+        _ptr(resid, torch.float32, "resid", t * h), t, h, None if hi is None else hi.data_ptr(),
+        None if lo is None else lo.data_ptr(), _ptr(out, torch.float32, "out", t * h), _stream())
     check(st, "mr_rmsnorm_bwd_split")
     _count()
     return hi, lo

@@ -330,12 +330,17 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     saved = None
     if save:
         saved = dict(shape=(b, s, h), h1=(h1[0], h1[1]), q=q, k=k, v=v, p=scores, probs=probs,
-                     att=att, hres=hres, rstd2=rstd2, h2=(h2_hi, h2_lo), gu=gu, act=act)
+                     att=att, hres=hres, rstd2=rstd2, h2=(h2_hi, h2_lo), gu=gu, act=act,
+                     x=x2, rstd1=h1[2])
     return out.view(b, s, h), saved
 
 
-def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Precision) -> None:
-    """Weight gradients of every tunable fused linear into ``layer.grad``."""
+def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Precision,
+                    want_dx: bool = False) -> torch.Tensor | None:
+    """Weight gradients of every fused linear that has a ``grad`` buffer, and,
+    with ``want_dx``, the gradient of the block input (float32, the shape of
+    ``dout``) -- the whole-model backward of the DeltaLoss scoring needs it;
+    the tuning step does not."""
     a = self.arch
     b, s, h = saved["shape"]
     t = b * s
@@ -369,7 +374,9 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     weight_grad(gu_l, g_gu, saved["h2"], 2 * inter, h)
     dh2 = input_grad(gu_l, g_gu, 2 * inter, h)
     del g_gu
-    g_h = kernels.rmsnorm_bwd_split(dh2, saved["hres"], self.post_norm, saved["rstd2"], dout2)
+    g_h_f32 = torch.empty_like(dout2) if want_dx else None
+    g_h = kernels.rmsnorm_bwd_split(dh2, saved["hres"], self.post_norm, saved["rstd2"], dout2,
+                                    out=g_h_f32)
     del dh2
     weight_grad(o_l, g_h, saved["att"], h, hq * d)
     datt = input_grad(o_l, g_h, h, hq * d)
@@ -397,6 +404,15 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     g_qkv = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)
     del dq, dk, dv
     weight_grad(qkv_l, g_qkv, saved["h1"], qkv_l.out_features, h)
+    if not want_dx:
+        return None
+    dh1 = input_grad(qkv_l, g_qkv, qkv_l.out_features, h)
+    del g_qkv
+    dx = torch.empty_like(dout2)
+    # h = x + attention: the input gradient is the first norm's backward plus dL/dh
+    kernels.rmsnorm_bwd_split(dh1, saved["x"], self.input_norm, saved["rstd1"], g_h_f32,
+                              split=False, out=dx)
+    return dx.view(b, s, h)
 
 
 DeviceBlock.forward_fused = _fused_forward

@@ -10,6 +10,11 @@ layer and width ``sum |g * (Q_b(W) - W)|`` accumulated over batches
 reading the gradient once for all widths it scores, so no gradient or
 perturbation is ever held beyond its layer.
 
+The backward is the blocks' explicit fused forward/backward (the same K3 GEMMs
+and K7 element-wise kernels as the tuning step, plus the block-input gradient)
+and the LM head on K3; the cross-entropy gradient is formed in place on the
+logits.
+
 ``own_width`` takes one backward per width at that width's anchors (the
 reference's procedure); ``widest`` one backward at the widest width, scoring
 every width's perturbation against it.  Sequences are padded to a multiple of
@@ -25,11 +30,10 @@ from collections.abc import Callable, Sequence
 
 import numpy as np
 import torch
-import torch.nn.functional as F
 
 from mround_b200 import kernels
 from mround_b200.exceptions import SchemeError
-from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision, rms_norm
+from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision
 from mround_b200.pipeline.model import SyntheticModel
 from mround_b200.core.scale_search import search_scales
 from mround_b200.schemes import DEFAULT_EPS_FP32, QuantScheme, ScaleInit, Symmetry
@@ -43,33 +47,6 @@ class SensitivityScores:
     shapes: dict[str, tuple[int, int]]
     skipped: tuple[tuple[str, str], ...]
     seconds: float
-
-
-class _LMHead(torch.autograd.Function):
-    """logits = h @ E^T with E exact in bf16 (two products); dh = dlogits @ E."""
-
-    @staticmethod
-    def forward(ctx, h, weight):
-        t, d = h.shape
-        v = weight.shape[0]
-        h_hi, h_lo = kernels.split_bf16(h.contiguous())
-        logits = torch.empty((t, v), dtype=torch.float32, device=h.device)
-        kernels.gemm(h_hi, h_lo, weight, None, logits, m=t, n=v, k=d, a_kmajor=True, b_kmajor=True,
-                     lda=d, ldb=d, ldc=v, precision=2)
-        ctx.weight = weight
-        return logits
-
-    @staticmethod
-    def backward(ctx, dlogits):
-        weight = ctx.weight
-        v, d = weight.shape
-        dl = dlogits.contiguous().float()
-        t = dl.shape[0]
-        g_hi, g_lo = kernels.split_bf16(dl)
-        dh = torch.empty((t, d), dtype=torch.float32, device=dl.device)
-        kernels.gemm(g_hi, g_lo, weight, None, dh, m=t, n=d, k=v, a_kmajor=True, b_kmajor=False,
-                     lda=v, ldb=d, ldc=d, precision=2)
-        return dh, None
 
 
 def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: Sequence[int],
@@ -171,23 +148,58 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
                 layer.wq_hi, layer.wq_lo = hi, lo
 
     embed = model.embed_tokens().to(dev)
-    head = model.lm_head().to(dev)
+    head = model.lm_head().to(dev).contiguous()
     final_norm = model.final_norm().to(dev)
 
+    hidden = arch.hidden
+
     def backward_pass(batch: np.ndarray) -> None:
+        """Mean shifted cross-entropy of one batch, backward through every block
+        (explicit fused forward/backward; each block's weight-gradient GEMMs run
+        the K6 hooks)."""
         tokens = torch.as_tensor(batch, dtype=torch.long, device=dev)
         inp, labels = tokens[:, :-1], tokens[:, 1:]
         b, s = inp.shape
         pad = (-s) % 8
         if pad:
             inp = torch.cat([inp, inp[:, -1:].expand(b, pad)], dim=1)
-        x = embed[inp].float()
+        sp = s + pad
+        x = embed[inp].float().contiguous()
+        saved_all = []
         for blk in blocks:
-            x = blk.forward(x, prec, train=True)
-        h = rms_norm(x, final_norm, arch.rms_eps)[:, :s].reshape(b * s, -1)
-        logits = _LMHead.apply(h, head)
-        loss = F.cross_entropy(logits, labels.reshape(-1), reduction="mean")
-        loss.backward()
+            x, saved = blk.forward_fused(x, prec, True)
+            saved_all.append(saved)
+        x2 = x.reshape(b * sp, hidden)
+        n_hi, n_lo, rstd_f = kernels.rmsnorm_split(x2, final_norm, arch.rms_eps)
+        t = b * s
+        real = n_hi.view(b, sp, hidden)[:, :s].reshape(t, hidden), \
+            n_lo.view(b, sp, hidden)[:, :s].reshape(t, hidden)
+        vocab = head.shape[0]
+        logits = torch.empty((t, vocab), dtype=torch.float32, device=dev)
+        kernels.gemm(real[0], real[1], head, None, logits, m=t, n=vocab, k=hidden, a_kmajor=True,
+                     b_kmajor=True, lda=hidden, ldb=hidden, ldc=vocab, precision=2)
+        # d(mean CE)/dlogits = (softmax - onehot) / t, formed in place
+        lse = torch.logsumexp(logits, dim=-1, keepdim=True)
+        logits.sub_(lse).exp_()
+        logits[torch.arange(t, device=dev), labels.reshape(-1)] -= 1.0
+        logits.div_(t)
+        g_hi, g_lo = kernels.split_bf16(logits)
+        del logits
+        dh = torch.empty((t, hidden), dtype=torch.float32, device=dev)
+        kernels.gemm(g_hi, g_lo, head, None, dh, m=t, n=hidden, k=vocab, a_kmajor=True,
+                     b_kmajor=False, lda=vocab, ldb=hidden, ldc=hidden, precision=2)
+        del g_hi, g_lo
+        dn = torch.zeros((b, sp, hidden), dtype=torch.float32, device=dev)
+        dn[:, :s] = dh.view(b, s, hidden)
+        del dh
+        dx = torch.empty((b * sp, hidden), dtype=torch.float32, device=dev)
+        kernels.rmsnorm_bwd_split(dn.view(b * sp, hidden), x2, final_norm, rstd_f, None,
+                                  split=False, out=dx)
+        del dn, x, x2
+        dx = dx.view(b, sp, hidden)
+        for i in range(len(blocks) - 1, -1, -1):
+            dx = blocks[i].backward_fused(saved_all[i], dx, prec, want_dx=i > 0)
+            saved_all[i] = None
 
     schedule = [(w, [w]) for w in widths] if gradient_source == "own_width" else [(widths[-1], widths)]
     done = 0

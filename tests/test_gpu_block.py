@@ -178,13 +178,16 @@ def test_fused_path_matches_autograd_path(env, name, seq):
     # seq % 128 == 0 exercises the causal tile-skipping GEMM modes and band softmax
     x = make_inputs(arch, 1, 2, seq, seed=5)[0].cuda()
     g = torch.randn(x.shape, device="cuda") * 1e-3
-    out_a = block.forward(x, Precision(), train=True)
+    xa = x.clone().requires_grad_(True)
+    out_a = block.forward(xa, Precision(), train=True)
     out_a.backward(g)
     grads_a = {n: l.grad.clone() for n, l in block.layers.items()}
     out_f, saved = block.forward_fused(x, Precision(), True)
-    block.backward_fused(saved, g, Precision())
+    dx = block.backward_fused(saved, g, Precision(), want_dx=True)
     torch.cuda.synchronize()
     assert relative_error(out_f.detach().cpu().numpy(), out_a.detach().cpu().numpy()) < 1e-5
     for n, l in block.layers.items():
         assert relative_error(l.grad.cpu().numpy(), grads_a[n].cpu().numpy()) < 1e-4, n
+    # the block-input gradient (used by the scoring backward)
+    assert relative_error(dx.cpu().numpy(), xa.grad.cpu().numpy()) < 1e-4
     del tuner
