@@ -167,8 +167,8 @@ class ClockSampler:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
 #       --clock-control none -k regex:gemm_kernel -s 96 -c 36
 #       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-e2e
-# (58.2 GB read + 11.0 GB written per step).
-GEMM_TRAFFIC_7B = 4.07e9
+# (60.9 GB read + 10.9 GB written per step).
+GEMM_TRAFFIC_7B = 4.22e9
 
 
 # ----------------------------------------------------------------- workload
