@@ -273,8 +273,9 @@ int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* s
  *   mr_swiglu_bwd_split:  dgu = [dact * u * silu'(g) | dact * silu(g)]
  *   mr_softmax_causal_split: rows of length S, row r at position r % S:
  *                         P = softmax(scale * scores) over columns <= position,
- *                         written in place (float32) and as hi/lo
- *   mr_softmax_bwd_split: dS = scale * P * (dP - sum(dP * P))
+ *                         written as hi/lo (scores unchanged); S % 4 == 0,
+ *                         S <= 8192
+ *   mr_softmax_bwd_split: dS = scale * P * (dP - sum(dP * P)), P given as hi/lo
  *   band != 0 (softmax kernels): columns from (pos/128 + 2)*128 on are not
  *   written -- the causal modes of mr_gemm_batched never read them.
  */
@@ -294,10 +295,11 @@ int mr_heads_split(const float* src, int b, int s, int h, int d, int merge, uint
 int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo, void* stream);
 int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t, int i, uint16_t* hi,
                         uint16_t* lo, void* stream);
-int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale, int band,
+int mr_softmax_causal_split(const float* scores, int64_t rows, int s, float scale, int band,
                             uint16_t* hi, uint16_t* lo, void* stream);
-int mr_softmax_bwd_split(const float* dp, const float* p, int64_t rows, int s, float scale,
-                         int band, uint16_t* hi, uint16_t* lo, void* stream);
+int mr_softmax_bwd_split(const float* dp, const uint16_t* p_hi, const uint16_t* p_lo,
+                         int64_t rows, int s, float scale, int band, uint16_t* hi, uint16_t* lo,
+                         void* stream);
 
 /*
  * K3 -- tcgen05/TMEM GEMM, bf16 operands, float32 accumulate in tensor memory.

@@ -298,53 +298,114 @@ __global__ void swiglu_bwd_split_kernel(const float* __restrict__ dact,
 }
 
 constexpr int kSoftThreads = 256;
-constexpr int kSoftVec = 8;  // rows up to 256*8 = 2048... extended by looping
+constexpr int kSoftVec = 8;  // float4 per thread: rows up to 256 * 4 * 8 = 8192 columns
 
-// Causal softmax of scale * scores, row r at position r % S: P in place + hi/lo.
-// With ``band`` set, columns from the end of the next 128-column block on are
-// left unwritten: the causal GEMM modes never read them.
+// Causal softmax rows, row r at position r % S.  With ``band`` set, columns
+// from the end of the next 128-column block on are left unwritten: the causal
+// GEMM modes never read them.
 __device__ __forceinline__ int write_limit(int pos, int S, int band) {
   return band ? min(S, (pos / 128 + 2) * 128) : S;
 }
 
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__device__ __forceinline__ void unpack4(const uint2 u, float (&x)[4]) {
+  x[0] = __uint_as_float(u.x << 16);
+  x[1] = __uint_as_float(u.x & 0xFFFF0000u);
+  x[2] = __uint_as_float(u.y << 16);
+  x[3] = __uint_as_float(u.y & 0xFFFF0000u);
+}
+
+// P = softmax(scale * scores) over columns <= pos, written as bf16 hi/lo only
+// (scores are not modified).  The row lives in registers: one float4 per
+// thread and 1024-column chunk, read once with 16-byte loads.
 __global__ void __launch_bounds__(kSoftThreads) softmax_causal_kernel(
-    float* __restrict__ scores, int S, float scale, int band, uint16_t* __restrict__ hi,
+    const float* __restrict__ scores, int S, float scale, int band, uint16_t* __restrict__ hi,
     uint16_t* __restrict__ lo) {
   __shared__ float sh[kSoftThreads / 32];
   const int64_t row = blockIdx.x;
   const int pos = int(row % S);
-  float* r = scores + row * S;
+  const float* r = scores + row * S;
+  float v[kSoftVec][4];
   float m = -INFINITY;
-  for (int c = threadIdx.x; c <= pos; c += kSoftThreads) m = fmaxf(m, __fmul_rn(r[c], scale));
+#pragma unroll
+  for (int i = 0; i < kSoftVec; ++i) {
+    const int c = (i * kSoftThreads + threadIdx.x) * 4;
+    if (c <= pos) {
+      const float4 q = ld4(r + c);
+      v[i][0] = __fmul_rn(q.x, scale);
+      v[i][1] = c + 1 <= pos ? __fmul_rn(q.y, scale) : -INFINITY;
+      v[i][2] = c + 2 <= pos ? __fmul_rn(q.z, scale) : -INFINITY;
+      v[i][3] = c + 3 <= pos ? __fmul_rn(q.w, scale) : -INFINITY;
+    } else {
+      v[i][0] = v[i][1] = v[i][2] = v[i][3] = -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) m = fmaxf(m, v[i][j]);
+  }
   m = block_max<kSoftThreads>(m, sh);
   float sum = 0.f;
-  for (int c = threadIdx.x; c <= pos; c += kSoftThreads) sum += expf(__fmul_rn(r[c], scale) - m);
+#pragma unroll
+  for (int i = 0; i < kSoftVec; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[i][j] = v[i][j] == -INFINITY ? 0.f : expf(v[i][j] - m);
+      sum += v[i][j];
+    }
+  }
   sum = block_sum<kSoftThreads>(sum, sh);
   const float inv = 1.f / sum;
   const int lim = write_limit(pos, S, band);
-  for (int c = threadIdx.x; c < lim; c += kSoftThreads) {
-    const float p = c <= pos ? expf(__fmul_rn(r[c], scale) - m) * inv : 0.f;
-    r[c] = p;
-    put_split(hi, lo, row * S + c, p);
+#pragma unroll
+  for (int i = 0; i < kSoftVec; ++i) {
+    const int c = (i * kSoftThreads + threadIdx.x) * 4;
+    if (c < lim)
+      put_split4(hi, lo, row * S + c,
+                 make_float4(v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv));
   }
 }
 
-// dS = scale * P * (dP - sum(dP * P)) -> hi/lo (rows of length S).
+// dS = scale * P * (dP - sum(dP * P)) -> hi/lo, with P = p_hi + p_lo.
 __global__ void __launch_bounds__(kSoftThreads) softmax_bwd_kernel(
-    const float* __restrict__ dp, const float* __restrict__ p, int S, float scale, int band,
-    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+    const float* __restrict__ dp, const uint16_t* __restrict__ p_hi,
+    const uint16_t* __restrict__ p_lo, int S, float scale, int band, uint16_t* __restrict__ hi,
+    uint16_t* __restrict__ lo) {
   __shared__ float sh[kSoftThreads / 32];
   const int64_t row = blockIdx.x;
   const int pos = int(row % S);
   const float* dr = dp + row * S;
-  const float* pr = p + row * S;
+  float pv[kSoftVec][4], dv[kSoftVec][4];
   float dot = 0.f;
-  for (int c = threadIdx.x; c <= pos; c += kSoftThreads) dot += dr[c] * pr[c];
+#pragma unroll
+  for (int i = 0; i < kSoftVec; ++i) {
+    const int c = (i * kSoftThreads + threadIdx.x) * 4;
+    if (c <= pos) {
+      const float4 d = ld4(dr + c);
+      float ph[4], pl[4];
+      unpack4(*reinterpret_cast<const uint2*>(p_hi + row * S + c), ph);
+      unpack4(*reinterpret_cast<const uint2*>(p_lo + row * S + c), pl);
+      dv[i][0] = d.x; dv[i][1] = d.y; dv[i][2] = d.z; dv[i][3] = d.w;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        pv[i][j] = c + j <= pos ? __fadd_rn(ph[j], pl[j]) : 0.f;
+        dot += pv[i][j] * dv[i][j];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pv[i][j] = dv[i][j] = 0.f;
+    }
+  }
   dot = block_sum<kSoftThreads>(dot, sh);
   const int lim = write_limit(pos, S, band);
-  for (int c = threadIdx.x; c < lim; c += kSoftThreads) {
-    const float v = c <= pos ? scale * pr[c] * (dr[c] - dot) : 0.f;
-    put_split(hi, lo, row * S + c, v);
+#pragma unroll
+  for (int i = 0; i < kSoftVec; ++i) {
+    const int c = (i * kSoftThreads + threadIdx.x) * 4;
+    if (c < lim) {
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = scale * pv[i][j] * (dv[i][j] - dot);
+      put_split4(hi, lo, row * S + c, make_float4(o[0], o[1], o[2], o[3]));
+    }
   }
 }
 
@@ -429,19 +490,28 @@ extern "C" int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t
   return launch_status();
 }
 
-extern "C" int mr_softmax_causal_split(float* scores, int64_t rows, int s, float scale, int band,
-                                       uint16_t* hi, uint16_t* lo, void* stream) {
+extern "C" int mr_softmax_causal_split(const float* scores, int64_t rows, int s, float scale,
+                                       int band, uint16_t* hi, uint16_t* lo, void* stream) {
   if (!scores || !hi || !lo || rows <= 0 || s <= 0 || rows % s) return MR_ERR_ARGUMENT;
+  if (s % 4 || s > 4 * kSoftVec * kSoftThreads) return MR_ERR_ARGUMENT;
+  if (!aligned16(scores) || (reinterpret_cast<uintptr_t>(hi) & 7u) ||
+      (reinterpret_cast<uintptr_t>(lo) & 7u))
+    return MR_ERR_ALIGNMENT;
   softmax_causal_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       scores, s, scale, band, hi, lo);
   return launch_status();
 }
 
-extern "C" int mr_softmax_bwd_split(const float* dp, const float* p, int64_t rows, int s,
-                                    float scale, int band, uint16_t* hi, uint16_t* lo,
-                                    void* stream) {
-  if (!dp || !p || !hi || !lo || rows <= 0 || s <= 0 || rows % s) return MR_ERR_ARGUMENT;
+extern "C" int mr_softmax_bwd_split(const float* dp, const uint16_t* p_hi, const uint16_t* p_lo,
+                                    int64_t rows, int s, float scale, int band, uint16_t* hi,
+                                    uint16_t* lo, void* stream) {
+  if (!dp || !p_hi || !p_lo || !hi || !lo || rows <= 0 || s <= 0 || rows % s)
+    return MR_ERR_ARGUMENT;
+  if (s % 4 || s > 4 * kSoftVec * kSoftThreads) return MR_ERR_ARGUMENT;
+  if (!aligned16(dp) || ((reinterpret_cast<uintptr_t>(p_hi) | reinterpret_cast<uintptr_t>(p_lo) |
+                          reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 7u))
+    return MR_ERR_ALIGNMENT;
   softmax_bwd_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      dp, p, s, scale, band, hi, lo);
+      dp, p_hi, p_lo, s, scale, band, hi, lo);
   return launch_status();
 }

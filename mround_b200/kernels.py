@@ -450,7 +450,8 @@ def swiglu_bwd_split(dact, gu, t: int, i: int):
 
 
 def softmax_causal_split(scores, rows: int, s: int, scale: float, band: bool = False):
-    """Causal softmax in place (row r at position r % s); returns the hi/lo parts."""
+    """Causal softmax (row r at position r % s) as bf16 hi/lo parts; ``scores``
+    is left unchanged."""
     hi, lo = _pair(scores.shape, scores.device)
     st = lib().mr_softmax_causal_split(_ptr(scores, torch.float32, "scores", rows * s), rows, s,
                                        float(scale), int(band), hi.data_ptr(), lo.data_ptr(),
@@ -461,10 +462,13 @@ def softmax_causal_split(scores, rows: int, s: int, scale: float, band: bool = F
 
 
 def softmax_bwd_split(dp, p, rows: int, s: int, scale: float, band: bool = False):
+    """Softmax backward from dP (float32) and P as its (hi, lo) parts."""
     hi, lo = _pair(dp.shape, dp.device)
     st = lib().mr_softmax_bwd_split(_ptr(dp, torch.float32, "dp", rows * s),
-                                    _ptr(p, torch.float32, "p", rows * s), rows, s, float(scale),
-                                    int(band), hi.data_ptr(), lo.data_ptr(), _stream())
+                                    _ptr(p[0], torch.bfloat16, "p_hi", rows * s),
+                                    _ptr(p[1], torch.bfloat16, "p_lo", rows * s), rows, s,
+                                    float(scale), int(band), hi.data_ptr(), lo.data_ptr(),
+                                    _stream())
     check(st, "mr_softmax_bwd_split")
     _count()
     return hi, lo

@@ -301,7 +301,8 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     scores = torch.empty((nb, rep * s, s), dtype=torch.float32, device=x.device)
     _bmm(q, k, scores, m=rep * s, n=s, k=d, batch=nb, a_kmajor=True, b_kmajor=True, lda=d, ldb=d,
          sa=rep * s * d, sb=s * d, sc=rep * s * s, causal=c1, seq=s)
-    probs = kernels.softmax_causal_split(scores, nb * rep * s, s, scale, band)  # scores -> P
+    probs = kernels.softmax_causal_split(scores, nb * rep * s, s, scale, band)  # P as hi/lo
+    del scores
     o = torch.empty((b, hq, s, d), dtype=torch.float32, device=x.device)
     _bmm(probs, v, o, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,
          sa=rep * s * s, sb=s * d, sc=rep * s * d, causal=c2, seq=s)
@@ -329,7 +330,7 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
         lda=inter, ldb=inter, prec=_wprec(dn_l, prec.forward), accumulate=True)
     saved = None
     if save:
-        saved = dict(shape=(b, s, h), h1=(h1[0], h1[1]), q=q, k=k, v=v, p=scores, probs=probs,
+        saved = dict(shape=(b, s, h), h1=(h1[0], h1[1]), q=q, k=k, v=v, probs=probs,
                      att=att, hres=hres, rstd2=rstd2, h2=(h2_hi, h2_lo), gu=gu, act=act,
                      x=x2, rstd1=h1[2])
     return out.view(b, s, h), saved
@@ -382,13 +383,13 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     datt = input_grad(o_l, g_h, h, hq * d)
     g_o = kernels.heads_split(datt, b, s, hq, d, merge=False)
     del datt
-    q, k, v, p, probs = saved["q"], saved["k"], saved["v"], saved["p"], saved["probs"]
+    q, k, v, probs = saved["q"], saved["k"], saved["v"], saved["probs"]
     band = s % 128 == 0
     c1, c2, c3 = (1, 2, 3) if band else (0, 0, 0)
     dp = torch.empty((nb, rep * s, s), dtype=torch.float32, device=dout.device)
     _bmm(g_o, v, dp, m=rep * s, n=s, k=d, batch=nb, a_kmajor=True, b_kmajor=True, lda=d, ldb=d,
          sa=rep * s * d, sb=s * d, sc=rep * s * s, causal=c1, seq=s)
-    g_s = kernels.softmax_bwd_split(dp, p, nb * rep * s, s, scale, band)
+    g_s = kernels.softmax_bwd_split(dp, probs, nb * rep * s, s, scale, band)
     del dp
     dq = torch.empty((b, hq, s, d), dtype=torch.float32, device=dout.device)
     _bmm(g_s, k, dq, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,

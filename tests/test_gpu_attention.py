@@ -42,3 +42,35 @@ def test_attention_forward_backward(b, hq, hkv, s, d):
     assert relative_error(out.detach().cpu().numpy(), ref.detach().cpu().numpy()) < 5e-5
     for got, want in ((q.grad, q64.grad), (k.grad, k64.grad), (v.grad, v64.grad)):
         assert relative_error(got.cpu().numpy(), want.cpu().numpy()) < 5e-5
+
+
+@pytest.mark.parametrize("s,band", [(64, False), (256, True), (2048, True), (1000, False)])
+def test_softmax_kernels_match_float64(s, band):
+    """K7 causal softmax and its backward against float64: P = hi + lo to 2^-15
+    of the row's maximum; zeros above the diagonal up to the band limit."""
+    from mround_b200 import kernels
+
+    g = torch.Generator(device="cuda").manual_seed(s)
+    rows = 3 * s
+    scores = torch.randn(rows, s, device="cuda", generator=g) * 3.0
+    dp = torch.randn(rows, s, device="cuda", generator=g)
+    scale = 0.088
+    keep = scores.clone()
+    p = kernels.softmax_causal_split(scores, rows, s, scale, band)
+    ds = kernels.softmax_bwd_split(dp, p, rows, s, scale, band)
+    torch.cuda.synchronize()
+    assert torch.equal(scores, keep), "scores are read-only"
+    pos = torch.arange(rows, device="cuda") % s
+    col = torch.arange(s, device="cuda")
+    mask = col[None, :] <= pos[:, None]
+    ref = torch.softmax((scores.double() * scale).masked_fill(~mask, float("-inf")), -1)
+    got = p[0].double() + p[1].double()
+    dref = scale * ref * (dp.double() - (dp.double() * ref).sum(-1, keepdim=True))
+    dgot = ds[0].double() + ds[1].double()
+    lim = torch.minimum(((pos // 128) + 2) * 128, torch.tensor(s, device="cuda")) if band \
+        else torch.full_like(pos, s)
+    written = col[None, :] < lim[:, None]
+    assert ((got - ref).abs() * written).max() <= 2.0 ** -15
+    assert (got[written & ~mask] == 0).all()
+    tol = 2.0 ** -14 * dref.abs().max()
+    assert ((dgot - dref).abs() * written).max() <= tol
