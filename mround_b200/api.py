@@ -6,9 +6,10 @@ hold, load the model, build calibration, optionally score and plan mixed
 precision, run the block loop, round the remainder to nearest, export, write
 ``mround_run.json``.  Differences, all refusals rather than substitutions:
 
-- the model is a synthetic architecture (``"synthetic:<arch>[@seed]"``, e.g.
-  ``"synthetic:qwen2.5-7b"``) -- checkpoint loading (reference
-  mround/pipeline/loader.py) is not on this path;
+- the model is a local Llama/Qwen2 checkpoint directory (config.json +
+  safetensors, bf16 linears; :mod:`mround_b200.pipeline.loader`) or a
+  synthetic architecture (``"synthetic:<arch>[@seed]"``, e.g.
+  ``"synthetic:qwen2.5-7b"``) -- Hub downloads need a network;
 - calibration ``"auto"`` is Zipf(1.1) token ids over the vocabulary (the
   reference's pile-10k is not available offline);
 - every scheme the reference defines runs on the device (asymmetric and
@@ -95,17 +96,24 @@ def default_scale_init(narrowest_width: int, symmetry: Symmetry) -> ScaleInit:
     return ScaleInit.SEARCHED if narrowest_width < LOW_BIT_THRESHOLD else ScaleInit.OBSERVED_RANGE
 
 
-def load_model(model: str | Path | SyntheticModel) -> SyntheticModel:
-    if isinstance(model, SyntheticModel):
+def load_model(model):
+    """A synthetic architecture (``"synthetic:<arch>[@seed]"``), a local
+    Hugging Face checkpoint directory (config.json + safetensors; Llama or
+    Qwen2), or an already-built model object."""
+    from mround_b200.pipeline.loader import CheckpointModel, is_checkpoint_dir
+
+    if isinstance(model, (SyntheticModel, CheckpointModel)):
         return model
     text = str(model)
     if text.startswith("synthetic:"):
         spec = text.split(":", 1)[1]
         name, _, seed = spec.partition("@")
         return SyntheticModel(get_arch(name), seed=int(seed) if seed else 0)
+    if is_checkpoint_dir(text):
+        return CheckpointModel(text)
     raise ArchitectureError(
-        f"cannot load {text!r}: the B200 path quantizes synthetic architectures "
-        "(\"synthetic:<arch>[@seed]\"); checkpoint loading is not implemented here")
+        f"cannot load {text!r}: give a local checkpoint directory (config.json + safetensors) "
+        "or \"synthetic:<arch>[@seed]\"; there is no network for Hub downloads")
 
 
 def _resolve_scheme(*, bits, group_size, symmetry, average_bits, candidate_bits, remainder_bits,

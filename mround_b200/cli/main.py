@@ -2,8 +2,8 @@
 
 Restates the ``quantize`` sub-command of reference mround/cli/main.py:41-245,
 529-583: same flags and defaults; ``eval`` and ``doctor`` are not on the tuning
-path and are not provided.  The model argument is a synthetic architecture
-(``synthetic:qwen2.5-7b``).  Under torchrun each rank takes a shard of every
+path and are not provided.  The model argument is a local Llama/Qwen2
+checkpoint directory or a synthetic architecture (``synthetic:qwen2.5-7b``).  Under torchrun each rank takes a shard of every
 calibration batch.
 """
 
@@ -30,7 +30,8 @@ def build_parser() -> argparse.ArgumentParser:
     parser.add_argument("--version", action="version", version=f"mround-b200 {__version__}")
     sub = parser.add_subparsers(dest="command", required=True)
     q = sub.add_parser("quantize", help="Quantize a model and write an MLX checkpoint.")
-    q.add_argument("model", help="synthetic:<arch>[@seed], e.g. synthetic:qwen2.5-7b")
+    q.add_argument("model", help="a local Llama/Qwen2 checkpoint directory, or synthetic:<arch>[@seed] "
+                   "(e.g. synthetic:qwen2.5-7b)")
     q.add_argument("--output-dir", "-o", required=True)
     q.add_argument("--bits", type=int, default=4)
     q.add_argument("--group-size", type=int, default=64)

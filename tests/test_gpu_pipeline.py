@@ -162,3 +162,27 @@ def test_smollm2_config1_end_to_end(tmp_path):
     assert len(res.summary.blocks) == 30
     assert res.summary.mean_improvement > 0.0
     assert all(b.final_loss <= b.initial_loss for b in res.summary.blocks)
+
+
+def test_quantize_from_checkpoint_directory_matches_synthetic(tmp_path):
+    """A local HF checkpoint holding the same weights gives the same checkpoint,
+    tensor for tensor, as the synthetic model (the pipeline is deterministic)."""
+    from mround_b200.api import quantize
+    from mround_b200.formats.safetensors_io import read_safetensors
+    from mround_b200.schemes import TuningConfig
+    from tests.test_loader import write_checkpoint
+
+    ck = tmp_path / "ck"
+    ck.mkdir()
+    write_checkpoint(ck, "tiny-qwen2", seed=3)
+    tuning = TuningConfig(iters=6, n_samples=4, seq_len=64, batch_size=2)
+    out_a, out_b = tmp_path / "a", tmp_path / "b"
+    quantize(str(ck), output_dir=out_a, bits=2, group_size=32, symmetry="asym", tuning=tuning,
+             progress=None)
+    quantize("synthetic:tiny-qwen2@3", output_dir=out_b, bits=2, group_size=32, symmetry="asym",
+             tuning=tuning, progress=None)
+    a, _, _ = read_safetensors(out_a / "model.safetensors")
+    b, _, _ = read_safetensors(out_b / "model.safetensors")
+    assert set(a) == set(b)
+    for name in a:
+        assert np.array_equal(a[name], b[name]), name
