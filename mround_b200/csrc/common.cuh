@@ -72,11 +72,14 @@ __device__ __forceinline__ uint4 pack8(const uint16_t (&h)[8]) {
 // group, so quotients stay within a few thousand in magnitude; a quotient in
 // the subnormal range (a denormal weight) only ever feeds rint(q + v) with
 // |v| <= 0.5 or q == 0, where a last-bit difference cannot change the code.
+// A zero numerator returns a * y, which carries the IEEE quotient's sign of
+// zero (the correction step would turn -0 into +0; the zero point rint(-0/s)
+// = -0 reaches the stored bias through its sign).
 // mr_selftest_division compares it against __fdiv_rn on the device.
 __device__ __forceinline__ float div_rcp(float a, float b, float y) {
   const float q = __fmul_rn(a, y);
   const float r = __fmaf_rn(-q, b, a);
-  return __fmaf_rn(r, y, q);
+  return a == 0.f ? q : __fmaf_rn(r, y, q);
 }
 
 // Streaming loads/stores: the weight-sized tensors are touched once per pass.

@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
           const float neg = -w_min;
           const bool pos = w_max >= neg;
           const float dom = pos ? w_max : neg;
-          scale = clamp_mag(__fdiv_rn(pos ? -dom : dom, maxq), eps);
+          scale = clamp_mag(div_rcp(pos ? -dom : dom, maxq, __frcp_rn(maxq)), eps);
         }
         const float rcp = __frcp_rn(scale);
         const float hi = __fsub_rn(maxq, 1.f);
@@ -100,9 +100,9 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
           part = __fadd_rn(part, fabsf(__fmul_rn(gf[i], __fsub_rn(q, wf[i]))));
         }
       } else {
-        const float scale = fmaxf(__fdiv_rn(__fsub_rn(w_max, w_min), maxq), eps);
-        const float zp = rintf(__fdiv_rn(-w_min, scale));
+        const float scale = fmaxf(div_rcp(__fsub_rn(w_max, w_min), maxq, __frcp_rn(maxq)), eps);
         const float rcp = __frcp_rn(scale);
+        const float zp = rintf(div_rcp(-w_min, scale, rcp));
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float x = __fadd_rn(rintf(div_rcp(wf[i], scale, rcp)), zp);

@@ -11,10 +11,14 @@
 // Groups never straddle a tile because group divides 256.
 //
 // Arithmetic follows the float32 operation order of the reference quantizer
-// (mround/core/quantizer.py:185-195, 254-266, 341-347, 395-398) with IEEE
-// division (__fdiv_rn) and ties-to-even rounding (rintf), and no contraction
-// into FMA on the code path, so codes and reconstructions are bit-exact
-// against a float32 implementation of the same formulas.
+// (mround/core/quantizer.py:185-195, 254-266, 341-347, 395-398) with correctly
+// rounded division (a reciprocal and Markstein's correction, div_rcp in
+// common.cuh, bit-identical to IEEE division) and ties-to-even rounding
+// (rintf), and no contraction into FMA on the code path, so codes and
+// reconstructions are bit-exact against a float32 implementation of the same
+// formulas.
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -88,17 +92,19 @@ __device__ __forceinline__ GroupQ group_params(float gmax, float gmin, float alp
   if constexpr (MODE == kAsym) {
     const float w_max = __fmul_rn(q.wmax_raw, alpha);
     const float w_min = __fmul_rn(q.wmin_raw, beta);
-    const float span = __fdiv_rn(__fsub_rn(w_max, w_min), maxq);
+    const float span = div_rcp(__fsub_rn(w_max, w_min), maxq, __frcp_rn(maxq));
     q.live = span > eps;
     q.scale = fmaxf(span, eps);
-    q.zp = rintf(__fdiv_rn(-w_min, q.scale));
+    q.rcp = __frcp_rn(q.scale);
+    q.zp = rintf(div_rcp(-w_min, q.scale, q.rcp));
     q.w_min = w_min;
   } else if constexpr (MODE == kSym) {
     const float w_max = __fmul_rn(q.wmax_raw, alpha);
     const float neg = -__fmul_rn(q.wmin_raw, beta);
     q.pos = w_max >= neg;
     const float dominant = q.pos ? w_max : neg;
-    q.scale = clamp_magnitude(__fdiv_rn(q.pos ? -dominant : dominant, maxq), eps, q.live);
+    q.scale = clamp_magnitude(div_rcp(q.pos ? -dominant : dominant, maxq, __frcp_rn(maxq)), eps,
+                              q.live);
   } else {
     q.scale = clamp_magnitude(__fmul_rn(base, beta), eps, q.live);
   }
@@ -267,7 +273,7 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
 
     float gv[8];
     float sum_t = 0.f, sum_out = 0.f;
-    const float wmin_s = MODE == kAsym ? __fdiv_rn(q.w_min, q.scale) : 0.f;  // per group
+    const float wmin_s = MODE == kAsym ? div_rcp(q.w_min, q.scale, q.rcp) : 0.f;  // per group
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float ws = over_scale(wf[i], q);
@@ -290,11 +296,11 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
     if (!in) continue;
     float ga, gb;
     if constexpr (MODE == kAsym) {
-      const float gs = q.live ? __fdiv_rn(sum_t, maxq) : 0.f;
+      const float gs = q.live ? div_rcp(sum_t, maxq, __frcp_rn(maxq)) : 0.f;
       ga = __fmul_rn(gs, q.wmax_raw);
       gb = __fmul_rn(__fsub_rn(sum_out, gs), q.wmin_raw);
     } else if constexpr (MODE == kSym) {
-      const float gs = q.live ? __fdiv_rn(sum_t, maxq) : 0.f;  // maxq = 2^(b-1): exact
+      const float gs = q.live ? div_rcp(sum_t, maxq, __frcp_rn(maxq)) : 0.f;  // 2^(b-1): exact
       ga = q.pos ? -__fmul_rn(gs, q.wmax_raw) : 0.f;
       gb = q.pos ? 0.f : -__fmul_rn(gs, q.wmin_raw);
     } else {
@@ -337,16 +343,20 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
 // biases = bf16(-scales * zp), zp the zero point or the fixed 2^(b-1)
 // (mlx_export.py:159-195).  ``codes_out`` receives the codes one byte each:
 // uint8 under kAsym, int8 (two's complement) under the symmetric schemes.
-template <int LPG, int MODE>
+// The code width is a template parameter: the lane's 8 codes form a chunk of
+// 8 * BITS bits with constant shifts (one 32-bit word for BITS <= 4).
+template <int LPG, int MODE, int BITS>
 __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
     const uint16_t* __restrict__ w, const float* __restrict__ v, const float* __restrict__ alpha,
     const float* __restrict__ beta, const float* __restrict__ init_scale, int64_t n, int group,
-    int bits, float maxq, float eps, uint32_t* __restrict__ packed, uint16_t* __restrict__ scales,
+    float maxq, float eps, uint32_t* __restrict__ packed, uint16_t* __restrict__ scales,
     uint16_t* __restrict__ biases, uint8_t* __restrict__ codes_out) {
+  constexpr int bits = BITS;
+  using Chunk = typename std::conditional<(8 * BITS <= 32), uint32_t, uint64_t>::type;
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   const int64_t total_words = n * bits / 32;
-  const int chunk_bits = 8 * bits;  // bits one lane contributes, 16..64
+  constexpr int chunk_bits = 8 * bits;  // bits one lane contributes, 16..64
   const float offset = MODE == kAsym ? 0.f : maxq;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
        t += int64_t(gridDim.x) * kWarps) {
@@ -362,7 +372,7 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
     }
     float gmax, gmin;
     extremes_for<LPG, MODE>(wf, gmax, gmin);
-    uint64_t chunk = 0;
+    Chunk chunk = 0;
     if (in) {
       const int64_t gi = e / group;
       const GroupQ q = group_params<MODE>(gmax, gmin, alpha[gi], beta[gi],
@@ -372,7 +382,7 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
       for (int i = 0; i < 8; ++i) {
         const float code = clamp_code<MODE>(unclamped_code<MODE>(wf[i], vf[i], q), maxq);
         c8[i] = uint8_t(int(code));
-        chunk |= uint64_t(uint32_t(__fadd_rn(code, offset))) << (i * bits);
+        chunk |= Chunk(uint32_t(__fadd_rn(code, offset))) << (i * bits);
       }
       if (codes_out) {
         uint2 u;
@@ -389,15 +399,13 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
     }
     // Widths dividing 32 need no cross-lane assembly beyond a pair of lanes:
     // 4 bits -> one word per lane, 8 bits -> two, 2 bits -> half a word.
-    if (bits == 4) {
+    if constexpr (BITS == 4) {
       if (in) packed[e / 8] = uint32_t(chunk);
       continue;
-    }
-    if (bits == 8) {
-      if (in) *reinterpret_cast<uint2*>(packed + e / 4) = make_uint2(uint32_t(chunk), uint32_t(chunk >> 32));
+    } else if constexpr (BITS == 8) {
+      if (in) *reinterpret_cast<uint2*>(packed + e / 4) = make_uint2(uint32_t(chunk), uint32_t(uint64_t(chunk) >> 32));
       continue;
-    }
-    if (bits == 2) {
+    } else if constexpr (BITS == 2) {
       const uint32_t other = __shfl_xor_sync(0xffffffffu, uint32_t(chunk), 1);
       if (in && (lane & 1) == 0) packed[e / 16] = (uint32_t(chunk) & 0xFFFFu) | (other << 16);
       continue;
@@ -410,9 +418,9 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
       const int src = bitpos / chunk_bits;
       const int off = bitpos - src * chunk_bits;
       const uint32_t lo0 = __shfl_sync(0xffffffffu, uint32_t(chunk), src & 31);
-      const uint32_t hi0 = __shfl_sync(0xffffffffu, uint32_t(chunk >> 32), src & 31);
+      const uint32_t hi0 = __shfl_sync(0xffffffffu, uint32_t(uint64_t(chunk) >> 32), src & 31);
       const uint32_t lo1 = __shfl_sync(0xffffffffu, uint32_t(chunk), (src + 1) & 31);
-      const uint32_t hi1 = __shfl_sync(0xffffffffu, uint32_t(chunk >> 32), (src + 1) & 31);
+      const uint32_t hi1 = __shfl_sync(0xffffffffu, uint32_t(uint64_t(chunk) >> 32), (src + 1) & 31);
       if (j < chunk_bits) {
         const uint64_t c0 = (uint64_t(hi0) << 32) | lo0;
         const uint64_t c1 = (src + 1 < 32) ? ((uint64_t(hi1) << 32) | lo1) : 0ull;
@@ -532,7 +540,41 @@ extern "C" int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* 
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
   const float maxq = mode_maxq(mode, bits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  MR_DISPATCH(mode, group, pack_mlx_kernel, grid, s, w_bf16, v, alpha, beta, init_scale, n, group,
-              bits, maxq, eps, packed, scales_bf16, biases_bf16, codes);
+#define MR_PACK_LPG(MODE, B)                                                                 \
+  switch (group / 8) {                                                                       \
+    case 1: pack_mlx_kernel<1, MODE, B><<<grid, kThreads, 0, s>>>(MR_PACK_ARGS); break;      \
+    case 2: pack_mlx_kernel<2, MODE, B><<<grid, kThreads, 0, s>>>(MR_PACK_ARGS); break;      \
+    case 4: pack_mlx_kernel<4, MODE, B><<<grid, kThreads, 0, s>>>(MR_PACK_ARGS); break;      \
+    case 8: pack_mlx_kernel<8, MODE, B><<<grid, kThreads, 0, s>>>(MR_PACK_ARGS); break;      \
+    case 16: pack_mlx_kernel<16, MODE, B><<<grid, kThreads, 0, s>>>(MR_PACK_ARGS); break;    \
+    case 32: pack_mlx_kernel<32, MODE, B><<<grid, kThreads, 0, s>>>(MR_PACK_ARGS); break;    \
+    default: return MR_ERR_ARGUMENT;                                                         \
+  }
+#define MR_PACK_ARGS \
+  w_bf16, v, alpha, beta, init_scale, n, group, maxq, eps, packed, scales_bf16, biases_bf16, codes
+#define MR_PACK_BITS(B)                                                                      \
+  case B: {                                                                                  \
+    if (mode == kAsym) {                                                                     \
+      MR_PACK_LPG(kAsym, B)                                                                  \
+    } else if (mode == kSym) {                                                               \
+      MR_PACK_LPG(kSym, B)                                                                   \
+    } else {                                                                                 \
+      MR_PACK_LPG(kSearched, B)                                                              \
+    }                                                                                        \
+    break;                                                                                   \
+  }
+  switch (bits) {
+    MR_PACK_BITS(2)
+    MR_PACK_BITS(3)
+    MR_PACK_BITS(4)
+    MR_PACK_BITS(5)
+    MR_PACK_BITS(6)
+    MR_PACK_BITS(7)
+    MR_PACK_BITS(8)
+    default: return MR_ERR_ARGUMENT;
+  }
+#undef MR_PACK_BITS
+#undef MR_PACK_ARGS
+#undef MR_PACK_LPG
   return launch_status();
 }

@@ -312,7 +312,14 @@ def test_division_matches_ieee_over_quantizer_range(K):
     # bf16-valued weights against scales built like the quantizer's
     a[: n // 2] = a[: n // 2].to(torch.bfloat16).float()
     a[:1024] = 0.0
+    a[1024:2048] = -0.0  # the zero point of a group without negative weights: rint(-0 / s)
     b[:2048] = 1e-8
+    # signed (symmetric) scales, and the constant divisors 2^b - 1 and 2^(b-1)
+    b[n // 4: n // 2] = -b[n // 4: n // 2]
+    divisors = torch.tensor([3.0, 7.0, 15.0, 31.0, 63.0, 127.0, 255.0, 2.0, 4.0, 128.0],
+                            device="cuda")
+    b[n // 2: n // 2 + (1 << 20)] = divisors[torch.randint(0, 10, (1 << 20,), device="cuda",
+                                                           generator=g)]
     bad = torch.zeros(1, dtype=torch.int32, device="cuda")
     assert lib().mr_selftest_division(a.data_ptr(), b.data_ptr(), n, bad.data_ptr(), None) == 0
     torch.cuda.synchronize()
