@@ -203,9 +203,15 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
     const int64_t e = t * kTile + lane * 8;
     const bool in = e < n;
     float wf[8], vf[8];
+    // the group's coefficients are loaded with the tile, not after its reductions
+    const int64_t gi = in ? e / group : 0;
+    float ga = 1.f, gb = 1.f, gs = 0.f;
     if (in) {
       unpack8(ld_stream(reinterpret_cast<const uint4*>(w + e)), wf);
       load_f8(v + e, vf);
+      ga = alpha[gi];
+      gb = beta[gi];
+      if (MODE == kSearched) gs = init_scale[gi];
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) wf[i] = vf[i] = 0.f;
@@ -213,9 +219,7 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
     float gmax, gmin;
     extremes_for<LPG, MODE>(wf, gmax, gmin);
     if (!in) continue;  // whole groups lie past the end together
-    const int64_t gi = e / group;
-    const GroupQ q = group_params<MODE>(gmax, gmin, alpha[gi], beta[gi],
-                                        MODE == kSearched ? init_scale[gi] : 0.f, maxq, eps);
+    const GroupQ q = group_params<MODE>(gmax, gmin, ga, gb, gs, maxq, eps);
     float wq[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -255,20 +259,21 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
     const int64_t e = t * kTile + lane * 8;
     const bool in = e < n;
     float wf[8], vf[8], g[8];
+    const int64_t gi = in ? e / group : 0;
+    float a = 1.f, b = 1.f, base = 1.f;
     if (in) {
       unpack8(ld_stream(reinterpret_cast<const uint4*>(w + e)), wf);
       load_f8(v + e, vf);
       load_f8(gq + e, g);
+      a = alpha[gi];
+      b = beta[gi];
+      if (MODE == kSearched) base = init_scale[gi];
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) wf[i] = vf[i] = g[i] = 0.f;
     }
     float gmax, gmin;
     extremes_for<LPG, MODE>(wf, gmax, gmin);
-    const int64_t gi = in ? e / group : 0;
-    const float a = in ? alpha[gi] : 1.f;
-    const float b = in ? beta[gi] : 1.f;
-    const float base = (MODE == kSearched && in) ? init_scale[gi] : 1.f;
     const GroupQ q = group_params<MODE>(gmax, gmin, a, b, base, maxq, eps);
 
     float gv[8];
@@ -363,9 +368,14 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
     const int64_t e = t * kTile + lane * 8;
     const bool in = e < n;
     float wf[8], vf[8];
+    const int64_t gi = in ? e / group : 0;
+    float ga = 1.f, gb = 1.f, gs = 0.f;
     if (in) {
       unpack8(ld_stream(reinterpret_cast<const uint4*>(w + e)), wf);
       load_f8(v + e, vf);
+      ga = alpha[gi];
+      gb = beta[gi];
+      if (MODE == kSearched) gs = init_scale[gi];
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) wf[i] = vf[i] = 0.f;
@@ -374,9 +384,7 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
     extremes_for<LPG, MODE>(wf, gmax, gmin);
     Chunk chunk = 0;
     if (in) {
-      const int64_t gi = e / group;
-      const GroupQ q = group_params<MODE>(gmax, gmin, alpha[gi], beta[gi],
-                                          MODE == kSearched ? init_scale[gi] : 0.f, maxq, eps);
+      const GroupQ q = group_params<MODE>(gmax, gmin, ga, gb, gs, maxq, eps);
       uint8_t c8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
