@@ -179,7 +179,7 @@ def _rtn_layer(weight: torch.Tensor, scheme: QuantScheme, device) -> QuantizedLa
 
 
 def _plan_mixed(model, resolved, average_bits, candidate_bits, *, gradient_source, scoring_samples,
-                scoring_seq_len, scoring_batch_size, seed, device, given_plan=None):
+                scoring_seq_len, scoring_batch_size, seed, device, given_plan=None, dist=None):
     from mround_b200.pipeline.scoring import score_widths
     from mround_b200.planner.allocator import allocate_bits
     from mround_b200.planner.sensitivity import (
@@ -206,7 +206,8 @@ def _plan_mixed(model, resolved, average_bits, candidate_bits, *, gradient_sourc
     bsz = scoring_batch_size or batch_rule(n, s)
     tokens = zipf_tokens(arch.vocab, n, s, seed=DEFAULT_SEED if seed is None else seed)
     batches = [tokens[i:i + bsz] for i in range(0, n - bsz + 1, bsz)]
-    scored = score_widths(model, batches, widths, resolved, gradient_source=source, device=device)
+    scored = score_widths(model, batches, widths, resolved, gradient_source=source, device=device,
+                          dist=dist)
     budget = mixed_budget_bits(scored.shapes, average_bits, resolved.group_size)
     options = score_layer_options(scored.scores, scored.shapes, resolved)
     alloc = allocate_bits(options, budget_bits=budget)
@@ -306,7 +307,8 @@ def quantize(model: str | Path | SyntheticModel, *, output_dir: str | Path, bits
         overrides, plan_info = _plan_mixed(
             bundle, resolved, average_bits, candidate_bits, gradient_source=sensitivity_gradients,
             scoring_samples=scoring_samples, scoring_seq_len=scoring_seq_len,
-            scoring_batch_size=scoring_batch_size, seed=seed, device=device, given_plan=plan)
+            scoring_batch_size=scoring_batch_size, seed=seed, device=device, given_plan=plan,
+            dist=dist)
         remainder_scheme = resolved.with_bits(_remainder_width(average_bits, candidate_bits,
                                                                remainder_bits))
         plan_info["remainder_bits"] = remainder_scheme.bits

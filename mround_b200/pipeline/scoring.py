@@ -34,6 +34,7 @@ import torch
 from mround_b200 import kernels
 from mround_b200.exceptions import SchemeError
 from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision
+from mround_b200.pipeline.dist import DistContext
 from mround_b200.pipeline.model import SyntheticModel
 from mround_b200.core.scale_search import search_scales
 from mround_b200.schemes import DEFAULT_EPS_FP32, QuantScheme, ScaleInit, Symmetry
@@ -53,8 +54,14 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
                  base_scheme: QuantScheme, *, expected_blocks: int | None = None,
                  eps: float = DEFAULT_EPS_FP32, gradient_source: str = "own_width",
                  progress: Callable[[str], None] | None = None,
-                 device: torch.device | str = "cuda") -> SensitivityScores:
-    """Score every block linear at every width (float64 sums on the device)."""
+                 device: torch.device | str = "cuda",
+                 dist: DistContext | None = None) -> SensitivityScores:
+    """Score every block linear at every width (float64 sums on the device).
+
+    Under data parallelism (``dist`` with several ranks) rank r takes batches
+    r, r + N, ...; the per-layer float64 sums are all-reduced, so every rank
+    ends with the scores of all batches and plans identically.
+    """
     if not widths:
         raise ValueError("no candidate widths to score")
     if gradient_source not in ("own_width", "widest"):
@@ -203,15 +210,22 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
 
     schedule = [(w, [w]) for w in widths] if gradient_source == "own_width" else [(widths[-1], widths)]
     done = 0
+    dist = dist or DistContext()
+    mine = list(batches)[dist.rank::dist.world]
     for anchor_bits, scored in schedule:
         set_anchors(anchor_bits)
         active["bits"] = scored
-        for batch in batches:
+        for batch in mine:
             backward_pass(batch)
             done += 1
             if progress is not None:
-                progress(f"  scoring: backward {done}/{len(batches) * len(schedule)} "
+                progress(f"  scoring: backward {done}/{len(mine) * len(schedule)} "
                          f"at {time.perf_counter() - started:.0f}s")
+    if dist.world > 1:
+        names = sorted(acc)
+        stacked = torch.stack([acc[p] for p in names])
+        dist.all_reduce_(stacked)
+        acc = {p: stacked[i] for i, p in enumerate(names)}
     torch.cuda.synchronize(dev)
     for blk in blocks:
         for layer in blk.layers.values():

@@ -123,3 +123,60 @@ def test_two_gpu_step_matches_single_process():
     differing = sum(int((a != b).sum()) for a, b in zip(res[0][3], want_v))
     total = sum(a.size for a in want_v)
     assert differing / total < 1e-3, f"{differing} of {total} V entries differ"
+
+
+def _score_rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as tdist
+
+    from mround_b200.pipeline.dist import DistContext
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    tdist.init_process_group("nccl", rank=rank, world_size=world,
+                             timeout=datetime.timedelta(seconds=120))
+    try:
+        got = _scores(torch.device("cuda", rank), DistContext(rank, world))
+        q.put((rank, got))
+        tdist.barrier()
+    finally:
+        tdist.destroy_process_group()
+
+
+def _scores(device, dist):
+    from mround_b200.pipeline.arch import get_arch
+    from mround_b200.pipeline.model import SyntheticModel, zipf_tokens
+    from mround_b200.pipeline.scoring import score_widths
+    from mround_b200.schemes import QuantScheme
+
+    model = SyntheticModel(get_arch(ARCH), seed=4)
+    tokens = zipf_tokens(model.arch.vocab, 4, 33, seed=1)
+    batches = [tokens[i:i + 1] for i in range(4)]
+    scheme = QuantScheme(bits=4, group_size=32, symmetry="asym")
+    return score_widths(model, batches, (2, 3, 4), scheme, device=device, dist=dist).scores
+
+
+def test_two_gpu_scoring_matches_single_process():
+    """DeltaLoss scoring with the batches split over two ranks (float64 sums
+    all-reduced) equals the single-process scores, on both ranks."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from mround_b200.pipeline.dist import DistContext
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_score_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    want = _scores(torch.device("cuda", 0), DistContext())
+    for _, got in res:
+        assert set(got) == set(want)
+        for layer in want:
+            for bits in (2, 3, 4):
+                assert got[layer][bits] == pytest.approx(want[layer][bits], rel=1e-12)
