@@ -414,6 +414,9 @@ def main():
         "config": {"workload": f"{args.arch} block SignRound step, W{args.bits} asym g{args.group}, "
                                f"global batch {BATCH}x{SEQ}, {ITERS} it/block, {N_BATCHES} batches",
                    "global_batch": BATCH, "seq_len": SEQ, "parallelism": f"dp{dist.world}",
+                   "gradient_exchange": ("none" if dist.world == 1 else
+                                         "fused dW GEMM -> reduce-scatter over NVLink peer stores"
+                                         if tuner.peer is not None else "NCCL reduce-scatter"),
                    "l2": "inputs larger than L2 (235 MB per batch input)"},
         "ms_forward_batch": t_fwd, "block_seconds": blk_s, "wall_s_model": blk_s * arch.layers,
         "gpu_launches": launches,
@@ -435,6 +438,7 @@ def main():
             out["cpu_baseline"] = {"value": None, "error": str(exc)}
     if dist.rank == 0:
         print(json.dumps(out), file=out_stream, flush=True)
+    tuner.close()
     if dist.world > 1:
         import torch.distributed as tdist
 

@@ -347,6 +347,52 @@ int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int
  * reset != 0 clears it. */
 int mr_gemm_status(int reset);
 
+/*
+ * K3 fused with the data-parallel reduce-scatter of a weight gradient.
+ * Replaces the gradient all-reduce of the data-parallel step (the reference's
+ * micro-batch sum, mround/pipeline/runner.py:984-1044, across GPUs): the same
+ * GEMM as mr_gemm (no bias, no accumulate, batch 1), but row r of the
+ * (m, n) result is stored over NVLink into its owner's slot,
+ *   dst[r / rows_per_rank] + (r % rows_per_rank) * ldd,
+ * where dst[o] is rank o's slot buffer for this source rank (a peer pointer
+ * from mr_ipc_import, or local memory for this rank's own rows);
+ * m == rows_per_rank * world.  After every tile is stored, the kernel
+ * releases ``epoch`` (> 0, increasing) into flags[o] on every rank o, each a
+ * peer pointer to rank o's flag for this source.  ``done`` is a zeroed device
+ * counter owned by this rank (left zero on return).  Plain peer stores only: no
+ * multicast, no loads from peer memory.
+ */
+int mr_gemm_rs(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
+               const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor, int64_t m,
+               int64_t n, int64_t k, int precision, float* const* dst, int64_t ldd,
+               int64_t rows_per_rank, unsigned long long* const* flags, int world,
+               unsigned int* done, unsigned long long epoch, void* stream);
+
+/*
+ * Peer memory of the exchange.  mr_ipc_export writes the CUDA IPC handle
+ * (mr_ipc_handle_bytes() bytes) of the allocation holding ``ptr`` and the
+ * offset of ``ptr`` in it; mr_ipc_import maps a peer's handle into this
+ * device's address space (base, and base + offset in ``ptr``); mr_ipc_close
+ * releases a mapping by its base.
+ */
+size_t mr_ipc_handle_bytes(void);
+int mr_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int mr_ipc_import(const void* handle, int64_t offset, void** base, void** ptr);
+int mr_ipc_close(void* base);
+
+/*
+ * The owner's side of mr_gemm_rs: wait (bounded: 2 s, then the status word
+ * below) until flags[r] >= epoch for every source rank r, then
+ * out[i] = sum over r in rank order of slots[r * slot_stride + i], i < n.
+ * Float32, 16-byte aligned, n and slot_stride multiples of 4.
+ */
+int mr_reduce_slots(const float* slots, int64_t slot_stride, int64_t n, int world,
+                    const unsigned long long* flags, unsigned long long epoch, float* out,
+                    void* stream);
+
+/* Device status word of the exchange (0 ok, MR_ERR_TIMEOUT); synchronizes. */
+int mr_peer_status(int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_gemm_batched": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _I64, _I64, _I, _P, _I64, _I64, _P,
                              _I, _I64, _I64, _I64, _I64, _I, _I, _I64, _P]),
     "mr_gemm_status": (_I, [_I]),
+    "mr_gemm_rs": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I64, _I64, _I64, _I, _P, _I64, _I64,
+                        _P, _I, _P, ctypes.c_uint64, _P]),
+    "mr_ipc_handle_bytes": (ctypes.c_size_t, []),
+    "mr_ipc_export": (_I, [_P, _P, _P]),
+    "mr_ipc_import": (_I, [_P, _I64, _P, _P]),
+    "mr_ipc_close": (_I, [_P]),
+    "mr_reduce_slots": (_I, [_P, _I64, _I64, _I, _P, ctypes.c_uint64, _P, _P]),
+    "mr_peer_status": (_I, [_I]),
     "mr_rmsnorm_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P, _P]),
     "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P, _P]),
     "mr_rope_split": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),

@@ -207,6 +207,23 @@ struct Maps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;
 };
 
+// Fused reduce-scatter epilogue (mr_gemm_rs): row r of C belongs to rank
+// r / rows_per_rank and is stored, over NVLink, into that rank's slot for this
+// source rank (dst[owner] + (r % rows_per_rank) * ldd).  When every CTA has
+// stored its tiles, the last one releases ``epoch`` into flag[owner] on every
+// rank (system scope); the owner waits for all flags before reading its slots.
+constexpr int kMaxRanks = 8;
+struct RemoteOut {
+  float* dst[kMaxRanks];
+  unsigned long long* flag[kMaxRanks];
+  unsigned int* done;  // local CTA counter, zero between launches
+  unsigned long long epoch;
+  long long rows_per_rank;
+  long long ldd;
+  int world;
+  int active;
+};
+
 // Load one operand part (rows x BK) of a stage.  K-major: one box {BK, rows}.
 // MN-major: rows/64 boxes {64, BK} at 64 * BK * 2 bytes spacing.
 template <int ROWS, int BK>
@@ -299,7 +316,8 @@ template <int BN, int BK, int PREC>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
                 int64_t stride_c, const float* __restrict__ bias, int accumulate, int m, int n,
-                int k, int a_kmajor, int b_kmajor, int causal, int clen, int total_tiles) {
+                int k, int a_kmajor, int b_kmajor, int causal, int clen, int total_tiles,
+                const __grid_constant__ RemoteOut remote) {
   using C = Cfg<BN, BK, PREC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -447,7 +465,13 @@ __global__ void __launch_bounds__(192, 1)
           }
           const int gc = tl.n0 + col;
           if (row < m && gc < n) {
-            float* dst = cz + int64_t(row) * ldc + gc;
+            float* dst;
+            if (remote.active) {
+              const int owner = int(row / remote.rows_per_rank);
+              dst = remote.dst[owner] + (row - owner * remote.rows_per_rank) * remote.ldd + gc;
+            } else {
+              dst = cz + int64_t(row) * ldc + gc;
+            }
             const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
             if (full_chunk) {
 #pragma unroll
@@ -477,6 +501,23 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
+    }
+    if (remote.active) {
+      // every epilogue thread's peer stores are ordered before the CTA's
+      // arrival; the last CTA publishes the epoch to every owner
+      __threadfence_system();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0) {
+        const unsigned int prev = atomicAdd(remote.done, 1u);
+        if (prev == gridDim.x - 1) {
+          __threadfence_system();
+          for (int r = 0; r < remote.world; ++r)
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(remote.flag[r]),
+                         "l"(remote.epoch)
+                         : "memory");
+          atomicExch(remote.done, 0u);
+        }
+      }
     }
   }
   tc_fence_before();
@@ -550,7 +591,7 @@ int sm_count() {
 template <int BN, int BK, int PREC>
 int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const float* bias,
            int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
-           int causal, int clen, cudaStream_t stream) {
+           int causal, int clen, const RemoteOut& remote, cudaStream_t stream) {
   using C = Cfg<BN, BK, PREC>;
   static bool configured = false;
   if (!configured) {
@@ -567,7 +608,7 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
   const int grid = int(tiles < sm_count() ? tiles : sm_count());
   gemm_kernel<BN, BK, PREC><<<grid, kThreads, C::kSmem, stream>>>(
       maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor, causal, clen,
-      int(tiles));
+      int(tiles), remote);
   return launch_status();
 }
 
@@ -576,12 +617,13 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
 
 using namespace mr;
 
-extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda,
-                               int64_t stride_a, int a_kmajor, const uint16_t* b_hi,
-                               const uint16_t* b_lo, int64_t ldb, int64_t stride_b, int b_kmajor,
-                               float* c, int64_t ldc, int64_t stride_c, const float* bias,
-                               int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
-                               int precision, int causal, int64_t seq, void* stream) {
+namespace {
+
+int gemm_impl(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int64_t stride_a,
+              int a_kmajor, const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb,
+              int64_t stride_b, int b_kmajor, float* c, int64_t ldc, int64_t stride_c,
+              const float* bias, int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
+              int precision, int causal, int64_t seq, const RemoteOut& remote, void* stream) {
   if (!a_hi || !b_hi || !c || m <= 0 || n <= 0 || k <= 0 || batch <= 0) return MR_ERR_ARGUMENT;
   if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1 || batch > 65535)
     return MR_ERR_ARGUMENT;
@@ -623,11 +665,11 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
 #define MR_GEMM_LAUNCH(BN_, BK_)                                                               \
   switch (precision) {                                                                         \
     case 1: return launch<BN_, BK_, 1>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,     \
-                                       a_kmajor, b_kmajor, bt, causal, int(seq), s);           \
+                                       a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);   \
     case 2: return launch<BN_, BK_, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,     \
-                                       a_kmajor, b_kmajor, bt, causal, int(seq), s);           \
+                                       a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);   \
     default: return launch<BN_, BK_, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,    \
-                                        a_kmajor, b_kmajor, bt, causal, int(seq), s);          \
+                                        a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);  \
   }
   if (BNsel == 128) {
     if (BKsel == 64) { MR_GEMM_LAUNCH(128, 64) }
@@ -636,6 +678,49 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
   if (BKsel == 64) { MR_GEMM_LAUNCH(256, 64) }
   MR_GEMM_LAUNCH(256, 32)
 #undef MR_GEMM_LAUNCH
+}
+
+}  // namespace
+
+extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda,
+                               int64_t stride_a, int a_kmajor, const uint16_t* b_hi,
+                               const uint16_t* b_lo, int64_t ldb, int64_t stride_b, int b_kmajor,
+                               float* c, int64_t ldc, int64_t stride_c, const float* bias,
+                               int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
+                               int precision, int causal, int64_t seq, void* stream) {
+  RemoteOut none;
+  memset(&none, 0, sizeof(none));
+  return gemm_impl(a_hi, a_lo, lda, stride_a, a_kmajor, b_hi, b_lo, ldb, stride_b, b_kmajor, c,
+                   ldc, stride_c, bias, accumulate, m, n, k, batch, precision, causal, seq, none,
+                   stream);
+}
+
+extern "C" int mr_gemm_rs(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
+                          const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
+                          int64_t m, int64_t n, int64_t k, int precision, float* const* dst,
+                          int64_t ldd, int64_t rows_per_rank, unsigned long long* const* flags,
+                          int world, unsigned int* done, unsigned long long epoch, void* stream) {
+  if (!dst || !flags || !done || world < 1 || world > kMaxRanks || rows_per_rank <= 0 ||
+      m != rows_per_rank * world || ldd < n || epoch == 0)
+    return MR_ERR_ARGUMENT;
+  RemoteOut remote;
+  memset(&remote, 0, sizeof(remote));
+  for (int r = 0; r < world; ++r) {
+    if (!dst[r] || !flags[r]) return MR_ERR_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(dst[r]) & 15u) return MR_ERR_ALIGNMENT;
+    remote.dst[r] = dst[r];
+    remote.flag[r] = flags[r];
+  }
+  if ((ldd % 4) != 0) return MR_ERR_ALIGNMENT;
+  remote.done = done;
+  remote.epoch = epoch;
+  remote.rows_per_rank = rows_per_rank;
+  remote.ldd = ldd;
+  remote.world = world;
+  remote.active = 1;
+  // c is unused (every row goes to its owner); dst[0] stands in for the checks
+  return gemm_impl(a_hi, a_lo, lda, 0, a_kmajor, b_hi, b_lo, ldb, 0, b_kmajor, dst[0], n, 0,
+                   nullptr, 0, m, n, k, 1, precision, 0, 0, remote, stream);
 }
 
 extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,

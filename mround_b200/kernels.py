@@ -316,12 +316,59 @@ def gemm(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, a_kmajor: bool, b
         GEMM_EVENTS.append((start, end, 2.0 * m * n * k, precision))
 
 
-def causal_fraction(causal: int, m: int, n: int, k: int, seq: int) -> float:
+def gemm_rs(a_hi, a_lo, b_hi, b_lo, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool,
+            lda: int, ldb: int, precision: int, dst_ptrs, ldd: int, rows_per_rank: int,
+            flag_ptrs, done, epoch: int) -> None:
+    """K3 whose rows go to their owner ranks over NVLink (fused reduce-scatter).
+
+    ``dst_ptrs[o]`` / ``flag_ptrs[o]``: device addresses (ints) of rank o's
+    slot and flag for this source rank; ``done``: this rank's zeroed int32
+    counter; ``epoch``: the exchange's step number (> 0, increasing).
+    """
+    import ctypes
+
+    world = len(dst_ptrs)
+    if len(flag_ptrs) != world:
+        raise SchemeError("one flag per destination rank")
+    timing = GEMM_EVENTS is not None
+    if timing:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+    dsts = (ctypes.c_void_p * world)(*dst_ptrs)
+    flags = (ctypes.c_void_p * world)(*flag_ptrs)
+    status = lib().mr_gemm_rs(
+        _ptr(a_hi, torch.bfloat16, "a_hi"), _ptr(a_lo, torch.bfloat16, "a_lo"), lda, int(a_kmajor),
+        _ptr(b_hi, torch.bfloat16, "b_hi"), _ptr(b_lo, torch.bfloat16, "b_lo"), ldb, int(b_kmajor),
+        m, n, k, precision, ctypes.cast(dsts, ctypes.c_void_p), ldd, rows_per_rank,
+        ctypes.cast(flags, ctypes.c_void_p), world, _ptr(done, torch.int32, "done", 1), int(epoch),
+        _stream())
+    check(status, "mr_gemm_rs")
+    _count()
+    if timing:
+        end.record()
+        GEMM_EVENTS.append((start, end, 2.0 * m * n * k, precision))
+
+
+def reduce_slots(slots, flags, epoch: int, out) -> None:
+    """Wait for every source's flag to reach ``epoch``, then out = sum of the
+    ``slots`` (world, ...) in rank order."""
+    world = slots.shape[0]
+    n = out.numel()
+    status = lib().mr_reduce_slots(
+        _ptr(slots, torch.float32, "slots"), slots[0].numel(), n, world,
+        _ptr(flags, torch.int64, "flags", world), int(epoch), _ptr(out, torch.float32, "out", n),
+        _stream())
+    check(status, "mr_reduce_slots")
+    _count()
+
+
+def causal_fraction(causal: int, m: int, n: int, k: int, seq: int, bk: int = 64) -> float:
     """Share of the dense tile work a causal mode of K3 actually computes
-    (mirrors the kernel's tile and K-tile predicates; BM = 128, BK = 64)."""
+    (mirrors the kernel's tile and K-tile predicates; BM = 128, K slices of
+    ``bk``: 64 when both operands are MN-major, else 32)."""
     if not causal:
         return 1.0
-    bm, bk = 128, 64
+    bm = 128
     bn = 128 if n <= 128 else 256
     m_tiles = -(-m // bm)
     k_tiles = -(-k // bk)
@@ -356,7 +403,7 @@ def gemm_batched(a_hi, a_lo, b_hi, b_lo, c, *, m: int, n: int, k: int, batch: in
     _count()
     if timing:
         end.record()
-        frac = causal_fraction(causal, m, n, k, seq)
+        frac = causal_fraction(causal, m, n, k, seq, 64 if not (a_kmajor or b_kmajor) else 32)
         GEMM_EVENTS.append((start, end, 2.0 * m * n * k * batch * frac, precision))
 
 

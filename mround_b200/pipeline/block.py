@@ -80,6 +80,7 @@ class FusedLinear:
         self.accumulate_grad = False
         self.grad_ready: list = []  # callbacks run right after this layer's weight gradient
         self.pending: list = []  # collectives that must finish before wq_hi/wq_lo are read
+        self.exchange = None  # peer slots of the fused GEMM -> reduce-scatter (LayerExchange)
 
     @property
     def out_features(self) -> int:
@@ -355,9 +356,17 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     def weight_grad(layer, dy, x_in, n_out, n_in):
         if layer.grad is None:
             return
-        kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, m=n_out, n=n_in, k=t,
-                     a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in,
-                     precision=prec.grad_weight, accumulate=layer.accumulate_grad)
+        ex = layer.exchange
+        if ex is not None and ex.active and not layer.accumulate_grad:
+            # rows go straight to their owner ranks over NVLink
+            kernels.gemm_rs(dy[0], dy[1], x_in[0], x_in[1], m=n_out, n=n_in, k=t, a_kmajor=False,
+                            b_kmajor=False, lda=n_out, ldb=n_in, precision=prec.grad_weight,
+                            dst_ptrs=ex.dst_ptrs, ldd=n_in, rows_per_rank=ex.rows_per_rank,
+                            flag_ptrs=ex.flag_ptrs, done=ex.done, epoch=ex.epoch)
+        else:
+            kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, m=n_out, n=n_in, k=t,
+                         a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in,
+                         precision=prec.grad_weight, accumulate=layer.accumulate_grad)
         for hook in layer.grad_ready:
             hook(layer)
 

@@ -303,6 +303,7 @@ class QuantizationRunner:
         with meter.stage("commit"):
             layers = tuner.commit(self.keep_codes)
         torch.cuda.synchronize(self.device)
+        tuner.close()
         exported = {f"{name}.{p}": q for p, q in layers.items()}
         result = BlockResult(
             index=block.index, name=name, initial_loss=outcome["initial"],

@@ -224,7 +224,12 @@ class BlockTuner:
 
     def __init__(self, block: DeviceBlock, schemes: dict[str, QuantScheme], lrs: dict[str, float],
                  *, suppress: bool, eps: float, precision: Precision, dist: DistContext,
-                 pieces: int = 1) -> None:
+                 pieces: int = 1, exchange: str = "p2p") -> None:
+        """``exchange``: how the row-sharded update gathers each rank's rows of
+        the gradient -- "p2p" (the weight-gradient GEMM stores them into their
+        owners' slots over NVLink) or "nccl" (a reduce-scatter after the GEMM)."""
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', got {exchange!r}")
         self.block = block
         self.suppress = suppress
         self.precision = precision
@@ -269,6 +274,18 @@ class BlockTuner:
                 # untuned rows of a partly tuned fused weight keep their exact operand
                 self._shards[id(t.layer)] = (s0, s1, grad, t.layer.wq_hi[s0:s1].clone(),
                                              t.layer.wq_lo[s0:s1].clone())
+        # Fused GEMM -> reduce-scatter over NVLink peer memory (one piece per
+        # step; at most 8 ranks; every rank agrees before it is used).
+        self.peer = None
+        self._epoch = 0
+        if (self.sharded and exchange == "p2p" and pieces == 1 and dist.world <= 8
+                and all(t.layer.in_features % 4 == 0 for t in self.tunables)):
+            from mround_b200.pipeline.peer import PeerExchange
+
+            self.peer = PeerExchange(dist, [tuple(t.layer.w.shape) for t in self.tunables],
+                                     block.device)
+            for t, ex in zip(self.tunables, self.peer.layers):
+                t.layer.exchange = ex
 
     # ------------------------------------------------------------ search
     def search(self, inputs: list[torch.Tensor]) -> float:
@@ -318,6 +335,8 @@ class BlockTuner:
     def _reduce_hook(self, layer: FusedLinear) -> None:
         if not self._last_piece:
             return
+        if layer.exchange is not None and layer.exchange.active:
+            return  # the GEMM has already stored the rows with their owners
         if self._sharded_step:
             _, _, grad, _, _ = self._shards[id(layer)]
             self._pending[id(layer)] = self.dist.reduce_scatter_async(grad, layer.grad)
@@ -334,8 +353,15 @@ class BlockTuner:
         # rows of this rank, then the operands' all-gather; qkv first, so the
         # next forward's first GEMM waits on the smallest gather only
         for t in self.tunables:
-            self._wait(t.layer)
             s0, s1, grad, hi, lo = self._shards[id(t.layer)]
+            ex = t.layer.exchange
+            if ex is not None and ex.active:
+                # every source's rows are in this rank's slots once its flag
+                # carries this step's epoch; sum them in rank order
+                kernels.reduce_slots(ex.slots, ex.flags, ex.epoch, grad)
+                ex.active = False
+            else:
+                self._wait(t.layer)
             t.update_rows(step, iters, s0, s1, grad, hi, lo)
             t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_hi, hi))
             t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_lo, lo))
@@ -405,6 +431,11 @@ class BlockTuner:
     def step(self, x: torch.Tensor, target: torch.Tensor, step: int, iters: int) -> torch.Tensor:
         """One signed-gradient step on one batch; returns this rank's loss share."""
         self._sharded_step = self.sharded
+        if self.peer is not None:
+            self._epoch += 1
+            for t in self.tunables:
+                t.layer.exchange.epoch = self._epoch
+                t.layer.exchange.active = True
         bounds = piece_bounds(x.shape[0], self.pieces)
         if len(bounds) == 1:
             self._last_piece = True
@@ -457,6 +488,22 @@ class BlockTuner:
         for t in self.tunables:
             t.reset()
         self._dirty = False
+
+    def close(self) -> None:
+        """Release the peer mappings of the fused exchange and report a bounded
+        wait that gave up (``DeviceError``)."""
+        if self.peer is None:
+            return
+        from mround_b200._native import lib
+        from mround_b200.exceptions import DeviceError
+
+        status = int(lib().mr_peer_status(1))
+        for t in self.tunables:
+            t.layer.exchange = None
+        self.peer.close()
+        self.peer = None
+        if status:
+            raise DeviceError(f"the peer gradient exchange gave up waiting (status {status})")
 
     def snapshot(self) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         self.sync_params()

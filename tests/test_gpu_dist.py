@@ -1,9 +1,10 @@
 """Data-parallel step on 2 GPUs (NCCL) against one process on the whole batch.
 
 Each rank holds half the sequences of the batch; the threshold comes from
-all-reduced histograms, the weight gradients are reduce-scattered by rows,
-each rank steps its rows and the operands are all-gathered for the next step
-(two steps run).  Against a single-process step on the whole
+all-reduced histograms, the weight gradients are reduce-scattered by rows --
+by the weight-gradient GEMM itself storing rows into their owners' slots over
+NVLink (or, for comparison, an NCCL reduce-scatter) -- each rank steps its rows
+and the operands are all-gathered for the next step (two steps run).  Against a single-process step on the whole
 batch: the loss agrees to float64 summation order and the exact outlier
 threshold is identical; V after the steps agrees except where a gradient's
 sign flips between two summation orders (bounded here at 0.1 % of entries);
@@ -46,7 +47,7 @@ def _setup(device):
     return arch, DeviceBlock(arch, params, device), x, tgt
 
 
-def _tuner(block, dist):
+def _tuner(block, dist, exchange="p2p"):
     from mround_b200.pipeline.block import Precision
     from mround_b200.pipeline.tuning import BlockTuner
     from mround_b200.schemes import QuantScheme
@@ -54,10 +55,11 @@ def _tuner(block, dist):
 
     scheme = QuantScheme(bits=2, group_size=32, symmetry="asym")
     return BlockTuner(block, {p: scheme for p in LINEARS}, {p: 0.05 for p in LINEARS},
-                      suppress=True, eps=1e-8, precision=Precision(), dist=dist)
+                      suppress=True, eps=1e-8, precision=Precision(), dist=dist,
+                      exchange=exchange)
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, exchange="p2p"):
     import torch.distributed as tdist
 
     from mround_b200.pipeline.dist import DistContext
@@ -73,8 +75,9 @@ def _rank(rank, world, port, q):
         dev = torch.device("cuda", rank)
         _, block, x, tgt = _setup(dev)
         rows = ctx.shard(SHAPE[0])
-        tuner = _tuner(block, ctx)
+        tuner = _tuner(block, ctx, exchange)
         assert tuner.sharded, "tiny-qwen2's fused rows divide by 2: the row-sharded update runs"
+        assert (tuner.peer is not None) == (exchange == "p2p")
         loss = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 0, 10)
         # a second step runs on the all-gathered operands of the first
         loss2 = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 1, 10)
@@ -85,9 +88,38 @@ def _rank(rank, world, port, q):
         q.put((rank, total.tolist(), float(tuner.ws.thr.item()),
                [t.v.cpu().numpy() for t in tuner.tunables],
                [t.alpha.cpu().numpy() for t in tuner.tunables]))
+        tuner.close()
         tdist.barrier()
     finally:
         tdist.destroy_process_group()
+
+
+def _run_ranks(exchange):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, exchange)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+def test_two_gpu_fused_exchange_equals_nccl_reduce_scatter():
+    """The weight-gradient GEMM storing rows into their owners' slots over NVLink
+    gives the same parameters, bit for bit, as the GEMM plus an NCCL
+    reduce-scatter (two summands: the order cannot differ)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    fused = _run_ranks("p2p")
+    nccl = _run_ranks("nccl")
+    for a, b in zip(fused, nccl):
+        assert a[1] == b[1] and a[2] == b[2]
+        for x, y in zip(a[3] + a[4], b[3] + b[4]):
+            assert np.array_equal(x, y)
 
 
 def test_two_gpu_step_matches_single_process():
@@ -95,16 +127,7 @@ def test_two_gpu_step_matches_single_process():
         pytest.skip("needs two GPUs")
     from mround_b200.pipeline.dist import DistContext
 
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    res = _run_ranks("p2p")
     # single process, whole batch, on GPU 0
     dev = torch.device("cuda", 0)
     _, block, x, tgt = _setup(dev)
