@@ -199,7 +199,10 @@ struct Cfg {
   static constexpr int kBParts = PREC == 3 ? 2 : 1;
   static constexpr int kStage = kA * kAParts + kB * kBParts;
   static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
-  static constexpr int kSmem = kStages * kStage + 1024 /* align */ + 256 /* barriers */;
+  // per epilogue warp, a 32 x 32 float32 block (padded rows) through which the
+  // fused reduce-scatter turns row-per-lane values into row-contiguous stores
+  static constexpr int kStaging = 4 * 32 * 33 * 4;
+  static constexpr int kSmem = kStages * kStage + 1024 /* align */ + 256 /* barriers */ + kStaging;
   static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
 };
 
@@ -442,6 +445,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------ epilogue (warps 2-5)
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    float* stage = reinterpret_cast<float*>(smem + C::kStages * C::kStage + 256) + quarter * 32 * 33;
     bool ok = true;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
@@ -464,14 +468,37 @@ __global__ void __launch_bounds__(192, 1)
             for (int q = 0; q < 32; ++q) v[q] = 0.f;
           }
           const int gc = tl.n0 + col;
-          if (row < m && gc < n) {
-            float* dst;
-            if (remote.active) {
-              const int owner = int(row / remote.rows_per_rank);
-              dst = remote.dst[owner] + (row - owner * remote.rows_per_rank) * remote.ldd + gc;
-            } else {
-              dst = cz + int64_t(row) * ldc + gc;
+          if (remote.active) {
+            // Peer stores: lane i holds row i's 32 columns; through the staging
+            // block, each store instruction writes 4 rows x 128 contiguous bytes
+            // (8 lanes per row) instead of 32 scattered 16-byte pieces, so
+            // NVLink carries full-line writes.
+#pragma unroll
+            for (int q = 0; q < 32; ++q) stage[lane * 33 + q] = v[q];
+            __syncwarp();
+            const int sub = lane >> 3, c4 = (lane & 7) * 4;
+#pragma unroll 2
+            for (int p = 0; p < 8; ++p) {
+              const int r = p * 4 + sub;
+              const int grow = tl.m0 + quarter * 32 + r;
+              const int gcol = gc + c4;
+              if (grow < m && gcol < n) {
+                const int owner = int(grow / remote.rows_per_rank);
+                float* dst = remote.dst[owner] +
+                             (grow - owner * remote.rows_per_rank) * remote.ldd + gcol;
+                const float* src = stage + r * 33 + c4;
+                if (gcol + 4 <= n) {
+                  *reinterpret_cast<float4*>(dst) = make_float4(src[0], src[1], src[2], src[3]);
+                } else {
+                  for (int i = 0; gcol + i < n; ++i) dst[i] = src[i];
+                }
+              }
             }
+            __syncwarp();
+            continue;
+          }
+          if (row < m && gc < n) {
+            float* dst = cz + int64_t(row) * ldc + gc;
             const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
             if (full_chunk) {
 #pragma unroll

@@ -224,17 +224,12 @@ class BlockTuner:
 
     def __init__(self, block: DeviceBlock, schemes: dict[str, QuantScheme], lrs: dict[str, float],
                  *, suppress: bool, eps: float, precision: Precision, dist: DistContext,
-                 pieces: int = 1, exchange: str = "auto") -> None:
+                 pieces: int = 1, exchange: str = "p2p") -> None:
         """``exchange``: how the row-sharded update gathers each rank's rows of
         the gradient -- "p2p" (the weight-gradient GEMM stores them into their
-        owners' slots over NVLink), "nccl" (a reduce-scatter after the GEMM), or
-        "auto" (p2p on two ranks, nccl on more: measured on one 8-GPU box, the
-        epilogue's peer stores match NCCL at 2 ranks and fall behind NCCL's
-        contiguous transfers at 4 and 8)."""
-        if exchange not in ("p2p", "nccl", "auto"):
-            raise ValueError(f"exchange must be 'p2p', 'nccl' or 'auto', got {exchange!r}")
-        if exchange == "auto":
-            exchange = "p2p" if dist.world == 2 else "nccl"
+        owners' slots over NVLink) or "nccl" (a reduce-scatter after the GEMM)."""
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', got {exchange!r}")
         self.block = block
         self.suppress = suppress
         self.precision = precision
