@@ -409,6 +409,140 @@ __global__ void __launch_bounds__(kSoftThreads) softmax_bwd_kernel(
   }
 }
 
+// Rows up to 2048 columns: one warp per row, NV float4 per lane (columns
+// 128 i + 4 lane .. +3); the reductions stay inside the warp (the block kernels
+// above take longer rows).  Lanes past the causal position do not load.
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Four rows per block: the row stays in registers (86 per thread at 2048
+// columns, 164 in the backward), and small blocks let more of them share an
+// SM (measured at 8 x 28 x 2048 rows: 256-thread blocks 1.16 ms, 128-thread
+// 0.98 ms for the forward).
+constexpr int kSoftWarpThreads = 128;
+
+template <int NV>
+__global__ void __launch_bounds__(kSoftWarpThreads) softmax_causal_warp_kernel(
+    const float* __restrict__ scores, int64_t rows, int S, float scale, int band,
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * (kSoftWarpThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int pos = int(row % S);
+  const float* r = scores + row * S;
+  float v[NV][4];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c <= pos) {
+      const float4 q = __ldcs(reinterpret_cast<const float4*>(r + c));
+      v[i][0] = __fmul_rn(q.x, scale);
+      v[i][1] = c + 1 <= pos ? __fmul_rn(q.y, scale) : -INFINITY;
+      v[i][2] = c + 2 <= pos ? __fmul_rn(q.z, scale) : -INFINITY;
+      v[i][3] = c + 3 <= pos ? __fmul_rn(q.w, scale) : -INFINITY;
+    } else {
+      v[i][0] = v[i][1] = v[i][2] = v[i][3] = -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) m = fmaxf(m, v[i][j]);
+  }
+  m = warp_max(m);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[i][j] = v[i][j] == -INFINITY ? 0.f : expf(v[i][j] - m);
+      sum += v[i][j];
+    }
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+  const int lim = write_limit(pos, S, band);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < lim)
+      put_split4(hi, lo, row * S + c,
+                 make_float4(v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv));
+  }
+}
+
+
+template <int NV>
+__global__ void __launch_bounds__(kSoftWarpThreads) softmax_bwd_warp_kernel(
+    const float* __restrict__ dp, const uint16_t* __restrict__ p_hi,
+    const uint16_t* __restrict__ p_lo, int64_t rows, int S, float scale, int band,
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * (kSoftWarpThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int pos = int(row % S);
+  const float* dr = dp + row * S;
+  float dv[NV][4];
+  uint2 ph[NV], pl[NV];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c <= pos) {
+      const float4 d = __ldcs(reinterpret_cast<const float4*>(dr + c));
+      ph[i] = __ldcs(reinterpret_cast<const uint2*>(p_hi + row * S + c));
+      pl[i] = __ldcs(reinterpret_cast<const uint2*>(p_lo + row * S + c));
+      dv[i][0] = d.x; dv[i][1] = d.y; dv[i][2] = d.z; dv[i][3] = d.w;
+    } else {
+      ph[i] = pl[i] = make_uint2(0u, 0u);
+      dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    float a[4], b[4];
+    unpack4(ph[i], a);
+    unpack4(pl[i], b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a[j] = c + j <= pos ? __fadd_rn(a[j], b[j]) : 0.f;
+      dot += a[j] * dv[i][j];
+    }
+  }
+  dot = warp_sum(dot);
+  const int lim = write_limit(pos, S, band);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < lim) {
+      float a[4], b[4], o[4];
+      unpack4(ph[i], a);
+      unpack4(pl[i], b);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = c + j <= pos ? __fadd_rn(a[j], b[j]) : 0.f;
+        o[j] = scale * p * (dv[i][j] - dot);
+      }
+      put_split4(hi, lo, row * S + c, make_float4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
+// float4 per lane for the warp-per-row kernels (0: the row needs the block kernels)
+int soft_vec(int s) {
+  for (int nv = 1; nv <= 16; nv *= 2)
+    if (s <= nv * 128) return nv;
+  return 0;
+}
+
 int grid_elems(int64_t n, int threads = 256) { return grid_for(n, threads, 8); }
 
 }  // namespace
@@ -497,8 +631,19 @@ extern "C" int mr_softmax_causal_split(const float* scores, int64_t rows, int s,
   if (!aligned16(scores) || (reinterpret_cast<uintptr_t>(hi) & 7u) ||
       (reinterpret_cast<uintptr_t>(lo) & 7u))
     return MR_ERR_ALIGNMENT;
-  softmax_causal_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      scores, s, scale, band, hi, lo);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned warp_grid = unsigned((rows + kSoftWarpThreads / 32 - 1) / (kSoftWarpThreads / 32));
+  switch (soft_vec(s)) {
+#define MR_SOFT(NV)                                                                  \
+    case NV:                                                                         \
+      softmax_causal_warp_kernel<NV><<<warp_grid, kSoftWarpThreads, 0, st>>>(scores, rows, s, scale, \
+                                                                          band, hi, lo);         \
+      break;
+    MR_SOFT(1) MR_SOFT(2) MR_SOFT(4) MR_SOFT(8) MR_SOFT(16)
+#undef MR_SOFT
+    default:
+      softmax_causal_kernel<<<unsigned(rows), kSoftThreads, 0, st>>>(scores, s, scale, band, hi, lo);
+  }
   return launch_status();
 }
 
@@ -511,7 +656,19 @@ extern "C" int mr_softmax_bwd_split(const float* dp, const uint16_t* p_hi, const
   if (!aligned16(dp) || ((reinterpret_cast<uintptr_t>(p_hi) | reinterpret_cast<uintptr_t>(p_lo) |
                           reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 7u))
     return MR_ERR_ALIGNMENT;
-  softmax_bwd_kernel<<<unsigned(rows), kSoftThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      dp, p_hi, p_lo, s, scale, band, hi, lo);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned warp_grid = unsigned((rows + kSoftWarpThreads / 32 - 1) / (kSoftWarpThreads / 32));
+  switch (soft_vec(s)) {
+#define MR_SOFT(NV)                                                                        \
+    case NV:                                                                               \
+      softmax_bwd_warp_kernel<NV><<<warp_grid, kSoftWarpThreads, 0, st>>>(dp, p_hi, p_lo, rows, s,  \
+                                                                       scale, band, hi, lo);    \
+      break;
+    MR_SOFT(1) MR_SOFT(2) MR_SOFT(4) MR_SOFT(8) MR_SOFT(16)
+#undef MR_SOFT
+    default:
+      softmax_bwd_kernel<<<unsigned(rows), kSoftThreads, 0, st>>>(dp, p_hi, p_lo, s, scale, band,
+                                                                  hi, lo);
+  }
   return launch_status();
 }

@@ -1,4 +1,4 @@
-"""Kernel sweep: HBM throughput of K1, K2, K5, K6.
+"""Kernel sweep: HBM throughput of K1, K2, K5, K6 (and K7).
 
 Shapes 896x896, 4864x896, 3584x3584, 18944x3584 (bf16 weights N(0, 0.02)
 with 0.1 % outliers x20; V ~ U(-0.5, 0.5); alpha, beta ~ U(0.5, 1.0); upstream
@@ -17,7 +17,13 @@ read once (2 B) but evaluated against ~200 candidates at ~8 float32 operations
 each; it is reported as candidate-element evaluations per second beside its
 bandwidth.
 
-Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick]
+``--attention`` times K7's causal softmax and its backward instead, at the 7B
+step's attention shape (8 x 28 heads x 2048 x 2048, band-limited writes):
+forward reads the scores up to each row's position (4 B) and writes P hi+lo
+(4 B) up to the band limit; backward reads dP (4 B) and P hi+lo (4 B) up to the
+position and writes dS hi+lo (4 B) up to the band limit.
+
+Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick | --attention]
 Prints one JSON line per case, then a summary line.
 """
 
@@ -138,12 +144,49 @@ def run(reps: int = 5, quick: bool = False) -> list[dict]:
     return results
 
 
+def attention(reps: int = 5, batch: int = 8, heads: int = 28, seq: int = 2048) -> list[dict]:
+    device = torch.device("cuda")
+    peak, src = _peak()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    rows = batch * heads * seq
+    g = torch.Generator(device=device).manual_seed(seq)
+    scores = torch.randn(rows, seq, device=device, generator=g) * 3.0
+    dp = torch.randn(rows, seq, device=device, generator=g)
+    live = sum((p // 4 + 1) * 4 for p in range(seq)) * (rows // seq)
+    band = sum(min(seq, (p // 128 + 2) * 128) for p in range(seq)) * (rows // seq)
+    scale = 1.0 / 128 ** 0.5
+    state = {}
+
+    def fwd():
+        state["p"] = kernels.softmax_causal_split(scores, rows, seq, scale, True)
+
+    def bwd():
+        kernels.softmax_bwd_split(dp, state["p"], rows, seq, scale, True)
+
+    results = []
+    for name, fn, nbytes in (("K7_softmax_causal", fwd, 4 * live + 4 * band),
+                             ("K7_softmax_bwd", bwd, 8 * live + 4 * band)):
+        fn()
+        torch.cuda.synchronize()
+        ms = _time(fn, flush, reps)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        rec = {"kernel": name, "rows": rows, "cols": seq, "ms": ms, "bytes": nbytes, "gbs": gbs,
+               "frac": gbs / peak, "peak_gbs": peak, "peak_source": src}
+        results.append(rec)
+        print(json.dumps(rec), flush=True)
+    return results
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--quick", action="store_true")
+    ap.add_argument("--attention", action="store_true")
     args = ap.parse_args()
-    run(args.reps, args.quick)
+    if args.attention:
+        attention(args.reps)
+    else:
+        run(args.reps, args.quick)
 
 
 if __name__ == "__main__":
