@@ -27,6 +27,7 @@ constexpr int kMaxWidths = 8;
 struct Widths {
   int n;
   float maxq[kMaxWidths];          // 2^b - 1 (asymmetric) or 2^(b-1) (symmetric)
+  float rmaxq[kMaxWidths];         // RN(1 / maxq), formed on the host
   const float* grid[kMaxWidths];   // searched scale per group, or NULL
 };
 
@@ -41,12 +42,14 @@ __device__ __forceinline__ float clamp_mag(float s, float eps) {
 // the same results as the scalar operations, half the instructions).
 __device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
 
-// a / b correctly rounded for a pair, from y = RN(1/b) (div_rcp, two lanes)
+// a / b correctly rounded for a pair, from y = RN(1/b) (div_rcp, two lanes).
+// For a = 0 the result is a zero whose sign may differ from IEEE division's
+// (div_rcp keeps it); here only |g * (q - w)| is used, where the sign of a
+// zero quotient cannot show.
 __device__ __forceinline__ float2 div_rcp2(float2 a, float2 b, float2 y) {
   const float2 q = __fmul2_rn(a, y);
   const float2 r = __ffma2_rn(neg2(q), b, a);
-  const float2 d = __ffma2_rn(r, y, q);
-  return make_float2(a.x == 0.f ? q.x : d.x, a.y == 0.f ? q.y : d.y);
+  return __ffma2_rn(r, y, q);
 }
 
 template <int LPG, int SYM>
@@ -93,6 +96,7 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
     for (int j = 0; j < kMaxWidths; ++j) {
       if (j >= widths.n) break;
       const float maxq = widths.maxq[j];
+      const float rmaxq = widths.rmaxq[j];
       float part = 0.f;
       if constexpr (SYM) {
         float scale;
@@ -102,7 +106,7 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
           const float neg = -w_min;
           const bool pos = w_max >= neg;
           const float dom = pos ? w_max : neg;
-          scale = clamp_mag(div_rcp(pos ? -dom : dom, maxq, __frcp_rn(maxq)), eps);
+          scale = clamp_mag(div_rcp(pos ? -dom : dom, maxq, rmaxq), eps);
         }
         const float rcp = __frcp_rn(scale);
         const float hi = __fsub_rn(maxq, 1.f);
@@ -119,18 +123,21 @@ __global__ void __launch_bounds__(kThreads) deltaloss_kernel(const float* __rest
           part = __fadd_rn(part, fabsf(t.y));
         }
       } else {
-        const float scale = fmaxf(div_rcp(__fsub_rn(w_max, w_min), maxq, __frcp_rn(maxq)), eps);
+        const float scale = fmaxf(div_rcp(__fsub_rn(w_max, w_min), maxq, rmaxq), eps);
         const float rcp = __frcp_rn(scale);
         const float zp = rintf(div_rcp(-w_min, scale, rcp));
+        // clamp(rint(w / s) + zp, 0, maxq) - zp == clamp(rint(w / s), -zp, maxq - zp):
+        // every operand is an integer-valued float of magnitude <= maxq (|w| is at
+        // most the group's range, s at least range / maxq), so both sides are exact.
+        const float lo_c = -zp, hi_c = __fsub_rn(maxq, zp);
         const float2 s2 = make_float2(scale, scale), y2 = make_float2(rcp, rcp);
-        const float2 z2 = make_float2(zp, zp);
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
           const float2 wv = make_float2(wf[i], wf[i + 1]);
           const float2 d = div_rcp2(wv, s2, y2);
-          const float2 x = __fadd2_rn(make_float2(rintf(d.x), rintf(d.y)), z2);
-          const float2 c = make_float2(fminf(fmaxf(x.x, 0.f), maxq), fminf(fmaxf(x.y, 0.f), maxq));
-          const float2 q = __fmul2_rn(s2, __fadd2_rn(c, neg2(z2)));
+          const float2 c = make_float2(fminf(fmaxf(rintf(d.x), lo_c), hi_c),
+                                       fminf(fmaxf(rintf(d.y), lo_c), hi_c));
+          const float2 q = __fmul2_rn(s2, c);
           const float2 t = __fmul2_rn(make_float2(gf[i], gf[i + 1]), __fadd2_rn(q, neg2(wv)));
           part = __fadd_rn(part, fabsf(t.x));
           part = __fadd_rn(part, fabsf(t.y));
@@ -174,6 +181,7 @@ extern "C" int mr_deltaloss(const float* g, const uint16_t* w_bf16, int64_t rows
   for (int j = 0; j < n_bits; ++j) {
     if (bits[j] < 2 || bits[j] > 8) return MR_ERR_ARGUMENT;
     widths.maxq[j] = symmetric ? float(1 << (bits[j] - 1)) : float((1 << bits[j]) - 1);
+    widths.rmaxq[j] = 1.0f / widths.maxq[j];  // host float division: correctly rounded
     widths.grid[j] = grids ? grids[j] : nullptr;
     if (grids && !grids[j]) return MR_ERR_ARGUMENT;
   }
