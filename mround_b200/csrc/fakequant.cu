@@ -419,24 +419,34 @@ __global__ void __launch_bounds__(kThreads) pack_mlx_kernel(
       continue;
     }
     // Word j of this tile takes its bits from lane j*32/chunk_bits and the
-    // next one; a tile holds 8*bits words, so each lane forms up to two.
+    // next one; a tile holds 8*bits words (24 for 3 bits: one pass, 32-bit
+    // chunks; 40-56 for 5-7 bits: two passes over 64-bit chunks).
+    constexpr int kWords = 8 * BITS;
 #pragma unroll
-    for (int j = lane; j < 64; j += 32) {
+    for (int j0 = 0; j0 < kWords; j0 += 32) {
+      const int j = j0 + lane;
       const int bitpos = j * 32;
       const int src = bitpos / chunk_bits;
       const int off = bitpos - src * chunk_bits;
+      const int up = chunk_bits - off;
       const uint32_t lo0 = __shfl_sync(0xffffffffu, uint32_t(chunk), src & 31);
-      const uint32_t hi0 = __shfl_sync(0xffffffffu, uint32_t(uint64_t(chunk) >> 32), src & 31);
       const uint32_t lo1 = __shfl_sync(0xffffffffu, uint32_t(chunk), (src + 1) & 31);
-      const uint32_t hi1 = __shfl_sync(0xffffffffu, uint32_t(uint64_t(chunk) >> 32), (src + 1) & 31);
-      if (j < chunk_bits) {
+      uint32_t word;
+      if constexpr (8 * BITS <= 32) {
+        const uint32_t c1 = src + 1 < 32 ? lo1 : 0u;
+        word = (lo0 >> off) | (up < 32 ? c1 << up : 0u);
+      } else {
+        const uint32_t hi0 = __shfl_sync(0xffffffffu, uint32_t(uint64_t(chunk) >> 32), src & 31);
+        const uint32_t hi1 = __shfl_sync(0xffffffffu, uint32_t(uint64_t(chunk) >> 32), (src + 1) & 31);
         const uint64_t c0 = (uint64_t(hi0) << 32) | lo0;
         const uint64_t c1 = (src + 1 < 32) ? ((uint64_t(hi1) << 32) | lo1) : 0ull;
-        uint64_t word = c0 >> off;
-        const int up = chunk_bits - off;
-        if (up < 64) word |= c1 << up;
+        uint64_t w64 = c0 >> off;
+        if (up < 64) w64 |= c1 << up;
+        word = uint32_t(w64);
+      }
+      if (j < kWords) {
         const int64_t wi = t * (kTile * bits / 32) + j;
-        if (wi < total_words) packed[wi] = uint32_t(word);
+        if (wi < total_words) packed[wi] = word;
       }
     }
   }
