@@ -247,6 +247,125 @@ __global__ void heads_kernel(const float* __restrict__ src, int B, int S, int H,
   }
 }
 
+// Token-row forms of the three kernels above for head dims divisible by 8:
+// one block walks one token's row (all heads), each thread 4 columns of a
+// head's first half and the matching 4 of its second half, with 16-byte loads
+// and 8-byte hi/lo stores; the index arithmetic is 32-bit inside the row
+// (the per-element 64-bit divisions of the forms above made them issue-bound).
+__device__ __forceinline__ float4 ldv4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+__device__ __forceinline__ float4 rot_fwd1(float4 x1, float4 x2, float4 c, float4 sn) {
+  return make_float4(__fsub_rn(__fmul_rn(x1.x, c.x), __fmul_rn(x2.x, sn.x)),
+                     __fsub_rn(__fmul_rn(x1.y, c.y), __fmul_rn(x2.y, sn.y)),
+                     __fsub_rn(__fmul_rn(x1.z, c.z), __fmul_rn(x2.z, sn.z)),
+                     __fsub_rn(__fmul_rn(x1.w, c.w), __fmul_rn(x2.w, sn.w)));
+}
+
+__device__ __forceinline__ float4 rot_fwd2(float4 x1, float4 x2, float4 c, float4 sn) {
+  return make_float4(__fadd_rn(__fmul_rn(x1.x, sn.x), __fmul_rn(x2.x, c.x)),
+                     __fadd_rn(__fmul_rn(x1.y, sn.y), __fmul_rn(x2.y, c.y)),
+                     __fadd_rn(__fmul_rn(x1.z, sn.z), __fmul_rn(x2.z, c.z)),
+                     __fadd_rn(__fmul_rn(x1.w, sn.w), __fmul_rn(x2.w, c.w)));
+}
+
+__global__ void __launch_bounds__(256) rope_row_kernel(
+    const float* __restrict__ qkv, const float* __restrict__ cosv, const float* __restrict__ sinv,
+    int B, int S, int Hq, int Hkv, int D, uint16_t* __restrict__ q_hi, uint16_t* __restrict__ q_lo,
+    uint16_t* __restrict__ k_hi, uint16_t* __restrict__ k_lo, uint16_t* __restrict__ v_hi,
+    uint16_t* __restrict__ v_lo) {
+  const int half = D / 2, per_head = half / 4;
+  const int H = Hq + 2 * Hkv;
+  const int units = H * per_head;
+  const int64_t T = int64_t(B) * S;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const int s = int(t % S), b = int(t / S);
+    const float* row = qkv + t * int64_t(H) * D;
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const int head = u / per_head;
+      const int j = (u - head * per_head) * 4;
+      const float4 x1 = ldv4(row + head * D + j), x2 = ldv4(row + head * D + half + j);
+      float4 o1 = x1, o2 = x2;
+      if (head < Hq + Hkv) {
+        const float4 c = ldv4(cosv + int64_t(s) * half + j), sn = ldv4(sinv + int64_t(s) * half + j);
+        o1 = rot_fwd1(x1, x2, c, sn);
+        o2 = rot_fwd2(x1, x2, c, sn);
+      }
+      uint16_t *dh, *dl;
+      int64_t base;
+      if (head < Hq) {
+        dh = q_hi; dl = q_lo;
+        base = ((int64_t(b) * Hq + head) * S + s) * D;
+      } else if (head < Hq + Hkv) {
+        dh = k_hi; dl = k_lo;
+        base = ((int64_t(b) * Hkv + (head - Hq)) * S + s) * D;
+      } else {
+        dh = v_hi; dl = v_lo;
+        base = ((int64_t(b) * Hkv + (head - Hq - Hkv)) * S + s) * D;
+      }
+      put_split4(dh, dl, base + j, o1);
+      put_split4(dh, dl, base + half + j, o2);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) rope_bwd_row_kernel(
+    const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv,
+    const float* __restrict__ cosv, const float* __restrict__ sinv, int B, int S, int Hq, int Hkv,
+    int D, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  const int half = D / 2, per_head = half / 4;
+  const int H = Hq + 2 * Hkv;
+  const int units = H * per_head;
+  const int64_t T = int64_t(B) * S;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const int s = int(t % S), b = int(t / S);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const int head = u / per_head;
+      const int j = (u - head * per_head) * 4;
+      const float* src;
+      if (head < Hq) src = dq + ((int64_t(b) * Hq + head) * S + s) * D;
+      else if (head < Hq + Hkv) src = dk + ((int64_t(b) * Hkv + (head - Hq)) * S + s) * D;
+      else src = dv + ((int64_t(b) * Hkv + (head - Hq - Hkv)) * S + s) * D;
+      const float4 d1 = ldv4(src + j), d2 = ldv4(src + half + j);
+      float4 g1 = d1, g2 = d2;
+      if (head < Hq + Hkv) {
+        const float4 c = ldv4(cosv + int64_t(s) * half + j), sn = ldv4(sinv + int64_t(s) * half + j);
+        g1 = make_float4(d1.x * c.x + d2.x * sn.x, d1.y * c.y + d2.y * sn.y,
+                         d1.z * c.z + d2.z * sn.z, d1.w * c.w + d2.w * sn.w);
+        g2 = make_float4(d2.x * c.x - d1.x * sn.x, d2.y * c.y - d1.y * sn.y,
+                         d2.z * c.z - d1.z * sn.z, d2.w * c.w - d1.w * sn.w);
+      }
+      const int64_t o = t * int64_t(H) * D + int64_t(head) * D;
+      put_split4(hi, lo, o + j, g1);
+      put_split4(hi, lo, o + half + j, g2);
+    }
+  }
+}
+
+// heads (B,H,S,D) <-> token rows (T, H*D), one token's row per block iteration
+__global__ void __launch_bounds__(256) heads_row_kernel(const float* __restrict__ src, int B, int S,
+                                                        int H, int D, int merge,
+                                                        uint16_t* __restrict__ hi,
+                                                        uint16_t* __restrict__ lo) {
+  const int per_head = D / 4;
+  const int units = H * per_head;
+  const int64_t T = int64_t(B) * S;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const int s = int(t % S), b = int(t / S);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const int h = u / per_head;
+      const int d = (u - h * per_head) * 4;
+      const int64_t row_idx = t * int64_t(H) * D + int64_t(u) * 4;
+      const int64_t head_idx = ((int64_t(b) * H + h) * S + s) * D + d;
+      if (merge)
+        put_split4(hi, lo, row_idx, ldv4(src + head_idx));
+      else
+        put_split4(hi, lo, head_idx, ldv4(src + row_idx));
+    }
+  }
+}
+
 __device__ __forceinline__ float silu_of(float g) { return g / (1.f + expf(-g)); }
 
 // act = silu(g) * u, gu = [g | u] per row -> hi/lo (T, I).
@@ -545,6 +664,11 @@ int soft_vec(int s) {
 
 int grid_elems(int64_t n, int threads = 256) { return grid_for(n, threads, 8); }
 
+// one block per token row, at most 2^31 - 1 blocks (the kernels stride beyond)
+unsigned row_grid(int64_t tokens) { return unsigned(tokens < 0x7fffffff ? tokens : 0x7fffffff); }
+
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
 }  // namespace
 }  // namespace mr
 
@@ -580,9 +704,18 @@ extern "C" int mr_rope_split(const float* qkv, const float* cosv, const float* s
                              void* stream) {
   if (!qkv || !cosv || !sinv || b <= 0 || s <= 0 || hq <= 0 || hkv <= 0 || d <= 0 || d % 2)
     return MR_ERR_ARGUMENT;
-  const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
-  rope_split_kernel<<<grid_elems(total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      qkv, cosv, sinv, b, s, hq, hkv, d, q_hi, q_lo, k_hi, k_lo, v_hi, v_lo);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool rows = d % 8 == 0 && aligned16(qkv) && aligned16(cosv) && aligned16(sinv) &&
+                    aligned8(q_hi) && aligned8(q_lo) && aligned8(k_hi) && aligned8(k_lo) &&
+                    aligned8(v_hi) && aligned8(v_lo);
+  if (rows) {
+    rope_row_kernel<<<row_grid(int64_t(b) * s), 256, 0, st>>>(qkv, cosv, sinv, b, s, hq, hkv, d,
+                                                               q_hi, q_lo, k_hi, k_lo, v_hi, v_lo);
+  } else {
+    const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
+    rope_split_kernel<<<grid_elems(total), 256, 0, st>>>(qkv, cosv, sinv, b, s, hq, hkv, d, q_hi,
+                                                         q_lo, k_hi, k_lo, v_hi, v_lo);
+  }
   return launch_status();
 }
 
@@ -590,9 +723,17 @@ extern "C" int mr_rope_bwd_split(const float* dq, const float* dk, const float* 
                                  const float* cosv, const float* sinv, int b, int s, int hq,
                                  int hkv, int d, uint16_t* hi, uint16_t* lo, void* stream) {
   if (!dq || !dk || !dv || !cosv || !sinv || b <= 0 || s <= 0 || d % 2) return MR_ERR_ARGUMENT;
-  const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
-  rope_bwd_split_kernel<<<grid_elems(total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      dq, dk, dv, cosv, sinv, b, s, hq, hkv, d, hi, lo);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool rows = d % 8 == 0 && aligned16(dq) && aligned16(dk) && aligned16(dv) &&
+                    aligned16(cosv) && aligned16(sinv) && aligned8(hi) && aligned8(lo);
+  if (rows) {
+    rope_bwd_row_kernel<<<row_grid(int64_t(b) * s), 256, 0, st>>>(dq, dk, dv, cosv, sinv, b, s, hq,
+                                                                   hkv, d, hi, lo);
+  } else {
+    const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
+    rope_bwd_split_kernel<<<grid_elems(total), 256, 0, st>>>(dq, dk, dv, cosv, sinv, b, s, hq, hkv,
+                                                             d, hi, lo);
+  }
   return launch_status();
 }
 
@@ -600,9 +741,13 @@ extern "C" int mr_heads_split(const float* src, int b, int s, int h, int d, int 
                               uint16_t* hi, uint16_t* lo, void* stream) {
   if (!src || !hi || !lo || b <= 0 || s <= 0 || h <= 0 || d % 4) return MR_ERR_ARGUMENT;
   if (!aligned16(src)) return MR_ERR_ALIGNMENT;
-  const int64_t total4 = int64_t(b) * s * h * d / 4;
-  heads_kernel<<<grid_elems(total4), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, b, s, h, d,
-                                                                                  merge, hi, lo);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (aligned8(hi) && aligned8(lo)) {
+    heads_row_kernel<<<row_grid(int64_t(b) * s), 256, 0, st>>>(src, b, s, h, d, merge, hi, lo);
+  } else {
+    const int64_t total4 = int64_t(b) * s * h * d / 4;
+    heads_kernel<<<grid_elems(total4), 256, 0, st>>>(src, b, s, h, d, merge, hi, lo);
+  }
   return launch_status();
 }
 

@@ -17,11 +17,13 @@ read once (2 B) but evaluated against ~200 candidates at ~8 float32 operations
 each; it is reported as candidate-element evaluations per second beside its
 bandwidth.
 
-``--attention`` times K7's causal softmax and its backward instead, at the 7B
-step's attention shape (8 x 28 heads x 2048 x 2048, band-limited writes):
-forward reads the scores up to each row's position (4 B) and writes P hi+lo
-(4 B) up to the band limit; backward reads dP (4 B) and P hi+lo (4 B) up to the
-position and writes dS hi+lo (4 B) up to the band limit.
+``--attention`` times K7's attention-side kernels instead, at the 7B step's
+shapes (8 x 2048 tokens, 28 query / 4 key-value heads of 128): the causal
+softmax (reads the scores up to each row's position, 4 B, and writes P hi+lo,
+4 B, up to the band limit) and its backward (reads dP 4 B and P hi+lo 4 B up
+to the position, writes dS hi+lo up to the band limit), RoPE with the head
+re-layout and its backward (4 B read + 4 B of hi+lo written per q/k/v element),
+and the head merge of the attention output (the same per element).
 
 Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick | --attention]
 Prints one JSON line per case, then a summary line.
@@ -163,9 +165,32 @@ def attention(reps: int = 5, batch: int = 8, heads: int = 28, seq: int = 2048) -
     def bwd():
         kernels.softmax_bwd_split(dp, state["p"], rows, seq, scale, True)
 
+    hq, hkv, d = heads, 4, 128
+    tokens = batch * seq
+    width = (hq + 2 * hkv) * d
+    qkv = torch.randn(tokens, width, device=device, generator=g)
+    ang = torch.rand(seq, d // 2, device=device, generator=g) * 6.0
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    dq = torch.randn(batch, hq, seq, d, device=device, generator=g)
+    dk = torch.randn(batch, hkv, seq, d, device=device, generator=g)
+    dv = torch.randn(batch, hkv, seq, d, device=device, generator=g)
+    o_heads = torch.randn(batch, hq, seq, d, device=device, generator=g)
+
+    def rope():
+        kernels.rope_split(qkv, cos, sin, batch, seq, hq, hkv, d)
+
+    def rope_bwd():
+        kernels.rope_bwd_split(dq, dk, dv, cos, sin, batch, seq, hq, hkv, d)
+
+    def merge():
+        kernels.heads_split(o_heads, batch, seq, hq, d, merge=True)
+
     results = []
     for name, fn, nbytes in (("K7_softmax_causal", fwd, 4 * live + 4 * band),
-                             ("K7_softmax_bwd", bwd, 8 * live + 4 * band)):
+                             ("K7_softmax_bwd", bwd, 8 * live + 4 * band),
+                             ("K7_rope", rope, 8 * tokens * width),
+                             ("K7_rope_bwd", rope_bwd, 8 * tokens * width),
+                             ("K7_heads_merge", merge, 8 * tokens * hq * d)):
         fn()
         torch.cuda.synchronize()
         ms = _time(fn, flush, reps)

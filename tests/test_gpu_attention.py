@@ -74,3 +74,59 @@ def test_softmax_kernels_match_float64(s, band):
     assert (got[written & ~mask] == 0).all()
     tol = 2.0 ** -14 * dref.abs().max()
     assert ((dgot - dref).abs() * written).max() <= tol
+
+
+def _rot(x1, x2, c, sn):
+    return x1 * c - x2 * sn, x1 * sn + x2 * c
+
+
+@pytest.mark.parametrize("b,s,hq,hkv,d", [(2, 64, 4, 2, 64), (1, 48, 3, 1, 128), (2, 16, 2, 1, 12)])
+def test_rope_and_head_layout_kernels_match_float64(b, s, hq, hkv, d):
+    """K7 RoPE (+bwd) and the head merge/split against float64 (head dims
+    divisible by 8 take the token-row kernels; d = 12 the element-wise ones).
+    hi + lo carries 16 significant bits, so values agree to 2^-15 of the largest."""
+    from mround_b200 import kernels
+
+    g = torch.Generator(device="cuda").manual_seed(d)
+    h = hq + 2 * hkv
+    half = d // 2
+    qkv = torch.randn(b * s, h * d, device="cuda", generator=g)
+    ang = torch.rand(s, half, device="cuda", generator=g) * 6.0
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    q, k, v = kernels.rope_split(qkv, cos, sin, b, s, hq, hkv, d)
+    x = qkv.double().view(b, s, h, d).permute(0, 2, 1, 3)  # (b, h, s, d)
+    c, sn = cos.double()[None, None], sin.double()[None, None]
+    o1, o2 = _rot(x[..., :half], x[..., half:], c, sn)
+    rot = torch.cat([o1, o2], -1)
+    want = {"q": rot[:, :hq], "k": rot[:, hq:hq + hkv], "v": x[:, hq + hkv:]}
+    for name, got in (("q", q), ("k", k), ("v", v)):
+        val = got[0].double() + got[1].double()
+        ref = want[name]
+        assert (val - ref).abs().max().item() <= 2.0 ** -15 * ref.abs().max().item(), name
+
+    dq = torch.randn(b, hq, s, d, device="cuda", generator=g)
+    dk = torch.randn(b, hkv, s, d, device="cuda", generator=g)
+    dv = torch.randn(b, hkv, s, d, device="cuda", generator=g)
+    hi, lo = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)
+    dd = torch.cat([dq, dk, dv], 1).double()  # (b, h, s, d)
+    g1 = dd[..., :half] * c + dd[..., half:] * sn
+    g2 = dd[..., half:] * c - dd[..., :half] * sn
+    back = torch.cat([g1, g2], -1)
+    back[:, hq + hkv:] = dd[:, hq + hkv:]
+    ref = back.permute(0, 2, 1, 3).reshape(b * s, h * d)
+    val = hi.double() + lo.double()
+    assert (val - ref).abs().max().item() <= 2.0 ** -15 * ref.abs().max().item()
+
+    if d % 4 == 0:
+        heads = torch.randn(b, h, s, d, device="cuda", generator=g)
+        mh, ml = kernels.heads_split(heads, b, s, h, d, merge=True)
+        ref = heads.permute(0, 2, 1, 3).reshape(b * s, h * d)
+        assert torch.equal(mh.float() + ml.float(), (ref.to(torch.bfloat16).float()
+                                                      + (ref - ref.to(torch.bfloat16).float())
+                                                      .to(torch.bfloat16).float()))
+        rows = torch.randn(b * s, h * d, device="cuda", generator=g)
+        sh, sl = kernels.heads_split(rows, b, s, h, d, merge=False)
+        ref = rows.view(b, s, h, d).permute(0, 2, 1, 3)
+        assert torch.equal(sh.float() + sl.float(), (ref.to(torch.bfloat16).float()
+                                                      + (ref - ref.to(torch.bfloat16).float())
+                                                      .to(torch.bfloat16).float()))
