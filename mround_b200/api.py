@@ -40,6 +40,7 @@ from mround_b200.formats.mlx_export import export_mlx, require_mlx_representable
 from mround_b200.pipeline.arch import get_arch
 from mround_b200.pipeline.dist import DistContext, init_from_env
 from mround_b200.pipeline.model import SyntheticModel, zipf_tokens
+from mround_b200.pipeline.resume import ResumeStore, run_fingerprint
 from mround_b200.pipeline.runner import QuantizationRunner, RunSummary
 from mround_b200.pipeline.tuning import QuantizedLayer
 from mround_b200.schemes import (
@@ -266,8 +267,14 @@ def quantize(model: str | Path | SyntheticModel, *, output_dir: str | Path, bits
              plan: Mapping[str, int] | None = None, scale_init: ScaleInit | str | None = None,
              min_block_coverage: float = MIN_BLOCK_COVERAGE, seed: int | None = None,
              memory_budget: int | None = None, memory_check: bool = True,
-             progress=print, dist: DistContext | None = None) -> QuantizeResult:
-    """Quantize ``model`` and write an MLX checkpoint to ``output_dir``."""
+             progress=print, dist: DistContext | None = None,
+             resume_dir: str | Path | None = None) -> QuantizeResult:
+    """Quantize ``model`` and write an MLX checkpoint to ``output_dir``.
+
+    ``resume_dir`` (not in the reference): record every finished block there,
+    and continue a run that stopped, tuning only the blocks it had not
+    finished (:mod:`mround_b200.pipeline.resume`).  A directory written by a
+    run with different settings or calibration is refused."""
     if export_format != "mlx":
         raise UnsupportedSchemeError(f"export_format {export_format!r} is not available; use 'mlx'")
     if holdout_batches < 0:
@@ -317,8 +324,17 @@ def quantize(model: str | Path | SyntheticModel, *, output_dir: str | Path, bits
     runner = QuantizationRunner(resolved, tuning, progress=(lambda r: progress(r.describe())) if progress else None,
                                 quantized_inputs=quantized_inputs, holdout_batches=holdout_batches,
                                 per_layer_recipe=per_layer_recipe, dist=dist, device=device)
+    resume = None
+    if resume_dir is not None:
+        fingerprint = run_fingerprint(
+            model=bundle.name, arch=arch, scheme=resolved, tuning=tuning, scheme_by_layer=overrides,
+            batches=batches, world=dist.world, quantized_inputs=quantized_inputs,
+            holdout_batches=holdout_batches, per_layer_recipe=per_layer_recipe,
+            calibration=calibration)
+        resume = ResumeStore(resume_dir, fingerprint, rank=dist.rank)
+        dist.barrier()
     summary, quantized = runner.run(bundle, batches, scheme_by_layer=overrides,
-                                    expected_blocks=arch.layers)
+                                    expected_blocks=arch.layers, resume=resume)
     skipped: list[tuple[str, str]] = [s for b in summary.blocks for s in b.skipped]
     t0 = time.perf_counter()
     remainder = {"model.embed_tokens": bundle.embed_tokens()}

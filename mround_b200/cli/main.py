@@ -52,6 +52,9 @@ def build_parser() -> argparse.ArgumentParser:
     q.add_argument("--memory-budget", type=int, default=None)
     q.add_argument("--skip-memory-check", action="store_true")
     q.add_argument("--dry-run", action="store_true", help="Resolve and validate, then stop.")
+    q.add_argument("--resume-dir", default=None,
+                   help="Record each finished block here; rerunning the same command with "
+                        "the same directory continues after the last finished block.")
     q.add_argument("--scoring-samples", type=int, default=None,
                    help="Sequences for the mixed-precision scoring pass (api scoring_samples).")
     q.add_argument("--scoring-seq-len", type=int, default=None,
@@ -84,7 +87,8 @@ def _quantize(args: argparse.Namespace) -> int:
                       scoring_samples=args.scoring_samples, scoring_seq_len=args.scoring_seq_len,
                       sensitivity_gradients=args.sensitivity_gradients,
                       memory_check=not args.skip_memory_check,
-                      min_block_coverage=0.0 if args.allow_dense else MIN_BLOCK_COVERAGE)
+                      min_block_coverage=0.0 if args.allow_dense else MIN_BLOCK_COVERAGE,
+                      resume_dir=args.resume_dir)
     if result.summary is not None:
         print(result.summary.describe())
     print(result.describe())

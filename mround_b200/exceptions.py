@@ -20,6 +20,7 @@ __all__ = [
     "MemoryBudgetError",
     "NativeLibraryError",
     "PlatformError",
+    "ResumeError",
     "SchemeError",
     "UnsupportedSchemeError",
 ]
@@ -63,6 +64,10 @@ class MemoryBudgetError(MRoundError):
 
 class DeviceError(MRoundError):
     """The native CUDA library reported a failure (a CUDA error or a timeout)."""
+
+
+class ResumeError(MRoundError):
+    """A resume directory belongs to another run, or one of its block files is unreadable."""
 
 
 class NativeLibraryError(MRoundError):

@@ -27,10 +27,11 @@ from typing import Any
 
 import torch
 
-from mround_b200.exceptions import ArchitectureError, CalibrationError
+from mround_b200.exceptions import ArchitectureError, CalibrationError, ResumeError
 from mround_b200.pipeline.block import DeviceBlock, Precision
 from mround_b200.pipeline.dist import DistContext
 from mround_b200.pipeline.model import SyntheticModel
+from mround_b200.pipeline.resume import ResumeStore
 from mround_b200.pipeline.tuning import BlockTuner, QuantizedLayer
 from mround_b200.schemes import DEFAULT_EPS_FP32, QuantScheme, TuningConfig
 
@@ -224,7 +225,12 @@ class QuantizationRunner:
     def run(self, model: SyntheticModel, calibration_batches: Sequence[Any], *,
             scheme_by_layer: Mapping[str, QuantScheme] | None = None,
             expected_blocks: int | None = None, blocks: Sequence[int] | None = None,
+            resume: ResumeStore | None = None,
             ) -> tuple[RunSummary, dict[str, QuantizedLayer]]:
+        """Quantize the model's blocks in order.  With ``resume``, blocks that
+        an earlier run with the same fingerprint finished are loaded instead
+        of tuned (a leading run of them; the first block without a record and
+        every later one are tuned), and each newly tuned block is recorded."""
         started = time.perf_counter()
         meter = _Meter(self.device)
         n_blocks = model.arch.layers
@@ -238,9 +244,13 @@ class QuantizationRunner:
         results: list[BlockResult] = []
         exported: dict[str, QuantizedLayer] = {}
         schemes: dict[str, QuantScheme] = {}
+        resuming = resume is not None
         for index in indices:
             block = DeviceBlock(model.arch, model.block(index), self.device)
             name = model.block_name(index)
+            # every rank takes the same decision, even if one sees the file late
+            resuming = resuming and self.dist.max_scalar(0.0 if resume.has(index) else 1.0,
+                                                         self.device) == 0.0
             with meter.stage("targets"):
                 with torch.no_grad():
                     if quantized_stream is not None:
@@ -251,8 +261,11 @@ class QuantizationRunner:
                         targets = [block.forward_fused(x, self.precision, False)[0]
                                    for x in reference_stream]
             inputs = quantized_stream if quantized_stream is not None else reference_stream
-            result, layers = self.quantize_block(block, name, inputs, targets,
-                                                 scheme_by_layer=scheme_by_layer, meter=meter)
+            if resuming:
+                result, layers = self._restore_block(block, resume, index)
+            else:
+                result, layers = self.quantize_block(block, name, inputs, targets,
+                                                     scheme_by_layer=scheme_by_layer, meter=meter)
             exported.update(layers)
             for path in layers:
                 schemes[path] = self._scheme_for(path, scheme_by_layer)
@@ -263,9 +276,15 @@ class QuantizationRunner:
                             quantized_stream[i] = block.forward_fused(x, self.precision, False)[0]
             if quantized_stream is None:
                 reference_stream = targets
+            if not resuming:
+                result = dataclasses.replace(result, peak_memory_bytes=meter.peak,
+                                             stage_peaks=meter.take())
+                if resume is not None:
+                    resume.save(index, result, layers,
+                                {n: l.wq_hi for n, l in block.layers.items() if l.wq_hi is not l.w})
+            else:
+                meter.take()
             del block
-            result = dataclasses.replace(result, peak_memory_bytes=meter.peak,
-                                         stage_peaks=meter.take())
             results.append(result)
             if self.progress is not None and self.dist.rank == 0:
                 self.progress(result)
@@ -275,6 +294,26 @@ class QuantizationRunner:
                        scheme_by_layer=schemes, before_blocks=before_blocks),
             exported,
         )
+
+    def _restore_block(self, block: DeviceBlock, resume: ResumeStore,
+                       index: int) -> tuple[BlockResult, dict[str, QuantizedLayer]]:
+        """A finished block from ``resume``: its committed bf16 weights become
+        the block's operands (so the quantized stream advances exactly as it
+        did), its stored layers and result are returned as tuned ones."""
+        stored = resume.load(index)
+        for lname, weight in stored.committed.items():
+            if lname not in block.layers:
+                raise ResumeError(f"{resume.path(index)} holds a weight {lname!r} this block lacks")
+            layer = block.layers[lname]
+            if tuple(weight.shape) != tuple(layer.w.shape) or weight.dtype != layer.w.dtype:
+                raise ResumeError(f"{resume.path(index)}: {lname} is {tuple(weight.shape)} "
+                                  f"{weight.dtype}, the block's is {tuple(layer.w.shape)} {layer.w.dtype}")
+            layer.wq_hi, layer.wq_lo, layer.grad = weight.to(self.device), None, None
+        f = dict(stored.result)
+        f["tuned"] = tuple(f.get("tuned", ()))
+        f["skipped"] = tuple(tuple(x) for x in f.get("skipped", ()))
+        f["stage_peaks"] = dict(f.get("stage_peaks") or {})
+        return BlockResult(**f), ResumeStore.quantized_layers(stored, QuantizedLayer)
 
     # ------------------------------------------------------------------ block
     def tuner_for(self, block: DeviceBlock, name: str,

@@ -186,3 +186,45 @@ def test_quantize_from_checkpoint_directory_matches_synthetic(tmp_path):
     assert set(a) == set(b)
     for name in a:
         assert np.array_equal(a[name], b[name]), name
+
+
+def test_resume_continues_a_stopped_run(tmp_path):
+    """A run stopped after block 0 and restarted with the same resume
+    directory writes the same checkpoint, tensor for tensor, as a run that was
+    never stopped (block 0 is loaded, not re-tuned); a run with other settings
+    refuses the directory."""
+    from mround_b200.api import quantize
+    from mround_b200.exceptions import ResumeError
+    from mround_b200.formats.safetensors_io import read_safetensors
+    from mround_b200.schemes import TuningConfig
+
+    tuning = TuningConfig(iters=6, n_samples=4, seq_len=64, batch_size=2)
+    kw = dict(bits=2, group_size=32, symmetry="asym", tuning=tuning)
+    full, part, rdir = tmp_path / "full", tmp_path / "part", tmp_path / "resume"
+    quantize("synthetic:tiny-qwen2@5", output_dir=full, progress=None, **kw)
+
+    class Stop(Exception):
+        pass
+
+    def stop_after_block_0(line):
+        if line.startswith("block   0"):
+            raise Stop
+
+    with pytest.raises(Stop):
+        quantize("synthetic:tiny-qwen2@5", output_dir=part, progress=stop_after_block_0,
+                 resume_dir=rdir, **kw)
+    assert sorted(p.name for p in rdir.glob("block_*.pt")) == ["block_0000.pt"]
+    lines = []
+    quantize("synthetic:tiny-qwen2@5", output_dir=part, progress=lines.append, resume_dir=rdir,
+             **kw)
+    assert sorted(p.name for p in rdir.glob("block_*.pt")) == ["block_0000.pt", "block_0001.pt"]
+    assert len([ln for ln in lines if ln.startswith("block")]) == 2
+    a, _, _ = read_safetensors(full / "model.safetensors")
+    b, _, _ = read_safetensors(part / "model.safetensors")
+    assert set(a) == set(b)
+    for name in a:
+        assert np.array_equal(a[name], b[name]), name
+    with pytest.raises(ResumeError):
+        quantize("synthetic:tiny-qwen2@5", output_dir=part, progress=None, resume_dir=rdir,
+                 bits=2, group_size=32, symmetry="asym",
+                 tuning=TuningConfig(iters=7, n_samples=4, seq_len=64, batch_size=2))
