@@ -390,6 +390,19 @@ int mr_reduce_slots(const float* slots, int64_t slot_stride, int64_t n, int worl
                     const unsigned long long* flags, unsigned long long epoch, float* out,
                     void* stream);
 
+/*
+ * Copy-engine form of the source side of the exchange (the GEMM writes the
+ * full weight gradient locally): copy ``bytes`` from ``src`` (this rank's rows
+ * for one owner) to ``dst`` (the owner's slot for this source; peer memory
+ * from mr_ipc_import, or this rank's own slot) with one cudaMemcpyAsync on
+ * ``stream``, then release ``epoch`` into ``flag`` (the owner's flag for this
+ * source) from a one-thread kernel ordered after the copy.  No SM moves data.
+ * Replaces, like mr_gemm_rs, the gradient sum across data-parallel ranks
+ * (mround/pipeline/runner.py:984-1044).
+ */
+int mr_peer_send(void* dst, const void* src, int64_t bytes, unsigned long long* flag,
+                 unsigned long long epoch, void* stream);
+
 /* Device status word of the exchange (0 ok, MR_ERR_TIMEOUT); synchronizes. */
 int mr_peer_status(int reset);
 

@@ -70,6 +70,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_ipc_import": (_I, [_P, _I64, _P, _P]),
     "mr_ipc_close": (_I, [_P]),
     "mr_reduce_slots": (_I, [_P, _I64, _I64, _I, _P, ctypes.c_uint64, _P, _P]),
+    "mr_peer_send": (_I, [_P, _P, _I64, _P, ctypes.c_uint64, _P]),
     "mr_peer_status": (_I, [_I]),
     "mr_rmsnorm_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P, _P]),
     "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P, _P]),

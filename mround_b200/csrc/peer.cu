@@ -1,5 +1,9 @@
 // Peer memory for the fused GEMM -> reduce-scatter of the data-parallel step.
 //
+// mr_peer_send: the copy-engine source side -- one cudaMemcpyAsync of a rank's
+// rows into their owner's slot, then a one-thread kernel that releases the
+// step's epoch into the owner's flag.
+//
 // mr_ipc_export / mr_ipc_import: CUDA IPC handles of device buffers, so every
 // rank (one process per GPU) can store into every other rank's slot buffers
 // over NVLink; the handle names the allocation that holds the buffer and the
@@ -82,6 +86,14 @@ __global__ void __launch_bounds__(kThreads) reduce_slots_kernel(
   }
 }
 
+// Publishes ``epoch`` to one owner's flag after the stream's preceding copy:
+// the copy has completed when this kernel starts (stream order), the fence
+// orders the flag after it at system scope.
+__global__ void release_flag_kernel(unsigned long long* flag, unsigned long long epoch) {
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(epoch) : "memory");
+}
+
 using GetRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
 
 GetRangeFn range_fn() {
@@ -156,6 +168,22 @@ extern "C" int mr_reduce_slots(const float* slots, int64_t slot_stride, int64_t 
   const int grid = grid_for(n / 4, kThreads, 4);
   reduce_slots_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       slots, slot_stride, n, world, flags, epoch, out);
+  return launch_status();
+}
+
+extern "C" int mr_peer_send(void* dst, const void* src, int64_t bytes, unsigned long long* flag,
+                            unsigned long long epoch, void* stream) {
+  if (!dst || !src || !flag || bytes < 0 || epoch == 0) return MR_ERR_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(flag) & 7u) return MR_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bytes > 0) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, size_t(bytes), cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return MR_ERR_LAUNCH;
+    }
+  }
+  release_flag_kernel<<<1, 1, 0, s>>>(flag, epoch);
   return launch_status();
 }
 

@@ -4,14 +4,16 @@ Usage: python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.
        -m mround_b200.exchange_probe
 
 For the block's four fused weight gradients (qkv, o, gate_up, down) at the
-step's per-rank token count (16384 / N), three ways, each averaged over 10
+step's per-rank token count (16384 / N), four ways, each averaged over 10
 iterations after 3 warm-up ones, CUDA events, max over ranks:
 
 * ``gemm``: the four dW GEMMs only (no exchange -- the lower bound);
 * ``nccl``: each dW GEMM into a local buffer, then an async NCCL
   reduce-scatter of its rows;
 * ``p2p``: each dW GEMM storing its rows into the owners' slots over NVLink
-  (``mr_gemm_rs``), then every owner's ordered sum (``mr_reduce_slots``).
+  (``mr_gemm_rs``), then every owner's ordered sum (``mr_reduce_slots``);
+* ``copy``: each dW GEMM into a local buffer, then the copy engines move each
+  owner's rows into its slot (``mr_peer_send``), then the same ordered sum.
 
 Rank 0 prints one line per way.
 """
@@ -43,6 +45,7 @@ def main() -> None:
     grads = [torch.empty(r, c, device=dev) for r, c in SHAPES]
     shards = [torch.empty(r // world, c, device=dev) for r, c in SHAPES]
     peer = PeerExchange(dist, SHAPES, dev) if world > 1 else None
+    copier = PeerExchange(dist, SHAPES, dev, copy_engine=True) if world > 1 else None
     epoch = 0
 
     def step(way: str) -> None:
@@ -57,6 +60,18 @@ def main() -> None:
             for ex, out in zip(peer.layers, shards):
                 kernels.reduce_slots(ex.slots, ex.flags, epoch, out)
             return
+        if way == "copy":
+            epoch += 1
+            for (rows, cols), (dy, x), g, ex in zip(SHAPES, ins, grads, copier.layers):
+                kernels.gemm(dy[0], dy[1], x[0], x[1], g, m=rows, n=cols, k=t, a_kmajor=False,
+                             b_kmajor=False, lda=rows, ldb=cols, ldc=cols, precision=3)
+                ex.epoch = epoch
+                ex.send(g)
+            for ex in copier.layers:
+                ex.wait_copies()
+            for ex, out in zip(copier.layers, shards):
+                kernels.reduce_slots(ex.slots, ex.flags, epoch, out)
+            return
         works = []
         for (rows, cols), (dy, x), g, out in zip(SHAPES, ins, grads, shards):
             kernels.gemm(dy[0], dy[1], x[0], x[1], g, m=rows, n=cols, k=t, a_kmajor=False,
@@ -66,7 +81,7 @@ def main() -> None:
         for w in works:
             w.wait()
 
-    ways = ("gemm", "nccl", "p2p") if world > 1 else ("gemm",)
+    ways = ("gemm", "nccl", "p2p", "copy") if world > 1 else ("gemm",)
     for way in ways:
         for _ in range(3):
             step(way)
@@ -86,6 +101,7 @@ def main() -> None:
     dist.barrier()
     if peer is not None:
         peer.close()
+        copier.close()
     if world > 1:
         tdist.destroy_process_group()
 

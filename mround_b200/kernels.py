@@ -362,6 +362,18 @@ def reduce_slots(slots, flags, epoch: int, out) -> None:
     _count()
 
 
+def peer_send(dst_ptr: int, src, flag_ptr: int, epoch: int) -> None:
+    """Copy ``src`` (contiguous float32 rows) to ``dst_ptr`` with the copy
+    engine, then release ``epoch`` into the flag at ``flag_ptr`` -- both on the
+    current stream."""
+    if not src.is_contiguous():
+        raise SchemeError("peer_send needs contiguous rows")
+    status = lib().mr_peer_send(dst_ptr, _ptr(src, torch.float32, "src"), src.numel() * 4,
+                                flag_ptr, int(epoch), _stream())
+    check(status, "mr_peer_send")
+    _count()
+
+
 def causal_fraction(causal: int, m: int, n: int, k: int, seq: int, bk: int = 64) -> float:
     """Share of the dense tile work a causal mode of K3 actually computes
     (mirrors the kernel's tile and K-tile predicates; BM = 128, K slices of

@@ -357,7 +357,14 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
         if layer.grad is None:
             return
         ex = layer.exchange
-        if ex is not None and ex.active and not layer.accumulate_grad:
+        if ex is not None and ex.active and not layer.accumulate_grad and ex.copy_engine:
+            # the whole gradient locally, then the copy engines move each
+            # owner's rows over NVLink while the backward goes on
+            kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, m=n_out, n=n_in, k=t,
+                         a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in,
+                         precision=prec.grad_weight)
+            ex.send(layer.grad)
+        elif ex is not None and ex.active and not layer.accumulate_grad:
             # rows go straight to their owner ranks over NVLink
             kernels.gemm_rs(dy[0], dy[1], x_in[0], x_in[1], m=n_out, n=n_in, k=t, a_kmajor=False,
                             b_kmajor=False, lda=n_out, ldb=n_in, precision=prec.grad_weight,

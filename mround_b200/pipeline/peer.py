@@ -9,6 +9,12 @@ that a rank's weight-gradient GEMM (``mr_gemm_rs``) stores each row directly
 into its owner's slot for this source and releases the step's epoch into the
 owner's flag, and the owner sums its slots in rank order (``mr_reduce_slots``).
 
+With ``copy_engine``, the GEMM instead writes the whole gradient locally and
+the copy engines move each owner's rows (``mr_peer_send``: one
+cudaMemcpyAsync per owner on that owner's stream, then a one-thread kernel
+releasing the epoch), so no SM stores to peer memory and the transfer overlaps
+the rest of the backward.  The owner's sum is the same ``mr_reduce_slots``.
+
 One allocation per rank means one handle per peer mapping.  Mappings are
 closed by :meth:`PeerExchange.close`.  No multicast object is involved.
 """
@@ -21,6 +27,7 @@ import dataclasses
 import torch
 import torch.distributed as tdist
 
+from mround_b200 import kernels
 from mround_b200._native import check, lib
 from mround_b200.pipeline.dist import DistContext
 
@@ -40,14 +47,47 @@ class LayerExchange:
     done: torch.Tensor     # this rank's CTA counter (int32, zero between launches)
     epoch: int = 0
     active: bool = False
+    streams: list | None = None  # copy-engine mode: one stream per owner rank
+    copy_events: list = dataclasses.field(default_factory=list)
+
+    @property
+    def copy_engine(self) -> bool:
+        return self.streams is not None
+
+    def send(self, grad: torch.Tensor) -> None:
+        """Copy-engine mode: after the current stream's work so far (the GEMM
+        that wrote ``grad``, the full float32 gradient), move each owner's rows
+        into its slot for this rank and release the epoch into its flag."""
+        ready = torch.cuda.Event()
+        ready.record()
+        self.copy_events = []
+        per = self.rows_per_rank
+        for owner, stream in enumerate(self.streams):
+            stream.wait_event(ready)
+            with torch.cuda.stream(stream):
+                kernels.peer_send(self.dst_ptrs[owner], grad[owner * per:(owner + 1) * per],
+                                  self.flag_ptrs[owner], self.epoch)
+                done = torch.cuda.Event()
+                done.record(stream)
+            self.copy_events.append(done)
+
+    def wait_copies(self) -> None:
+        """Order the current stream after this rank's copies (its own flag is
+        then set, and the gradient buffer may be written again)."""
+        stream = torch.cuda.current_stream()
+        for event in self.copy_events:
+            stream.wait_event(event)
+        self.copy_events = []
 
 
 class PeerExchange:
     def __init__(self, dist: DistContext, shapes: list[tuple[int, int]],
-                 device: torch.device) -> None:
+                 device: torch.device, *, copy_engine: bool = False) -> None:
         """``shapes``: (rows, cols) of each fused weight, rows divisible by the
         rank count, cols by 4.  Collective: every rank calls it in the same order."""
         world, rank = dist.world, dist.rank
+        self.streams = ([torch.cuda.Stream(device) for _ in range(world)] if copy_engine
+                        else None)
         self.world, self.rank = world, rank
         offsets, total = [], 0
         for rows, cols in shapes:
@@ -86,7 +126,7 @@ class PeerExchange:
             dst = [pool_ptrs[o] + start * 4 + rank * slot_bytes for o in range(world)]
             flag = [pool_ptrs[o] + flag_off * 4 + (i * world + rank) * 8 for o in range(world)]
             self.layers.append(LayerExchange(per, cols, dst, flag, slots, flags_all[i],
-                                             self.done[i:i + 1]))
+                                             self.done[i:i + 1], streams=self.streams))
 
     def close(self) -> None:
         """Release the peer mappings (after the device has finished with them)."""

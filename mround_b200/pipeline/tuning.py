@@ -227,9 +227,11 @@ class BlockTuner:
                  pieces: int = 1, exchange: str = "p2p") -> None:
         """``exchange``: how the row-sharded update gathers each rank's rows of
         the gradient -- "p2p" (the weight-gradient GEMM stores them into their
-        owners' slots over NVLink) or "nccl" (a reduce-scatter after the GEMM)."""
-        if exchange not in ("p2p", "nccl"):
-            raise ValueError(f"exchange must be 'p2p' or 'nccl', got {exchange!r}")
+        owners' slots over NVLink), "copy" (the GEMM writes locally and the
+        copy engines move the rows into the same slots) or "nccl" (a
+        reduce-scatter after the GEMM)."""
+        if exchange not in ("p2p", "copy", "nccl"):
+            raise ValueError(f"exchange must be 'p2p', 'copy' or 'nccl', got {exchange!r}")
         self.block = block
         self.suppress = suppress
         self.precision = precision
@@ -278,12 +280,12 @@ class BlockTuner:
         # step; at most 8 ranks; every rank agrees before it is used).
         self.peer = None
         self._epoch = 0
-        if (self.sharded and exchange == "p2p" and pieces == 1 and dist.world <= 8
+        if (self.sharded and exchange in ("p2p", "copy") and pieces == 1 and dist.world <= 8
                 and all(t.layer.in_features % 4 == 0 for t in self.tunables)):
             from mround_b200.pipeline.peer import PeerExchange
 
             self.peer = PeerExchange(dist, [tuple(t.layer.w.shape) for t in self.tunables],
-                                     block.device)
+                                     block.device, copy_engine=exchange == "copy")
             for t, ex in zip(self.tunables, self.peer.layers):
                 t.layer.exchange = ex
 
@@ -350,6 +352,13 @@ class BlockTuner:
                 self._wait(t.layer)
                 t.update(step, iters)
             return
+        # Copy-engine exchange: every copy and flag release of this rank ends
+        # before the first owner-side sum spins on this GPU, so no flag kernel
+        # of this rank ever waits for an SM behind a spinning sum.
+        for t in self.tunables:
+            ex = t.layer.exchange
+            if ex is not None and ex.active and ex.copy_engine:
+                ex.wait_copies()
         # rows of this rank, then the operands' all-gather; qkv first, so the
         # next forward's first GEMM waits on the smallest gather only
         for t in self.tunables:

@@ -77,7 +77,7 @@ def _rank(rank, world, port, q, exchange="p2p"):
         rows = ctx.shard(SHAPE[0])
         tuner = _tuner(block, ctx, exchange)
         assert tuner.sharded, "tiny-qwen2's fused rows divide by 2: the row-sharded update runs"
-        assert (tuner.peer is not None) == (exchange == "p2p")
+        assert (tuner.peer is not None) == (exchange in ("p2p", "copy"))
         loss = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 0, 10)
         # a second step runs on the all-gathered operands of the first
         loss2 = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 1, 10)
@@ -117,6 +117,20 @@ def test_two_gpu_fused_exchange_equals_nccl_reduce_scatter():
     fused = _run_ranks("p2p")
     nccl = _run_ranks("nccl")
     for a, b in zip(fused, nccl):
+        assert a[1] == b[1] and a[2] == b[2]
+        for x, y in zip(a[3] + a[4], b[3] + b[4]):
+            assert np.array_equal(x, y)
+
+
+def test_two_gpu_copy_engine_exchange_equals_nccl_reduce_scatter():
+    """The copy-engine form (local GEMM, cudaMemcpyAsync of each owner's rows
+    into its slot, flag released after the copy) gives the same parameters,
+    bit for bit, as the NCCL reduce-scatter."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    copied = _run_ranks("copy")
+    nccl = _run_ranks("nccl")
+    for a, b in zip(copied, nccl):
         assert a[1] == b[1] and a[2] == b[2]
         for x, y in zip(a[3] + a[4], b[3] + b[4]):
             assert np.array_equal(x, y)
