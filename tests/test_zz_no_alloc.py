@@ -13,8 +13,6 @@ everything else.
 
 from __future__ import annotations
 
-import ctypes
-
 import pytest
 import torch
 
