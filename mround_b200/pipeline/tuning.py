@@ -3,14 +3,18 @@
 One step of ``QuantizationRunner._tune`` (reference
 mround/pipeline/runner.py:914-937) is, here:
 
-1. forward of the block on the fake-quantized operands (K3 GEMMs, torch for
-   norms/rope/attention/SwiGLU);
+1. forward of the block on the fake-quantized operands (K3 GEMMs for the
+   linears and the attention products, K7 for norms, RoPE, softmax, SwiGLU);
 2. K4: residual, exact outlier threshold (radix select; the histograms are
    all-reduced across data-parallel ranks), loss and dL/dout;
-3. backward: K3 GEMMs for dX and dW, each fused weight's dW all-reduced over
-   NCCL as soon as it is produced (overlapping the rest of the backward);
-4. K2 per tunable linear: straight-through gradient, signed step, projection
-   and -- fused into the same pass -- the next step's fake-quantized operand.
+3. backward: K3 GEMMs for dX and dW; across data-parallel ranks each fused
+   weight's dW is exchanged as soon as it is produced -- by default its rows
+   go straight from the GEMM epilogue to their owner ranks over NVLink
+   (``mr_gemm_rs``), or through the copy engines or an NCCL reduce-scatter;
+4. K2 per tunable linear (on this rank's rows when the update is row-sharded):
+   straight-through gradient, signed step, projection and -- fused into the
+   same pass -- the next step's fake-quantized operand, all-gathered across
+   ranks before the next forward reads it.
 
 No host synchronisation happens inside a step: per-step losses stay on the
 device and are read once per block.
@@ -177,7 +181,7 @@ class TunableLayer:
 
     def load(self, path: str, v: torch.Tensor, alpha: torch.Tensor, beta: torch.Tensor,
              init_scale: torch.Tensor | None = None) -> None:
-        """Set one member's parameters (used by parity tests and resume)."""
+        """Set one member's parameters (used by the parity tests)."""
         for m in self.members:
             if m.path == path:
                 r0, r1 = m.rows
