@@ -1,8 +1,12 @@
 """One decoder block on the device: fused weights, forward, backward.
 
 The block is the mlx-lm Llama/Qwen2 decoder layer the reference runs in
-``block_output`` (mround/pipeline/blocks.py:578-606), restated in torch
-float32 with its linears on the tcgen05 GEMM (K3):
+``block_output`` (mround/pipeline/blocks.py:578-606), in float32 semantics.
+The tuning path (``forward_fused`` / ``backward_fused``) runs every op on this
+library's kernels -- the linears and the attention products on the tcgen05
+GEMM (K3), norms, RoPE, softmax and SwiGLU on K7 -- with an explicit
+backward; ``DeviceBlock.forward`` is an autograd form (K3 linears, torch for
+the rest) kept as a cross-check:
 
     h1  = rmsnorm(x) * w_in            q|k|v = h1 @ Wqkv^T (+ b)
     q,k = rope(q), rope(k)             a = causal_gqa_sdpa(q, k, v)
