@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--group", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "copy", "nccl"],
+                    help="weight-gradient exchange at N > 1 (default: fused GEMM peer stores)")
     return ap.parse_args()
 
 
@@ -199,7 +201,8 @@ def make_tuner(args, block, dist):
     from mround_b200.schemes import QuantScheme, TuningConfig
 
     scheme = QuantScheme(bits=args.bits, group_size=args.group, symmetry="asym")
-    runner = QuantizationRunner(scheme, TuningConfig(iters=ITERS), dist=dist)
+    runner = QuantizationRunner(scheme, TuningConfig(iters=ITERS), dist=dist,
+                                exchange=args.exchange)
     return runner.tuner_for(block, "model.layers.0")
 
 
@@ -431,8 +434,10 @@ def main():
                                f"global batch {BATCH}x{SEQ}, {ITERS} it/block, {N_BATCHES} batches",
                    "global_batch": BATCH, "seq_len": SEQ, "parallelism": f"dp{dist.world}",
                    "gradient_exchange": ("none" if dist.world == 1 else
-                                         "fused dW GEMM -> reduce-scatter over NVLink peer stores"
-                                         if tuner.peer is not None else "NCCL reduce-scatter"),
+                                         "NCCL reduce-scatter" if tuner.peer is None else
+                                         "dW GEMM, then copy-engine transfers of each owner's rows"
+                                         if tuner.peer.streams is not None else
+                                         "fused dW GEMM -> reduce-scatter over NVLink peer stores"),
                    "l2": "inputs larger than L2 (235 MB per batch input)"},
         "ms_forward_batch": t_fwd, "block_seconds": blk_s, "wall_s_model": blk_s * arch.layers,
         "gpu_launches": launches,

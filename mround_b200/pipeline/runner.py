@@ -184,7 +184,12 @@ class QuantizationRunner:
                  eps: float = DEFAULT_EPS_FP32, quantized_inputs: bool = True,
                  holdout_batches: int = 0, per_layer_recipe: bool = False,
                  precision: Precision | None = None, dist: DistContext | None = None,
-                 device: torch.device | str | None = None, keep_codes: bool = False) -> None:
+                 device: torch.device | str | None = None, keep_codes: bool = False,
+                 exchange: str = "p2p") -> None:
+        """``exchange``: the data-parallel weight-gradient exchange of the
+        row-sharded update -- "p2p" (GEMM epilogue stores into the owners'
+        memory over NVLink), "copy" (copy engines) or "nccl" (reduce-scatter);
+        see :class:`~mround_b200.pipeline.tuning.BlockTuner`."""
         if holdout_batches < 0:
             raise CalibrationError(f"holdout_batches must be zero or more, got {holdout_batches}")
         self.scheme = scheme
@@ -198,6 +203,7 @@ class QuantizationRunner:
         self.dist = dist or DistContext()
         self.device = torch.device(device or "cuda")
         self.keep_codes = keep_codes
+        self.exchange = exchange
 
     def _scheme_for(self, path: str, overrides: Mapping[str, QuantScheme] | None) -> QuantScheme:
         if overrides is None:
@@ -324,7 +330,7 @@ class QuantizationRunner:
                                        per_layer=self.per_layer_recipe)
         return BlockTuner(block, schemes, rates, suppress=suppress, eps=self.eps,
                           precision=self.precision, dist=self.dist,
-                          pieces=self.tuning.micro_batches)
+                          pieces=self.tuning.micro_batches, exchange=self.exchange)
 
     def quantize_block(self, block: DeviceBlock, name: str, inputs: list[torch.Tensor],
                        targets: list[torch.Tensor], *,
