@@ -34,7 +34,6 @@ from __future__ import annotations
 
 import dataclasses
 import hashlib
-import io
 import json
 import os
 from collections.abc import Mapping, Sequence
@@ -131,10 +130,16 @@ class ResumeStore:
         return sorted(int(p.stem.split("_")[1]) for p in self.directory.glob("block_*.pt"))
 
     @staticmethod
-    def _write_atomic(path: Path, payload: bytes) -> None:
+    def _write_atomic(path: Path, payload: bytes | dict) -> None:
+        """Write to a temporary name, flush to disk, then rename over ``path``
+        (bytes are written as they are; a dict is written by torch.save
+        straight to the file, without a second copy in host memory)."""
         tmp = path.with_name(path.name + f".tmp{os.getpid()}")
         with open(tmp, "wb") as f:
-            f.write(payload)
+            if isinstance(payload, bytes):
+                f.write(payload)
+            else:
+                torch.save(payload, f)
             f.flush()
             os.fsync(f.fileno())
         os.replace(tmp, path)
@@ -157,9 +162,7 @@ class ResumeStore:
             "committed": {name: t.detach().to("cpu", copy=True).contiguous()
                           for name, t in committed.items()},
         }
-        buf = io.BytesIO()
-        torch.save(record, buf)
-        self._write_atomic(self.path(index), buf.getvalue())
+        self._write_atomic(self.path(index), record)
 
     def load(self, index: int) -> StoredBlock:
         path = self.path(index)
