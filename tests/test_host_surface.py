@@ -122,6 +122,8 @@ def test_cli_dry_run(capsys):
     assert main(["quantize", "synthetic:tiny-qwen2", "-o", "/tmp/x", "--bits", "2",
                  "--dry-run"]) == 0
     assert "searched" in capsys.readouterr().out
+    assert main(["quantize", "synthetic:tiny-qwen2", "-o", "/tmp/x", "--resume-dir", "/tmp/r",
+                 "--dry-run"]) == 0
 
 
 def _fake_layer(rows, cols, bits, group, seed):
