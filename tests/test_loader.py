@@ -106,3 +106,48 @@ def test_cli_dry_run_on_checkpoint(tmp_path, capsys):
     write_checkpoint(tmp_path)
     assert main(["quantize", str(tmp_path), "-o", str(tmp_path / "out"), "--bits", "2",
                  "--asym", "--dry-run"]) == 0
+
+
+@pytest.mark.parametrize("family", ["qwen2", "llama"])
+def test_reads_a_checkpoint_written_by_transformers(tmp_path, family):
+    """A tiny model saved by transformers' own ``save_pretrained`` (bf16,
+    safetensors) loads here with every tensor equal and the architecture read
+    from its config.json."""
+    transformers = pytest.importorskip("transformers")
+    if family == "qwen2":
+        cfg = transformers.Qwen2Config(hidden_size=64, intermediate_size=160, num_hidden_layers=2,
+                                       num_attention_heads=4, num_key_value_heads=2,
+                                       vocab_size=300, rms_norm_eps=1e-6,
+                                       tie_word_embeddings=True, max_position_embeddings=256,
+                                       rope_parameters={"rope_type": "default",
+                                                        "rope_theta": 5.0e5})
+        lm = transformers.Qwen2ForCausalLM(cfg)
+    else:
+        cfg = transformers.LlamaConfig(hidden_size=64, intermediate_size=160, num_hidden_layers=2,
+                                       num_attention_heads=4, num_key_value_heads=2,
+                                       vocab_size=300, rms_norm_eps=1e-5,
+                                       tie_word_embeddings=False, max_position_embeddings=256,
+                                       rope_parameters={"rope_type": "default",
+                                                        "rope_theta": 5.0e5})
+        lm = transformers.LlamaForCausalLM(cfg)
+    lm = lm.to(torch.bfloat16)
+    lm.save_pretrained(tmp_path, safe_serialization=True)
+    ck = CheckpointModel(tmp_path)
+    arch = ck.arch
+    assert (arch.family, arch.hidden, arch.layers, arch.heads, arch.kv_heads) == (family, 64, 2, 4, 2)
+    assert arch.head_dim == 16 and arch.intermediate == 160 and arch.vocab == 300
+    assert arch.qkv_bias == (family == "qwen2") and arch.tied == (family == "qwen2")
+    assert arch.rope_theta == 5.0e5 and arch.rms_eps == cfg.rms_norm_eps
+    state = lm.state_dict()
+    assert torch.equal(ck.embed_tokens().to(torch.bfloat16), state["model.embed_tokens.weight"])
+    assert torch.equal(ck.final_norm().to(torch.bfloat16), state["model.norm.weight"])
+    if not arch.tied:
+        assert torch.equal(ck.lm_head().to(torch.bfloat16), state["lm_head.weight"])
+    for i in range(2):
+        p = ck.block(i)
+        for path, w in p.linears.items():
+            assert torch.equal(w, state[f"model.layers.{i}.{path}.weight"]), path
+        for path, b in p.biases.items():
+            assert torch.equal(b.to(torch.bfloat16), state[f"model.layers.{i}.{path}.bias"]), path
+        assert torch.equal(p.input_norm.to(torch.bfloat16),
+                           state[f"model.layers.{i}.input_layernorm.weight"])
