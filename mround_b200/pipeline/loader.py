@@ -92,6 +92,16 @@ class CheckpointModel:
         if config.get("rope_scaling"):
             raise ArchitectureError(f"rope_scaling {config['rope_scaling']} is not implemented "
                                     "by the device block")
+        # transformers >= 5 writes the rotary settings as ``rope_parameters``
+        # ({"rope_type", "rope_theta", ...}) instead of top-level keys
+        rope = config.get("rope_parameters") or {}
+        if rope.get("rope_type", "default") != "default":
+            raise ArchitectureError(f"rope_parameters {rope} (rope_type "
+                                    f"{rope.get('rope_type')!r}) is not implemented by the "
+                                    "device block")
+        theta = config.get("rope_theta")
+        if theta is None:
+            theta = rope.get("rope_theta", 10000.0)
         self._config = config
         heads = int(config["num_attention_heads"])
         hidden = int(config["hidden_size"])
@@ -102,7 +112,7 @@ class CheckpointModel:
             head_dim=int(config.get("head_dim") or hidden // heads),
             intermediate=int(config["intermediate_size"]), vocab=int(config["vocab_size"]),
             rms_eps=float(config.get("rms_norm_eps", 1e-6)),
-            rope_theta=float(config.get("rope_theta", 10000.0)),
+            rope_theta=float(theta),
             qkv_bias=family == "qwen2" or bool(config.get("attention_bias", False)),
             tied=bool(config.get("tie_word_embeddings", False)))
         self._files: dict[str, _SafetensorsFile] = {}

@@ -86,11 +86,24 @@ def test_load_model_routes_directories(tmp_path):
     (lambda c: c.update(quantization={"bits": 4, "group_size": 64}), "already quantized"),
     (lambda c: c.update(model_type="gemma"), "not supported"),
     (lambda c: c.update(rope_scaling={"type": "llama3", "factor": 8.0}), "rope_scaling"),
+    (lambda c: (c.pop("rope_theta", None),
+                c.update(rope_parameters={"rope_type": "yarn", "rope_theta": 1e6,
+                                          "factor": 4.0})), "rope_type"),
 ])
 def test_refusals(tmp_path, edit, msg):
     write_checkpoint(tmp_path, edit_config=edit)
     with pytest.raises(ArchitectureError, match=msg):
         CheckpointModel(tmp_path)
+
+
+def test_rope_theta_from_rope_parameters(tmp_path):
+    """transformers >= 5 configs carry the theta under ``rope_parameters``."""
+    def edit(c):
+        c.pop("rope_theta", None)
+        c["rope_parameters"] = {"rope_type": "default", "rope_theta": 123456.0}
+
+    write_checkpoint(tmp_path, edit_config=edit)
+    assert CheckpointModel(tmp_path).arch.rope_theta == 123456.0
 
 
 def test_non_bf16_linears_refused(tmp_path):
