@@ -92,6 +92,10 @@ class CheckpointModel:
         if config.get("rope_scaling"):
             raise ArchitectureError(f"rope_scaling {config['rope_scaling']} is not implemented "
                                     "by the device block")
+        if config.get("use_sliding_window"):
+            raise ArchitectureError(f"use_sliding_window with sliding_window="
+                                    f"{config.get('sliding_window')} is not implemented by the "
+                                    "device block (its attention is fully causal)")
         # transformers >= 5 writes the rotary settings as ``rope_parameters``
         # ({"rope_type", "rope_theta", ...}) instead of top-level keys
         rope = config.get("rope_parameters") or {}

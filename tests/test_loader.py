@@ -89,6 +89,7 @@ def test_load_model_routes_directories(tmp_path):
     (lambda c: (c.pop("rope_theta", None),
                 c.update(rope_parameters={"rope_type": "yarn", "rope_theta": 1e6,
                                           "factor": 4.0})), "rope_type"),
+    (lambda c: c.update(use_sliding_window=True, sliding_window=1024), "sliding_window"),
 ])
 def test_refusals(tmp_path, edit, msg):
     write_checkpoint(tmp_path, edit_config=edit)
