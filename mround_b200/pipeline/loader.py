@@ -96,6 +96,15 @@ class CheckpointModel:
             raise ArchitectureError(f"use_sliding_window with sliding_window="
                                     f"{config.get('sliding_window')} is not implemented by the "
                                     "device block (its attention is fully causal)")
+        # The device block applies biases to q/k/v only (Qwen2).  Llama's
+        # attention_bias also gives o_proj a bias, and mlp_bias gives the three
+        # MLP projections one: dropping them would tune a different function.
+        if family == "llama" and config.get("attention_bias"):
+            raise ArchitectureError("attention_bias=true gives the llama o_proj a bias, which the "
+                                    "device block does not apply")
+        if config.get("mlp_bias"):
+            raise ArchitectureError("mlp_bias=true (biases on gate/up/down_proj) is not "
+                                    "implemented by the device block")
         # transformers >= 5 writes the rotary settings as ``rope_parameters``
         # ({"rope_type", "rope_theta", ...}) instead of top-level keys
         rope = config.get("rope_parameters") or {}
@@ -117,7 +126,7 @@ class CheckpointModel:
             intermediate=int(config["intermediate_size"]), vocab=int(config["vocab_size"]),
             rms_eps=float(config.get("rms_norm_eps", 1e-6)),
             rope_theta=float(theta),
-            qkv_bias=family == "qwen2" or bool(config.get("attention_bias", False)),
+            qkv_bias=family == "qwen2",
             tied=bool(config.get("tie_word_embeddings", False)))
         self._files: dict[str, _SafetensorsFile] = {}
         self._where: dict[str, str] = {}
@@ -182,6 +191,13 @@ class CheckpointModel:
         if self.arch.qkv_bias and len(biases) != 3:
             raise ArchitectureError(f"{prefix}: the architecture has q/k/v biases but the "
                                     "checkpoint does not")
+        if not self.arch.qkv_bias and biases:
+            raise ArchitectureError(f"{prefix}: the checkpoint carries q/k/v biases the "
+                                    f"{self.arch.family} configuration does not declare")
+        for path in ("self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
+            if self.has(f"{prefix}.{path}.bias"):
+                raise ArchitectureError(f"{prefix}.{path}.bias: the device block applies no bias "
+                                        "to this projection")
         return BlockParams(index, linears, biases,
                            self.tensor(f"{prefix}.input_layernorm.weight"),
                            self.tensor(f"{prefix}.post_attention_layernorm.weight"))

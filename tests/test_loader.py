@@ -19,7 +19,7 @@ from mround_b200.pipeline.model import SyntheticModel
 
 
 def write_checkpoint(tmp, arch_name="tiny-qwen2", seed=3, *, shards=2, edit_config=None,
-                     linear_dtype=torch.bfloat16):
+                     linear_dtype=torch.bfloat16, extra=None):
     model = SyntheticModel(get_arch(arch_name), seed=seed)
     tensors = {"model.embed_tokens.weight": model.embed_tokens()}
     for i in range(model.arch.layers):
@@ -34,6 +34,7 @@ def write_checkpoint(tmp, arch_name="tiny-qwen2", seed=3, *, shards=2, edit_conf
     tensors["model.norm.weight"] = model.final_norm()
     if not model.arch.tied:
         tensors["lm_head.weight"] = model.lm_head()
+    tensors.update(extra or {})
     names = list(tensors)
     weight_map = {}
     for s in range(shards):
@@ -90,11 +91,31 @@ def test_load_model_routes_directories(tmp_path):
                 c.update(rope_parameters={"rope_type": "yarn", "rope_theta": 1e6,
                                           "factor": 4.0})), "rope_type"),
     (lambda c: c.update(use_sliding_window=True, sliding_window=1024), "sliding_window"),
+    (lambda c: c.update(mlp_bias=True), "mlp_bias"),
 ])
 def test_refusals(tmp_path, edit, msg):
     write_checkpoint(tmp_path, edit_config=edit)
     with pytest.raises(ArchitectureError, match=msg):
         CheckpointModel(tmp_path)
+
+
+def test_llama_attention_bias_refused(tmp_path):
+    """Llama's attention_bias puts a bias on o_proj too, which the block would drop."""
+    write_checkpoint(tmp_path, "tiny-llama", edit_config=lambda c: c.update(attention_bias=True))
+    with pytest.raises(ArchitectureError, match="o_proj"):
+        CheckpointModel(tmp_path)
+
+
+@pytest.mark.parametrize("path", ["self_attn.o_proj", "mlp.down_proj"])
+def test_unapplied_bias_tensors_refused(tmp_path, path):
+    """A bias tensor the block does not apply is refused even when the
+    configuration does not declare it."""
+    rows = get_arch("tiny-llama").linear_shapes()[path][0]
+    write_checkpoint(tmp_path, "tiny-llama",
+                     extra={f"model.layers.0.{path}.bias": torch.zeros(rows, dtype=torch.bfloat16)})
+    ck = CheckpointModel(tmp_path)
+    with pytest.raises(ArchitectureError, match="bias"):
+        ck.block(0)
 
 
 def test_rope_theta_from_rope_parameters(tmp_path):
