@@ -260,67 +260,45 @@ class HostStreams:
 
 
 # ----------------------------------------------------------------- cpu
-def cpu_sample(args, model, arch, budget_s: float = 25.0):
-    """The oracle's CPU step on a bounded sample, extrapolated to blocks/s.
+def cpu_run(args, model, arch, *, max_steps: int, budget_s: float, warmup: int = 0):
+    """The oracle's ``_tune`` restatement timed at full size on this host's cores.
 
-    The batch is 8 sequences of 2048 tokens.  Timed: the token-independent
-    work alone (fake-quant of every weight and its backward; best of two after
-    a warm-up run) and one full step on ONE 2048-token sequence (fake-quant,
-    block forward, loss, backward).  The batch's step is the token-independent
-    part plus 8 times the rest -- exact for the per-sequence work, attention
-    included -- and the forward pass is 8 times a one-sequence forward."""
-    from oracle.block_tuner import LINEARS, OracleBlock, fake_quant_ste, loss_fn
+    Two calibration batches of 8 x 2048 Zipf tokens (the GPU arm's first two),
+    their targets from the dense block (the first of these forwards also warms
+    the thread pool and the allocator), then ``oracle.block_tuner.tune_block``
+    as the reference's loop runs it: one scoring pass (a forward and loss per
+    batch, timed) and full-batch steps -- fake-quant of every weight, block
+    forward, outlier-suppressed loss, backward, signSGD update -- until
+    ``max_steps`` steps or ``budget_s`` seconds of steps (at least one), after
+    ``warmup`` untimed steps.
+    Nothing is extrapolated from a smaller batch: the block time is 200 timed
+    step means plus 64 timed forward means."""
+    from mround_b200.pipeline.model import zipf_tokens
+    from oracle.block_tuner import LINEARS, OracleBlock, tune_block
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     ob = OracleBlock(arch, model.block(0), {p: args.bits for p in LINEARS}, args.group)
-    params = ob.init_params()
-    g = torch.Generator().manual_seed(0)
-
-    def fixed_part() -> float:
-        leaves = {q: tuple(t.clone().requires_grad_(True) for t in params[q]) for q in params}
-        t1 = time.perf_counter()
-        s = 0
-        for q in LINEARS:
-            w = fake_quant_ste(ob.w[q], *leaves[q], args.bits, args.group)
-            s = s + (w * w).sum()
-        s.backward()
-        return time.perf_counter() - t1
-
-    def one_step(tok: int) -> float:
-        x = torch.randn(1, tok, arch.hidden, generator=g) * 0.02
-        with torch.no_grad():
-            tgt = ob.forward(x) + 1e-3
-        leaves = {q: tuple(t.clone().requires_grad_(True) for t in params[q]) for q in params}
-        t1 = time.perf_counter()
-        loss, _ = loss_fn(ob.forward(x, leaves), tgt, True)
-        loss.backward()
-        return time.perf_counter() - t1
-
-    t0 = time.perf_counter()
-    fixed_part()  # warm-up: thread pool, first-touch allocations
-    t_fixed = min(fixed_part(), fixed_part())
-    seq_times = [one_step(SEQ)]
-    if time.perf_counter() - t0 < budget_s:
-        seq_times.append(one_step(SEQ))
-    t_seq = min(seq_times)
-    per_seq = t_seq - t_fixed if t_seq > t_fixed else t_seq
-    t_step = t_fixed + BATCH * per_seq
-    x = torch.randn(1, SEQ, arch.hidden, generator=g) * 0.02
+    tokens = zipf_tokens(arch.vocab, 2 * BATCH, SEQ, seed=42)
+    embed = model.embed_tokens()
+    inputs = [embed[torch.as_tensor(tokens[i * BATCH:(i + 1) * BATCH], dtype=torch.long)].float()
+              for i in range(2)]
     with torch.no_grad():
-        t1 = time.perf_counter()
-        ob.forward(x, None)
-        t_fwd = BATCH * (time.perf_counter() - t1)
+        targets = [ob.forward(x) for x in inputs]
+    res = tune_block(ob, inputs, targets, iters=ITERS, lr0=1.0 / ITERS, suppress=args.bits < 4,
+                     max_steps=max_steps, step_budget_s=budget_s, warmup_steps=warmup)
+    steps = res["steps_run"]
+    t_step = res["step_seconds"] / steps
+    t_fwd = res["score_seconds"] / len(inputs)
     blk = ITERS * t_step + PASSES_PER_BATCH * N_BATCHES * t_fwd
     return {
         "value": 1.0 / blk, "unit": UNIT, "cores": threads, "kind": "port",
-        "sample": (f"torch-CPU float32 restatement (oracle/block_tuner.py), not the reference's MLX "
-                   f"code: one step of one {args.arch} block on one {SEQ}-token sequence (best of "
-                   f"{len(seq_times)}: {t_seq:.2f} s) and its token-independent fake-quant fwd+bwd "
-                   f"alone ({t_fixed:.2f} s); step = fixed + {BATCH} x the rest, x{ITERS} steps "
-                   f"+ {PASSES_PER_BATCH * N_BATCHES} forward passes of {BATCH} x a one-sequence "
-                   f"forward"),
-        "t_step_s": t_step,
+        "sample": (f"torch-CPU float32 restatement of the reference's loop (oracle/block_tuner.py; "
+                   f"the reference's MLX code cannot run without MLX): {steps} full step(s) of one "
+                   f"{args.arch} block on a {BATCH}x{SEQ} batch ({t_step:.2f} s each) and a timed "
+                   f"scoring pass over 2 batches ({t_fwd:.2f} s per forward); block time = "
+                   f"{ITERS} x step + {PASSES_PER_BATCH * N_BATCHES} x forward"),
+        "t_step_s": t_step, "t_forward_s": t_fwd, "steps_timed": steps, "warmup_steps": warmup,
     }
 
 
@@ -454,7 +432,7 @@ def main():
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         try:
-            out["cpu_baseline"] = cpu_sample(args, model, arch)
+            out["cpu_baseline"] = cpu_run(args, model, arch, max_steps=1, budget_s=0.0)
         except Exception as exc:  # noqa: BLE001 - the baseline is reported, not required
             out["cpu_baseline"] = {"value": None, "error": str(exc)}
     if dist.rank == 0:
@@ -468,7 +446,10 @@ def main():
 
 def reference_arm(args, out_stream):
     """The reference path's CPU implementation (the oracle restatement; the
-    reference's MLX loop cannot run here), timed on this host's cores."""
+    reference's MLX loop cannot run here), timed on this host's cores: full
+    8 x 2048 steps after one untimed warm-up step (``--warmup 0`` skips it),
+    at most ``--steps`` of them and as many as fit in two minutes (at least
+    one); ``steps`` and ``warmup`` in the line are the numbers run."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -477,13 +458,15 @@ def reference_arm(args, out_stream):
 
     arch = get_arch(args.arch)
     model = SyntheticModel(arch, seed=0)
-    res = cpu_sample(args, model, arch, budget_s=20.0)
+    res = cpu_run(args, model, arch, max_steps=max(1, args.steps), budget_s=120.0,
+                  warmup=min(1, args.warmup))
     cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": res["t_step_s"] * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": res["steps_timed"],
+        "warmup": res["warmup_steps"], "ms_per_step": res["t_step_s"] * 1e3, "ms_forward_batch": res["t_forward_s"] * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (random-init N(0,0.02) weights, Zipf(1.1) tokens)",
         "config": {"workload": f"{args.arch} block SignRound step, W{args.bits} asym g{args.group}, "
                                f"global batch {BATCH}x{SEQ}, {ITERS} it/block, {N_BATCHES} batches",
                    "global_batch": BATCH, "seq_len": SEQ, "parallelism": "cpu"},

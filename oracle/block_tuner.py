@@ -192,12 +192,17 @@ def loss_fn(pred, target, suppress: bool, fraction: float = 0.001):
 
 def tune_block(block: OracleBlock, inputs, targets, *, iters: int, lr0: float, suppress: bool,
                lo: float = 0.1, hi: float = 1.0, record_grads_at: int | None = None,
-               step_budget_s: float | None = None):
+               step_budget_s: float | None = None, max_steps: int | None = None,
+               warmup_steps: int = 0):
     """Restated ``_tune``; returns a dict with losses, params and timing.
 
     ``record_grads_at`` stores the loss and parameter gradients of that step
     (for parity tests).  ``step_budget_s`` stops early after that many seconds
-    of steps (a bounded timing sample); the result then says how many ran.
+    of timed steps, ``max_steps`` after that many timed steps (a bounded
+    timing sample); the first ``warmup_steps`` steps run untimed.  The result
+    says how many steps were timed (``steps_run``) and their seconds;
+    ``score_seconds`` is the time of the first scoring pass (one forward and
+    loss per batch).
     """
     params = block.init_params()
     nb = len(inputs)
@@ -208,10 +213,13 @@ def tune_block(block: OracleBlock, inputs, targets, *, iters: int, lr0: float, s
                     for i in range(nb)]
         return sum(vals) / nb, vals
 
+    t_score = time.perf_counter()
     initial, _ = mean_loss(params)
+    score_seconds = time.perf_counter() - t_score
     step_losses, recorded = [], None
     t0 = time.perf_counter()
     ran = 0
+
     def grad_of(t):
         # a parameter that does not reach the loss (alpha under a searched
         # scale) has no gradient: sign(0) = 0 leaves it in place
@@ -234,12 +242,18 @@ def tune_block(block: OracleBlock, inputs, targets, *, iters: int, lr0: float, s
             nb_ = torch.clamp(b.detach() - lr32 * torch.sign(grad_of(b)), lo, hi)
             new[p] = (nv, na, nb_)
         params = new
+        if step < warmup_steps:
+            t0 = time.perf_counter()
+            continue
         ran += 1
         if step_budget_s is not None and time.perf_counter() - t0 > step_budget_s:
             break
+        if max_steps is not None and ran >= max_steps:
+            break
     step_seconds = time.perf_counter() - t0
-    final, _ = mean_loss(params) if ran == iters else (float("nan"), None)
-    reverted = ran == iters and final >= initial
+    finished = ran + min(warmup_steps, iters) == iters
+    final, _ = mean_loss(params) if finished else (float("nan"), None)
+    reverted = finished and final >= initial
     return {
         "initial_loss": initial,
         "final_loss": initial if reverted else final,
@@ -249,4 +263,5 @@ def tune_block(block: OracleBlock, inputs, targets, *, iters: int, lr0: float, s
         "recorded": recorded,
         "steps_run": ran,
         "step_seconds": step_seconds,
+        "score_seconds": score_seconds,
     }
