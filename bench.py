@@ -406,7 +406,10 @@ def main():
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "fp32 via bf16x3 split tcgen05 GEMMs (float32 accumulate)",
+        "dtype": ("fp32 semantics on tcgen05 (float32 accumulate): forward GEMMs as the "
+                  "three-product bf16 split, backward GEMMs as one tf32 product"
+                  if tuner.precision.grad_weight == 4 else
+                  "fp32 via bf16x3 split tcgen05 GEMMs (float32 accumulate)"),
         "data": "synthetic (random-init N(0,0.02) weights, Zipf(1.1) tokens)",
         "config": {"workload": f"{args.arch} block SignRound step, W{args.bits} asym g{args.group}, "
                                f"global batch {BATCH}x{SEQ}, {ITERS} it/block, {N_BATCHES} batches",

@@ -83,14 +83,15 @@ const char* mr_last_cuda_error(void);
  *   symmetric:  q = clamp(rint(w/scale + v), -2^(bits-1), 2^(bits-1)-1); wq = scale * q
  * Outputs (any may be NULL): wq_hi = bf16(wq), wq_lo = bf16(wq - wq_hi) (the
  * split that lets two bf16 GEMM operands carry a float32 weight), wq_f32,
- * scale and zp per group (float32, (rows, cols/group); zp is 0 under the
- * symmetric schemes).
+ * wq_t32 = wq rounded to tf32 (the operand of mr_gemm_tf32), scale and zp per
+ * group (float32, (rows, cols/group); zp is 0 under the symmetric schemes).
  * IEEE division and ties-to-even rounding: codes are bit-exact.
  */
 int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
                   const float* beta, int64_t rows, int64_t cols, int group, int bits,
                   int symmetric, const float* init_scale, float eps, uint16_t* wq_hi,
-                  uint16_t* wq_lo, float* wq_f32, float* scale, float* zp, void* stream);
+                  uint16_t* wq_lo, float* wq_f32, float* wq_t32, float* scale, float* zp,
+                  void* stream);
 
 /*
  * K2 -- straight-through backward fused with signSGD and projection.
@@ -105,13 +106,14 @@ int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
  * alpha receives none.
  * Optional outputs (NULL to skip): the gradients gv (rows, cols), galpha and
  * gbeta (rows, cols/group); and, when update != 0, the NEXT step's operands
- * wq_hi/wq_lo recomputed from the updated parameters (fusing K1).
+ * wq_hi/wq_lo/wq_t32 recomputed from the updated parameters (fusing K1).
  */
 int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
                    float* beta, int64_t rows, int64_t cols, int group, int bits,
                    int symmetric, const float* init_scale, float eps, float lr,
                    float coef_lo, float coef_hi, int update, float* gv, float* galpha,
-                   float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, void* stream);
+                   float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_t32,
+                   void* stream);
 
 /*
  * K5 -- commit and MLX packing in one pass.
@@ -146,7 +148,8 @@ int mr_pack_mlx(const uint16_t* w_bf16, const float* v, const float* alpha,
  * batch's count).  thr_in >= 0 skips the selection and uses that threshold
  * (micro-batch pieces); otherwise the selected threshold is written to
  * *thr_out (device float, may be NULL).  `workspace` must hold
- * mr_loss_workspace_bytes() bytes.
+ * mr_loss_workspace_bytes() bytes.  n of 2^32 elements or more is refused
+ * with MR_ERR_ARGUMENT (the selection's histogram counters are 32-bit).
  */
 size_t mr_loss_workspace_bytes(void);
 int mr_loss_outlier(const float* pred, const float* target, int64_t n, int64_t k,
@@ -167,8 +170,10 @@ int mr_loss_outlier(const float* pred, const float* target, int64_t n, int64_t k
  * each device looks up the array's device address (cudaGetSymbolAddress);
  * make that first call before any stream capture.  All calls share the one
  * array: calls that overlap on the GPU (two streams, or two host threads on
- * one device) race and must be serialized by the caller.  Nothing is
- * allocated or freed.
+ * one device) race and must be serialized by the caller.  The stream must
+ * belong to the current device (the array's address is the current
+ * device's); a stream of another device is refused with MR_ERR_DEVICE.
+ * Nothing is allocated or freed.
  */
 size_t mr_loss_noalloc_scratch_bytes(void);
 int mr_loss_outlier_noalloc(const float* pred, const float* target, int64_t n, int64_t k,
@@ -183,7 +188,8 @@ int mr_loss_outlier_noalloc(const float* pred, const float* target, int64_t n, i
  * mr_loss_select_digit, which narrows the device-side selection state.
  * `state` is the workspace of mr_loss_workspace_bytes() (its selection
  * state comes first).
- * mr_loss_outlier uses the same passes with no exchange.
+ * mr_loss_outlier uses the same passes with no exchange.  n of 2^32 elements
+ * or more is refused with MR_ERR_ARGUMENT.
  */
 int mr_loss_hist_pass(const float* pred, const float* target, int64_t n, int pass,
                       const void* state, uint32_t* hist, void* stream);
@@ -259,10 +265,20 @@ int mr_selftest_division(const float* a, const float* b, int64_t n, unsigned int
 int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* stream);
 
 /*
+ * Operand preparation for the tf32 GEMM: out = x rounded to tf32 (round to
+ * nearest, ties away from zero; the low 13 bits cleared), n elements of
+ * float32; out may equal x.
+ */
+int mr_round_tf32(const float* x, int64_t n, float* out, void* stream);
+
+/*
  * Fused element-wise operators of the decoder block (the mlx-lm layer the
  * reference runs inside block_output, mround/pipeline/blocks.py:578-606).
  * Each reads float32 activations and writes the next GEMM operand directly as
- * a bf16 hi/lo pair.  Token t = b*S + s; attention operands are (B, H, S, D).
+ * a bf16 hi/lo pair, and, where a `t32` pointer is given, as float32 rounded
+ * to tf32 (the operand of mr_gemm_tf32).  In the backward kernels hi/lo may be
+ * NULL (together) when only t32 is wanted.  Token t = b*S + s; attention
+ * operands are (B, H, S, D).
  *   mr_rmsnorm_split:     y = x * rsqrt(mean(x^2) + eps) * w; rstd per row
  *   mr_rmsnorm_bwd_split: dx = resid + rstd * (g - xhat * mean(g * xhat)), g = dy * w;
  *                         resid may be NULL; written as hi/lo and/or float32 (out)
@@ -280,21 +296,22 @@ int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* s
  *   written -- the causal modes of mr_gemm_batched never read them.
  */
 int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows, int h, float eps,
-                     uint16_t* hi, uint16_t* lo, float* rstd, void* stream);
+                     uint16_t* hi, uint16_t* lo, float* t32, float* rstd, void* stream);
 int mr_rmsnorm_bwd_split(const float* dy, const float* x, const uint16_t* w, const float* rstd,
                          const float* resid, int64_t rows, int h, uint16_t* hi, uint16_t* lo,
-                         float* out, void* stream);
+                         float* t32, float* out, void* stream);
 int mr_rope_split(const float* qkv, const float* cosv, const float* sinv, int b, int s, int hq,
                   int hkv, int d, uint16_t* q_hi, uint16_t* q_lo, uint16_t* k_hi, uint16_t* k_lo,
                   uint16_t* v_hi, uint16_t* v_lo, void* stream);
 int mr_rope_bwd_split(const float* dq, const float* dk, const float* dv, const float* cosv,
                       const float* sinv, int b, int s, int hq, int hkv, int d, uint16_t* hi,
-                      uint16_t* lo, void* stream);
+                      uint16_t* lo, float* t32, void* stream);
 int mr_heads_split(const float* src, int b, int s, int h, int d, int merge, uint16_t* hi,
-                   uint16_t* lo, void* stream);
-int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo, void* stream);
+                   uint16_t* lo, float* t32, void* stream);
+int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo, float* t32,
+                    void* stream);
 int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t, int i, uint16_t* hi,
-                        uint16_t* lo, void* stream);
+                        uint16_t* lo, float* t32, void* stream);
 int mr_softmax_causal_split(const float* scores, int64_t rows, int s, float scale, int band,
                             uint16_t* hi, uint16_t* lo, void* stream);
 int mr_softmax_bwd_split(const float* dp, const uint16_t* p_hi, const uint16_t* p_lo,
@@ -367,6 +384,30 @@ int mr_gemm_rs(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_km
                int64_t n, int64_t k, int precision, float* const* dst, int64_t ldd,
                int64_t rows_per_rank, unsigned long long* const* flags, int world,
                unsigned int* done, unsigned long long epoch, void* stream);
+
+/*
+ * K3 with one tf32 product: float32 operands, float32 accumulate in tensor
+ * memory.  The backward products of the decoder-block linears
+ * (mround/pipeline/runner.py:920, the input and weight gradients MLX autodiff
+ * forms for y = x @ Wq.T at runner.py:367): same contraction, majorness,
+ * bias and accumulate semantics as mr_gemm, through tcgen05.mma kind::tf32.
+ * The tensor core reads the upper 19 bits of each float32 (10 explicit
+ * mantissa bits): operands must already be rounded to tf32 (round to nearest,
+ * as mr_round_tf32 and the *_split kernels' t32 outputs do) for the product
+ * to use exactly those values.  A tf32 product takes the tensor time of two
+ * bf16 products and keeps 11 significant bits per operand.  Leading
+ * dimensions multiples of 4 elements; pointers 16-byte aligned.
+ */
+int mr_gemm_tf32(const float* a, int64_t lda, int a_kmajor, const float* b, int64_t ldb,
+                 int b_kmajor, float* c, int64_t ldc, const float* bias, int accumulate,
+                 int64_t m, int64_t n, int64_t k, void* stream);
+
+/* mr_gemm_rs with tf32 operands (the fused weight-gradient GEMM ->
+ * reduce-scatter of the data-parallel step, one tf32 product). */
+int mr_gemm_rs_tf32(const float* a, int64_t lda, int a_kmajor, const float* b, int64_t ldb,
+                    int b_kmajor, int64_t m, int64_t n, int64_t k, float* const* dst,
+                    int64_t ldd, int64_t rows_per_rank, unsigned long long* const* flags,
+                    int world, unsigned int* done, unsigned long long epoch, void* stream);
 
 /*
  * Peer memory of the exchange.  mr_ipc_export writes the CUDA IPC handle

@@ -42,9 +42,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_device_check": (_I, []),
     "mr_last_cuda_error": (ctypes.c_char_p, []),
     "mr_fq_forward": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _P, _P, _P, _P, _P,
-                           _P]),
+                           _P, _P]),
     "mr_ste_signsgd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _F, _F, _F, _I,
-                            _P, _P, _P, _P, _P, _P]),
+                            _P, _P, _P, _P, _P, _P, _P]),
     "mr_pack_mlx": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _P, _P, _P, _P, _P]),
     "mr_loss_workspace_bytes": (ctypes.c_size_t, []),
     "mr_loss_outlier": (_I, [_P, _P, _I64, _I64, _I, _D, _F, _P, _P, _P, _P, _P]),
@@ -65,6 +65,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_gemm_status": (_I, [_I]),
     "mr_gemm_rs": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I64, _I64, _I64, _I, _P, _I64, _I64,
                         _P, _I, _P, ctypes.c_uint64, _P]),
+    "mr_gemm_tf32": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _P, _I, _I64, _I64, _I64, _P]),
+    "mr_gemm_rs_tf32": (_I, [_P, _I64, _I, _P, _I64, _I, _I64, _I64, _I64, _P, _I64, _I64, _P,
+                             _I, _P, ctypes.c_uint64, _P]),
     "mr_ipc_handle_bytes": (ctypes.c_size_t, []),
     "mr_ipc_export": (_I, [_P, _P, _P]),
     "mr_ipc_import": (_I, [_P, _I64, _P, _P]),
@@ -72,13 +75,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_reduce_slots": (_I, [_P, _I64, _I64, _I, _P, ctypes.c_uint64, _P, _P]),
     "mr_peer_send": (_I, [_P, _P, _I64, _P, ctypes.c_uint64, _P]),
     "mr_peer_status": (_I, [_I]),
-    "mr_rmsnorm_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P, _P]),
-    "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P, _P]),
+    "mr_rmsnorm_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P, _P, _P]),
+    "mr_rmsnorm_bwd_split": (_I, [_P, _P, _P, _P, _P, _I64, _I, _P, _P, _P, _P, _P]),
     "mr_rope_split": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
-    "mr_rope_bwd_split": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
-    "mr_heads_split": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
-    "mr_swiglu_split": (_I, [_P, _I64, _I, _P, _P, _P]),
-    "mr_swiglu_bwd_split": (_I, [_P, _P, _I64, _I, _P, _P, _P]),
+    "mr_rope_bwd_split": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "mr_heads_split": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "mr_swiglu_split": (_I, [_P, _I64, _I, _P, _P, _P, _P]),
+    "mr_swiglu_bwd_split": (_I, [_P, _P, _I64, _I, _P, _P, _P, _P]),
+    "mr_round_tf32": (_I, [_P, _I64, _P, _P]),
     "mr_softmax_causal_split": (_I, [_P, _I64, _I, _F, _I, _P, _P, _P]),
     "mr_softmax_bwd_split": (_I, [_P, _P, _P, _I64, _I, _F, _I, _P, _P, _P]),
 }

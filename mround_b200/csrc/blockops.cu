@@ -36,6 +36,22 @@ __device__ __forceinline__ void put_split4(uint16_t* hi, uint16_t* lo, int64_t i
                                                  uint32_t(l[2]) | (uint32_t(l[3]) << 16));
 }
 
+// Operand outputs of one element-wise kernel: the bf16 hi/lo pair (when hi is
+// given) and/or the tf32-rounded float32 copy (when t32 is given).
+__device__ __forceinline__ void put_out(uint16_t* hi, uint16_t* lo, float* t32, int64_t i,
+                                        float v) {
+  if (hi) put_split(hi, lo, i, v);
+  if (t32) t32[i] = tf32_rna(v);
+}
+
+__device__ __forceinline__ void put_out4(uint16_t* hi, uint16_t* lo, float* t32, int64_t i,
+                                         float4 v) {
+  if (hi) put_split4(hi, lo, i, v);
+  if (t32)
+    *reinterpret_cast<float4*>(t32 + i) =
+        make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+}
+
 template <int THREADS>
 __device__ __forceinline__ float block_sum(float v, float* sh) {
 #pragma unroll
@@ -70,7 +86,8 @@ constexpr int kMaxVec = 16;  // float4 per thread: rows up to 8192
 // y = x * rsqrt(mean(x^2) + eps) * w  -> hi/lo, and rstd per row.
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_split_kernel(
     const float* __restrict__ x, const uint16_t* __restrict__ w, int h, float eps,
-    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ rstd) {
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ t32,
+    float* __restrict__ rstd) {
   __shared__ float sh[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * h);
@@ -98,18 +115,20 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_split_kernel(
       y.y = __fmul_rn(__fmul_rn(v[i].y, r), bf16_to_f32(w[e + 1]));
       y.z = __fmul_rn(__fmul_rn(v[i].z, r), bf16_to_f32(w[e + 2]));
       y.w = __fmul_rn(__fmul_rn(v[i].w, r), bf16_to_f32(w[e + 3]));
-      put_split4(hi, lo, row * h + e, y);
+      put_out4(hi, lo, t32, row * h + e, y);
     }
   }
 }
 
 // dx = resid + rstd * (g - xhat * mean(g * xhat)),  g = dy * w,  xhat = x * rstd.
-// Written as hi/lo (when hi is given) and/or float32 (when out is given);
-// resid may be NULL (no residual term).
+// Written as hi/lo (when hi is given), tf32-rounded float32 (when t32 is
+// given) and/or float32 (when out is given); resid may be NULL (no residual
+// term).
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_split_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const uint16_t* __restrict__ w,
     const float* __restrict__ rstd, const float* __restrict__ resid, int h,
-    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ out) {
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ t32,
+    float* __restrict__ out) {
   __shared__ float sh[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const float r = rstd[row];
@@ -142,7 +161,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_split_kernel(
       d.y = q.y + r * (g[i].y - xh[i].y * dot);
       d.z = q.z + r * (g[i].z - xh[i].z * dot);
       d.w = q.w + r * (g[i].w - xh[i].w * dot);
-      if (hi) put_split4(hi, lo, row * h + c * 4, d);
+      put_out4(hi, lo, t32, row * h + c * 4, d);
       if (out) reinterpret_cast<float4*>(out + row * h)[c] = d;
     }
   }
@@ -193,7 +212,8 @@ __global__ void rope_split_kernel(const float* __restrict__ qkv, const float* __
 __global__ void rope_bwd_split_kernel(const float* __restrict__ dq, const float* __restrict__ dk,
                                       const float* __restrict__ dv, const float* __restrict__ cosv,
                                       const float* __restrict__ sinv, int B, int S, int Hq, int Hkv,
-                                      int D, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+                                      int D, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                                      float* __restrict__ t32) {
   const int half = D / 2;
   const int H = Hq + 2 * Hkv;
   const int64_t total = int64_t(B) * S * H * half;
@@ -216,14 +236,15 @@ __global__ void rope_bwd_split_kernel(const float* __restrict__ dq, const float*
       g2 = d2 * c - d1 * sn;
     }
     const int64_t o = t * int64_t(H) * D + int64_t(head) * D;
-    put_split(hi, lo, o + j, g1);
-    put_split(hi, lo, o + j + half, g2);
+    put_out(hi, lo, t32, o + j, g1);
+    put_out(hi, lo, t32, o + j + half, g2);
   }
 }
 
 // (B,H,S,D) float32 <-> (T, H*D): merge=1 reads heads and writes token rows.
 __global__ void heads_kernel(const float* __restrict__ src, int B, int S, int H, int D, int merge,
-                             uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+                             uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                             float* __restrict__ t32) {
   const int64_t total4 = int64_t(B) * S * H * D / 4;
   for (int64_t i4 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
        i4 += int64_t(gridDim.x) * blockDim.x) {
@@ -243,7 +264,7 @@ __global__ void heads_kernel(const float* __restrict__ src, int B, int S, int H,
       const int b = int(e / (int64_t(D) * S * H));
       s_idx = ((int64_t(b) * S + s) * H + h) * D + d;
     }
-    put_split4(hi, lo, e, *reinterpret_cast<const float4*>(src + s_idx));
+    put_out4(hi, lo, t32, e, *reinterpret_cast<const float4*>(src + s_idx));
   }
 }
 
@@ -313,7 +334,7 @@ __global__ void __launch_bounds__(256) rope_row_kernel(
 __global__ void __launch_bounds__(256) rope_bwd_row_kernel(
     const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv,
     const float* __restrict__ cosv, const float* __restrict__ sinv, int B, int S, int Hq, int Hkv,
-    int D, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+    int D, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo, float* __restrict__ t32) {
   const int half = D / 2, per_head = half / 4;
   const int H = Hq + 2 * Hkv;
   const int units = H * per_head;
@@ -337,8 +358,8 @@ __global__ void __launch_bounds__(256) rope_bwd_row_kernel(
                          d2.z * c.z - d1.z * sn.z, d2.w * c.w - d1.w * sn.w);
       }
       const int64_t o = t * int64_t(H) * D + int64_t(head) * D;
-      put_split4(hi, lo, o + j, g1);
-      put_split4(hi, lo, o + half + j, g2);
+      put_out4(hi, lo, t32, o + j, g1);
+      put_out4(hi, lo, t32, o + half + j, g2);
     }
   }
 }
@@ -347,7 +368,8 @@ __global__ void __launch_bounds__(256) rope_bwd_row_kernel(
 __global__ void __launch_bounds__(256) heads_row_kernel(const float* __restrict__ src, int B, int S,
                                                         int H, int D, int merge,
                                                         uint16_t* __restrict__ hi,
-                                                        uint16_t* __restrict__ lo) {
+                                                        uint16_t* __restrict__ lo,
+                                                        float* __restrict__ t32) {
   const int per_head = D / 4;
   const int units = H * per_head;
   const int64_t T = int64_t(B) * S;
@@ -359,18 +381,20 @@ __global__ void __launch_bounds__(256) heads_row_kernel(const float* __restrict_
       const int64_t row_idx = t * int64_t(H) * D + int64_t(u) * 4;
       const int64_t head_idx = ((int64_t(b) * H + h) * S + s) * D + d;
       if (merge)
-        put_split4(hi, lo, row_idx, ldv4(src + head_idx));
+        put_out4(hi, lo, t32, row_idx, ldv4(src + head_idx));
       else
-        put_split4(hi, lo, head_idx, ldv4(src + row_idx));
+        put_out4(hi, lo, t32, head_idx, ldv4(src + row_idx));
     }
   }
 }
 
 __device__ __forceinline__ float silu_of(float g) { return g / (1.f + expf(-g)); }
 
-// act = silu(g) * u, gu = [g | u] per row -> hi/lo (T, I).
+// act = silu(g) * u, gu = [g | u] per row -> hi/lo (T, I), and a tf32 copy
+// when t32 is given.
 __global__ void swiglu_split_kernel(const float* __restrict__ gu, int64_t T, int I,
-                                    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+                                    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                                    float* __restrict__ t32) {
   const int64_t total4 = T * I / 4;
   for (int64_t i4 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
        i4 += int64_t(gridDim.x) * blockDim.x) {
@@ -384,14 +408,15 @@ __global__ void swiglu_split_kernel(const float* __restrict__ gu, int64_t T, int
     a.y = silu_of(g.y) * u.y;
     a.z = silu_of(g.z) * u.z;
     a.w = silu_of(g.w) * u.w;
-    put_split4(hi, lo, e, a);
+    put_out4(hi, lo, t32, e, a);
   }
 }
 
-// dgu = [dact * u * silu'(g) | dact * silu(g)] -> hi/lo (T, 2I).
+// dgu = [dact * u * silu'(g) | dact * silu(g)] -> hi/lo and/or tf32 (T, 2I).
 __global__ void swiglu_bwd_split_kernel(const float* __restrict__ dact,
                                         const float* __restrict__ gu, int64_t T, int I,
-                                        uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+                                        uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                                        float* __restrict__ t32) {
   const int64_t total4 = T * I / 4;
   for (int64_t i4 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i4 < total4;
        i4 += int64_t(gridDim.x) * blockDim.x) {
@@ -411,8 +436,8 @@ __global__ void swiglu_bwd_split_kernel(const float* __restrict__ dact,
       dg[j] = ds[j] * us[j] * (sg * (1.f + gs[j] * (1.f - sg)));
       du[j] = ds[j] * sl;
     }
-    put_split4(hi, lo, t * 2 * I + c, make_float4(dg[0], dg[1], dg[2], dg[3]));
-    put_split4(hi, lo, t * 2 * I + I + c, make_float4(du[0], du[1], du[2], du[3]));
+    put_out4(hi, lo, t32, t * 2 * I + c, make_float4(dg[0], dg[1], dg[2], dg[3]));
+    put_out4(hi, lo, t32, t * 2 * I + I + c, make_float4(du[0], du[1], du[2], du[3]));
   }
 }
 
@@ -675,26 +700,29 @@ bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0
 using namespace mr;
 
 extern "C" int mr_rmsnorm_split(const float* x, const uint16_t* w, int64_t rows, int h, float eps,
-                                uint16_t* hi, uint16_t* lo, float* rstd, void* stream) {
+                                uint16_t* hi, uint16_t* lo, float* t32, float* rstd,
+                                void* stream) {
   if (!x || !w || !hi || !lo || !rstd || rows <= 0 || h <= 0 || h % 4 || h > 4 * kMaxVec * kRowThreads)
     return MR_ERR_ARGUMENT;
-  if (!aligned16(x)) return MR_ERR_ALIGNMENT;
+  if (!aligned16(x) || (t32 && !aligned16(t32))) return MR_ERR_ALIGNMENT;
   rmsnorm_split_kernel<<<unsigned(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, w, h, eps, hi, lo, rstd);
+      x, w, h, eps, hi, lo, t32, rstd);
   return launch_status();
 }
 
 extern "C" int mr_rmsnorm_bwd_split(const float* dy, const float* x, const uint16_t* w,
                                     const float* rstd, const float* resid, int64_t rows, int h,
-                                    uint16_t* hi, uint16_t* lo, float* out, void* stream) {
+                                    uint16_t* hi, uint16_t* lo, float* t32, float* out,
+                                    void* stream) {
   if (!dy || !x || !w || !rstd || rows <= 0 || h <= 0 || h % 4 ||
       h > 4 * kMaxVec * kRowThreads)
     return MR_ERR_ARGUMENT;
-  if ((hi == nullptr) != (lo == nullptr) || (!hi && !out)) return MR_ERR_ARGUMENT;
-  if (!aligned16(dy) || !aligned16(x) || (resid && !aligned16(resid)) || (out && !aligned16(out)))
+  if ((hi == nullptr) != (lo == nullptr) || (!hi && !out && !t32)) return MR_ERR_ARGUMENT;
+  if (!aligned16(dy) || !aligned16(x) || (resid && !aligned16(resid)) || (out && !aligned16(out)) ||
+      (t32 && !aligned16(t32)))
     return MR_ERR_ALIGNMENT;
   rmsnorm_bwd_split_kernel<<<unsigned(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      dy, x, w, rstd, resid, h, hi, lo, out);
+      dy, x, w, rstd, resid, h, hi, lo, t32, out);
   return launch_status();
 }
 
@@ -721,51 +749,56 @@ extern "C" int mr_rope_split(const float* qkv, const float* cosv, const float* s
 
 extern "C" int mr_rope_bwd_split(const float* dq, const float* dk, const float* dv,
                                  const float* cosv, const float* sinv, int b, int s, int hq,
-                                 int hkv, int d, uint16_t* hi, uint16_t* lo, void* stream) {
+                                 int hkv, int d, uint16_t* hi, uint16_t* lo, float* t32,
+                                 void* stream) {
   if (!dq || !dk || !dv || !cosv || !sinv || b <= 0 || s <= 0 || d % 2) return MR_ERR_ARGUMENT;
+  if ((hi == nullptr) != (lo == nullptr) || (!hi && !t32)) return MR_ERR_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool rows = d % 8 == 0 && aligned16(dq) && aligned16(dk) && aligned16(dv) &&
-                    aligned16(cosv) && aligned16(sinv) && aligned8(hi) && aligned8(lo);
+                    aligned16(cosv) && aligned16(sinv) && aligned8(hi) && aligned8(lo) &&
+                    aligned16(t32);
   if (rows) {
     rope_bwd_row_kernel<<<row_grid(int64_t(b) * s), 256, 0, st>>>(dq, dk, dv, cosv, sinv, b, s, hq,
-                                                                   hkv, d, hi, lo);
+                                                                   hkv, d, hi, lo, t32);
   } else {
     const int64_t total = int64_t(b) * s * (hq + 2 * hkv) * (d / 2);
     rope_bwd_split_kernel<<<grid_elems(total), 256, 0, st>>>(dq, dk, dv, cosv, sinv, b, s, hq, hkv,
-                                                             d, hi, lo);
+                                                             d, hi, lo, t32);
   }
   return launch_status();
 }
 
 extern "C" int mr_heads_split(const float* src, int b, int s, int h, int d, int merge,
-                              uint16_t* hi, uint16_t* lo, void* stream) {
+                              uint16_t* hi, uint16_t* lo, float* t32, void* stream) {
   if (!src || !hi || !lo || b <= 0 || s <= 0 || h <= 0 || d % 4) return MR_ERR_ARGUMENT;
-  if (!aligned16(src)) return MR_ERR_ALIGNMENT;
+  if (!aligned16(src) || !aligned16(t32)) return MR_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (aligned8(hi) && aligned8(lo)) {
-    heads_row_kernel<<<row_grid(int64_t(b) * s), 256, 0, st>>>(src, b, s, h, d, merge, hi, lo);
+    heads_row_kernel<<<row_grid(int64_t(b) * s), 256, 0, st>>>(src, b, s, h, d, merge, hi, lo,
+                                                                t32);
   } else {
     const int64_t total4 = int64_t(b) * s * h * d / 4;
-    heads_kernel<<<grid_elems(total4), 256, 0, st>>>(src, b, s, h, d, merge, hi, lo);
+    heads_kernel<<<grid_elems(total4), 256, 0, st>>>(src, b, s, h, d, merge, hi, lo, t32);
   }
   return launch_status();
 }
 
 extern "C" int mr_swiglu_split(const float* gu, int64_t t, int i, uint16_t* hi, uint16_t* lo,
-                               void* stream) {
+                               float* t32, void* stream) {
   if (!gu || !hi || !lo || t <= 0 || i <= 0 || i % 4) return MR_ERR_ARGUMENT;
-  if (!aligned16(gu)) return MR_ERR_ALIGNMENT;
+  if (!aligned16(gu) || !aligned16(t32)) return MR_ERR_ALIGNMENT;
   swiglu_split_kernel<<<grid_elems(t * i / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      gu, t, i, hi, lo);
+      gu, t, i, hi, lo, t32);
   return launch_status();
 }
 
 extern "C" int mr_swiglu_bwd_split(const float* dact, const float* gu, int64_t t, int i,
-                                   uint16_t* hi, uint16_t* lo, void* stream) {
-  if (!dact || !gu || !hi || !lo || t <= 0 || i <= 0 || i % 4) return MR_ERR_ARGUMENT;
-  if (!aligned16(dact) || !aligned16(gu)) return MR_ERR_ALIGNMENT;
+                                   uint16_t* hi, uint16_t* lo, float* t32, void* stream) {
+  if (!dact || !gu || t <= 0 || i <= 0 || i % 4) return MR_ERR_ARGUMENT;
+  if ((hi == nullptr) != (lo == nullptr) || (!hi && !t32)) return MR_ERR_ARGUMENT;
+  if (!aligned16(dact) || !aligned16(gu) || !aligned16(t32)) return MR_ERR_ALIGNMENT;
   swiglu_bwd_split_kernel<<<grid_elems(t * i / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      dact, gu, t, i, hi, lo);
+      dact, gu, t, i, hi, lo, t32);
   return launch_status();
 }
 
@@ -815,5 +848,32 @@ extern "C" int mr_softmax_bwd_split(const float* dp, const uint16_t* p_hi, const
       softmax_bwd_kernel<<<unsigned(rows), kSoftThreads, 0, st>>>(dp, p_hi, p_lo, s, scale, band,
                                                                   hi, lo);
   }
+  return launch_status();
+}
+
+namespace mr {
+namespace {
+
+__global__ void round_tf32_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
+  const int64_t n4 = n / 4;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    reinterpret_cast<float4*>(out)[i] =
+        make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+  }
+  for (int64_t i = n4 * 4 + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = tf32_rna(x[i]);
+}
+
+}  // namespace
+}  // namespace mr
+
+extern "C" int mr_round_tf32(const float* x, int64_t n, float* out, void* stream) {
+  if (!x || !out || n <= 0) return MR_ERR_ARGUMENT;
+  if (!aligned16(x) || !aligned16(out)) return MR_ERR_ALIGNMENT;
+  round_tf32_kernel<<<grid_elems((n + 3) / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n,
+                                                                                             out);
   return launch_status();
 }

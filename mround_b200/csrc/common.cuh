@@ -42,6 +42,14 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+// float32 -> tf32 value (round to nearest, ties away from zero; the low 13
+// bits cleared), the form the tf32 GEMM consumes exactly.
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
 // Unpack 8 bf16 held in a uint4 into floats (exact).
 __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};

@@ -167,6 +167,14 @@ __device__ __forceinline__ void store_f8(float* p, const float (&x)[8]) {
   reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
 }
 
+// The tf32-rounded copy of 8 values (the backward GEMMs' float32 operand).
+__device__ __forceinline__ void store_t8(float* p, const float (&x)[8]) {
+  reinterpret_cast<float4*>(p)[0] =
+      make_float4(tf32_rna(x[0]), tf32_rna(x[1]), tf32_rna(x[2]), tf32_rna(x[3]));
+  reinterpret_cast<float4*>(p)[1] =
+      make_float4(tf32_rna(x[4]), tf32_rna(x[5]), tf32_rna(x[6]), tf32_rna(x[7]));
+}
+
 __device__ __forceinline__ void store_split(const float (&wq)[8], int64_t e, uint16_t* hi,
                                             uint16_t* lo) {
   uint16_t h[8], l[8];
@@ -195,7 +203,8 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
     const uint16_t* __restrict__ w, const float* __restrict__ v, const float* __restrict__ alpha,
     const float* __restrict__ beta, const float* __restrict__ init_scale, int64_t n, int group,
     float maxq, float eps, uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo,
-    float* __restrict__ wq_f32, float* __restrict__ scale_out, float* __restrict__ zp_out) {
+    float* __restrict__ wq_f32, float* __restrict__ wq_t32, float* __restrict__ scale_out,
+    float* __restrict__ zp_out) {
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
@@ -226,6 +235,7 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
       wq[i] = dequant<MODE>(clamp_code<MODE>(unclamped_code<MODE>(wf[i], vf[i], q), maxq), q);
     store_split(wq, e, wq_hi, wq_lo);
     if (wq_f32) store_f8(wq_f32 + e, wq);
+    if (wq_t32) store_t8(wq_t32 + e, wq);
     if ((lane & (LPG - 1)) == 0) {
       if (scale_out) scale_out[gi] = q.scale;
       if (zp_out) zp_out[gi] = q.zp;
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
     float* __restrict__ alpha, float* __restrict__ beta, const float* __restrict__ init_scale,
     int64_t n, int group, float maxq, float eps, float lr, float lo, float hi, int update,
     float* __restrict__ gv_out, float* __restrict__ ga_out, float* __restrict__ gb_out,
-    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo) {
+    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo, float* __restrict__ wq_t32) {
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
@@ -330,13 +340,14 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
       alpha[gi] = an;
       beta[gi] = bn;
     }
-    if (wq_hi || wq_lo) {
+    if (wq_hi || wq_lo || wq_t32) {
       const GroupQ qn = group_params<MODE>(gmax, gmin, an, bn, base, maxq, eps);
       float wq[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         wq[i] = dequant<MODE>(clamp_code<MODE>(unclamped_code<MODE>(wf[i], vn[i], qn), maxq), qn);
       store_split(wq, e, wq_hi, wq_lo);
+      if (wq_t32) store_t8(wq_t32 + e, wq);
     }
   }
 }
@@ -503,20 +514,21 @@ float mode_maxq(int mode, int bits) {
 extern "C" int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float* alpha,
                              const float* beta, int64_t rows, int64_t cols, int group, int bits,
                              int symmetric, const float* init_scale, float eps, uint16_t* wq_hi,
-                             uint16_t* wq_lo, float* wq_f32, float* scale, float* zp,
-                             void* stream) {
+                             uint16_t* wq_lo, float* wq_f32, float* wq_t32, float* scale,
+                             float* zp, void* stream) {
   int st = check_common(w_bf16, v, rows, cols, group, bits);
   if (st) return st;
   const int mode = scheme_mode(symmetric, init_scale);
   if (!alpha || !beta || mode < 0) return MR_ERR_ARGUMENT;
-  if ((wq_hi && !aligned16(wq_hi)) || (wq_lo && !aligned16(wq_lo)) || (wq_f32 && !aligned16(wq_f32)))
+  if ((wq_hi && !aligned16(wq_hi)) || (wq_lo && !aligned16(wq_lo)) || (wq_f32 && !aligned16(wq_f32)) ||
+      (wq_t32 && !aligned16(wq_t32)))
     return MR_ERR_ALIGNMENT;
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
   const float maxq = mode_maxq(mode, bits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   MR_DISPATCH(mode, group, fq_forward_kernel, grid, s, w_bf16, v, alpha, beta, init_scale, n,
-              group, maxq, eps, wq_hi, wq_lo, wq_f32, scale, zp);
+              group, maxq, eps, wq_hi, wq_lo, wq_f32, wq_t32, scale, zp);
   return launch_status();
 }
 
@@ -524,20 +536,22 @@ extern "C" int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v,
                               float* beta, int64_t rows, int64_t cols, int group, int bits,
                               int symmetric, const float* init_scale, float eps, float lr,
                               float coef_lo, float coef_hi, int update, float* gv, float* galpha,
-                              float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, void* stream) {
+                              float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_t32,
+                              void* stream) {
   int st = check_common(w_bf16, v, rows, cols, group, bits);
   if (st) return st;
   const int mode = scheme_mode(symmetric, init_scale);
   if (!gq || !alpha || !beta || mode < 0) return MR_ERR_ARGUMENT;
   if (!aligned16(gq) || (gv && !aligned16(gv)) || (wq_hi && !aligned16(wq_hi)) ||
-      (wq_lo && !aligned16(wq_lo)))
+      (wq_lo && !aligned16(wq_lo)) || (wq_t32 && !aligned16(wq_t32)))
     return MR_ERR_ALIGNMENT;
   const int64_t n = rows * cols;
   const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
   const float maxq = mode_maxq(mode, bits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, init_scale, n,
-              group, maxq, eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo);
+              group, maxq, eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo,
+              wq_t32);
   return launch_status();
 }
 

@@ -6,7 +6,12 @@
 // bf16(x - hi)), so float32 activations and fake-quantized weights reach the
 // tensor cores with 16 significant bits: precision 3 issues hi*hi + hi*lo +
 // lo*hi into one TMEM accumulator, precision 2 hi*hi + lo*hi (B exact in
-// bf16), precision 1 hi*hi.
+// bf16), precision 1 hi*hi.  Precision 4 is one tf32 product
+// (tcgen05.mma kind::tf32): both operands are float32 tensors whose values
+// the producer has already rounded to tf32 (10 explicit mantissa bits, round
+// to nearest), so the tensor core's reading of the upper 19 bits is exact.
+// A tf32 product costs two bf16 products of tensor time and carries 11
+// significant bits per operand.
 //
 // Structure: a persistent kernel, one CTA (192 threads) per SM, walking the
 // flattened (batch, M-tile, N-tile) list of 128 x BN output tiles with stride
@@ -25,11 +30,14 @@
 //                      previous C, stores float32 rows, and arrives on
 //                      "tmem_empty" -- while the MMAs of the next tile run in
 //                      the other accumulator.
-// Operand majorness: K-major tiles are TMA boxes {BK (K), rows} with BK*2-byte
-// swizzle; MN-major tiles are boxes {64 (M or N), BK (K)} with 128-byte
-// swizzle, one per 64-wide MN chunk.  The UMMA shared-memory descriptors
-// describe the canonical layouts of both (K-major: 8-row groups BK*16 B apart;
-// MN-major: 8-K-row groups 1024 B apart, 64-wide MN chunks one box apart).
+// Operand majorness: K-major tiles are TMA boxes {BK (K), rows} whose rows of
+// BK elements (64 or 128 bytes) are swizzled at their width; MN-major tiles
+// are boxes {128 bytes of M or N, BK (K)}, one per MN chunk (64 bf16 or 32
+// float32 values).  The UMMA shared-memory descriptors describe the canonical
+// layouts of both (K-major: 8-row groups 8 rows apart; bf16 MN-major: 128-byte
+// swizzle, 8-K-row groups 1024 B apart; float32 MN-major: the 128-byte
+// swizzle of 32-byte atoms that kind::tf32 requires, 4-K-row groups 512 B
+// apart; MN chunks one box apart).
 // K slices are 32 wide (64-byte rows) when an operand is K-major: a stage is
 // then 48 KB for three products at BN = 256, four stages fit, and the loads
 // run several MMA groups ahead.  With both operands MN-major the slices are 64
@@ -41,6 +49,8 @@
 
 #include <cuda.h>
 #include <string.h>
+
+#include <atomic>
 
 #include "common.cuh"
 
@@ -134,6 +144,15 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint6
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -168,7 +187,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
 
 // ---------------------------------------------------------------- descriptors
 // UMMA shared-memory descriptor for a swizzled canonical layout
-// (layout type 2 = SWIZZLE_128B, 4 = SWIZZLE_64B).
+// (layout type 2 = SWIZZLE_128B, 4 = SWIZZLE_64B, 1 = SWIZZLE_128B with
+// 32-byte atoms).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
                                               uint32_t layout) {
   uint64_t d = 0;
@@ -180,11 +200,12 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return d;
 }
 
-// Instruction descriptor: bf16 x bf16 -> f32, M=128, N=BN, given majorness.
-__host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn) {
+// Instruction descriptor: bf16 x bf16 (or tf32 x tf32) -> f32, M=128, N=BN,
+// given majorness.
+__host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn, bool tf32) {
   return (1u << 4)                       // D format f32
-         | (1u << 7)                     // A bf16
-         | (1u << 10)                    // B bf16
+         | ((tf32 ? 2u : 1u) << 7)       // A bf16 (1) or tf32 (2)
+         | ((tf32 ? 2u : 1u) << 10)      // B bf16 (1) or tf32 (2)
          | (uint32_t(a_mn) << 15)        // A major
          | (uint32_t(b_mn) << 16)        // B major
          | (uint32_t(n >> 3) << 17)      // N
@@ -193,9 +214,12 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn) {
 
 template <int BN, int BK, int PREC>
 struct Cfg {
-  static constexpr int kA = BM * BK * 2;                  // bytes of one A part per stage
-  static constexpr int kB = BN * BK * 2;                  // bytes of one B part per stage
-  static constexpr int kAParts = PREC >= 2 ? 2 : 1;
+  static constexpr bool kTf32 = PREC == 4;
+  static constexpr int kElt = kTf32 ? 4 : 2;              // operand element bytes
+  static constexpr int kMmaK = 32 / kElt;                 // K of one MMA (32 bytes)
+  static constexpr int kA = BM * BK * kElt;               // bytes of one A part per stage
+  static constexpr int kB = BN * BK * kElt;               // bytes of one B part per stage
+  static constexpr int kAParts = (PREC == 2 || PREC == 3) ? 2 : 1;
   static constexpr int kBParts = PREC == 3 ? 2 : 1;
   static constexpr int kStage = kA * kAParts + kB * kBParts;
   static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
@@ -228,27 +252,30 @@ struct RemoteOut {
 };
 
 // Load one operand part (rows x BK) of a stage.  K-major: one box {BK, rows}.
-// MN-major: rows/64 boxes {64, BK} at 64 * BK * 2 bytes spacing.
-template <int ROWS, int BK>
+// MN-major: one box {128 / ELT, BK} per 128-byte MN chunk, 128 * BK bytes apart.
+template <int ROWS, int BK, int ELT>
 __device__ __forceinline__ void load_part(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                           bool kmajor, int row0, int k0, int z) {
   if (kmajor) {
     tma_load_3d(dst, map, bar, k0, row0, z);
   } else {
+    constexpr int kChunk = 128 / ELT;
 #pragma unroll
-    for (int c = 0; c < ROWS / 64; ++c)
-      tma_load_3d(dst + c * 64 * BK * 2, map, bar, row0 + c * 64, k0, z);
+    for (int c = 0; c < ROWS / kChunk; ++c)
+      tma_load_3d(dst + c * 128 * BK, map, bar, row0 + c * kChunk, k0, z);
   }
 }
 
-template <int BK>
+template <int BK, int ELT>
 __device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int kstep) {
-  // K-major: +32 B per 16-wide K step inside the swizzle row (BK * 2 bytes);
-  // 8-row groups 8 * BK * 2 bytes apart (SBO); SWIZZLE_64B or SWIZZLE_128B.
-  // MN-major: +2048 B (two 8-row K groups of 1024 B) per K step; LBO = one
-  // 64-wide MN box.
-  return kmajor ? smem_desc(base + kstep * 32, 16, 8 * BK * 2, BK == 32 ? 4 : 2)
-                : smem_desc(base + kstep * 2048, 64 * BK * 2, 1024, 2);
+  // K-major: +32 B per MMA K step inside the swizzle row (BK * ELT bytes);
+  // 8-row groups 8 rows apart (SBO); SWIZZLE_64B or SWIZZLE_128B by row width.
+  // bf16 MN-major: +2048 B (two 8-row K groups of 1024 B) per 16-deep K step;
+  // LBO = one MN box.  float32 MN-major (SWIZZLE_128B, 32-byte atoms): +1024 B
+  // (two 4-row K groups of 512 B) per 8-deep K step; LBO = one MN box.
+  if (kmajor) return smem_desc(base + kstep * 32, 16, 8 * BK * ELT, BK * ELT == 64 ? 4 : 2);
+  if (ELT == 2) return smem_desc(base + kstep * 2048, 128 * BK, 1024, 2);
+  return smem_desc(base + kstep * 1024, 128 * BK, 512, 1);
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -378,13 +405,15 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* st = smem + s * C::kStage;
           mbar_expect_tx(&full[s], C::kStage);
           const int k0 = kt * BK;
-          load_part<BM, BK>(st, &maps.a_hi, &full[s], a_kmajor, tl.m0, k0, tl.z);
+          load_part<BM, BK, C::kElt>(st, &maps.a_hi, &full[s], a_kmajor, tl.m0, k0, tl.z);
           if (C::kAParts == 2)
-            load_part<BM, BK>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, tl.m0, k0, tl.z);
+            load_part<BM, BK, C::kElt>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, tl.m0, k0,
+                                       tl.z);
           uint8_t* sb = st + C::kA * C::kAParts;
-          load_part<BN, BK>(sb, &maps.b_hi, &full[s], b_kmajor, tl.n0, k0, tl.z);
+          load_part<BN, BK, C::kElt>(sb, &maps.b_hi, &full[s], b_kmajor, tl.n0, k0, tl.z);
           if (C::kBParts == 2)
-            load_part<BN, BK>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, tl.n0, k0, tl.z);
+            load_part<BN, BK, C::kElt>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, tl.n0, k0,
+                                       tl.z);
         }
       }
       if (!ok) {
@@ -400,7 +429,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
-      const uint32_t idesc = instr_desc(BN, !a_kmajor, !b_kmajor);
+      const uint32_t idesc = instr_desc(BN, !a_kmajor, !b_kmajor, C::kTf32);
       bool ok = true;
       int it = 0, j = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++j) {
@@ -423,13 +452,19 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b_hi = st + C::kA * C::kAParts;
           const uint32_t b_lo = b_hi + C::kB;
 #pragma unroll
-          for (int ks = 0; ks < BK / 16; ++ks) {
+          for (int ks = 0; ks < BK / C::kMmaK; ++ks) {
             const uint32_t acc0 = (!first || ks > 0) ? 1u : 0u;
-            const uint64_t dah = part_desc<BK>(a_hi, a_kmajor, ks);
-            const uint64_t dbh = part_desc<BK>(b_hi, b_kmajor, ks);
-            umma_bf16(d, dah, dbh, idesc, acc0);
-            if (PREC == 3) umma_bf16(d, dah, part_desc<BK>(b_lo, b_kmajor, ks), idesc, 1u);
-            if (PREC >= 2) umma_bf16(d, part_desc<BK>(a_lo, a_kmajor, ks), dbh, idesc, 1u);
+            const uint64_t dah = part_desc<BK, C::kElt>(a_hi, a_kmajor, ks);
+            const uint64_t dbh = part_desc<BK, C::kElt>(b_hi, b_kmajor, ks);
+            if constexpr (C::kTf32) {
+              umma_tf32(d, dah, dbh, idesc, acc0);
+            } else {
+              umma_bf16(d, dah, dbh, idesc, acc0);
+              if (PREC == 3)
+                umma_bf16(d, dah, part_desc<BK, 2>(b_lo, b_kmajor, ks), idesc, 1u);
+              if (PREC >= 2)
+                umma_bf16(d, part_desc<BK, 2>(a_lo, a_kmajor, ks), dbh, idesc, 1u);
+            }
           }
           umma_commit(&empty[s]);
           ++it;
@@ -576,41 +611,60 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
-              int64_t batch, int64_t batch_stride, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle swizzle) {
+// 3-D tiled map (inner, outer, batch) of bf16 (elt 2) or float32 (elt 4) values.
+bool make_map(CUtensorMap* map, const void* base, int elt, int64_t inner, int64_t outer,
+              int64_t ld, int64_t batch, int64_t batch_stride, uint32_t box_inner,
+              uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn encode = encode_fn();
   if (!encode) return false;
   const cuuint64_t dims[3] = {cuuint64_t(inner), cuuint64_t(outer), cuuint64_t(batch)};
-  const cuuint64_t strides[2] = {cuuint64_t(ld) * 2,
-                                 cuuint64_t(batch > 1 ? batch_stride : ld * outer) * 2};
+  const cuuint64_t strides[2] = {cuuint64_t(ld) * elt,
+                                 cuuint64_t(batch > 1 ? batch_stride : ld * outer) * elt};
   const cuuint32_t box[3] = {box_inner, box_outer, 1};
   const cuuint32_t elem_strides[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
-                      strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  CUresult r = encode(map, elt == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                      3, const_cast<void*>(base), dims, strides, box, elem_strides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-// Map for an operand with `rows` logical rows (M or N) and K columns.
-bool operand_map(CUtensorMap* map, const void* p, bool kmajor, int64_t rows, int64_t k,
+// Map for an operand with `rows` logical rows (M or N) and K columns.  K-major
+// boxes are {bk, tile_rows} swizzled at their row width (bk * elt bytes);
+// MN-major boxes are {128 bytes of rows, bk}: 128-byte swizzle for bf16, the
+// 32-byte-atom form of it for float32 (the layout kind::tf32 reads MN-major).
+bool operand_map(CUtensorMap* map, const void* p, int elt, bool kmajor, int64_t rows, int64_t k,
                  int64_t ld, int64_t batch, int64_t batch_stride, int tile_rows, int bk) {
   if (kmajor)
-    return make_map(map, p, k, rows, ld, batch, batch_stride, uint32_t(bk), uint32_t(tile_rows),
-                    bk == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
-  return make_map(map, p, rows, k, ld, batch, batch_stride, 64, uint32_t(bk),
-                  CU_TENSOR_MAP_SWIZZLE_128B);
+    return make_map(map, p, elt, k, rows, ld, batch, batch_stride, uint32_t(bk),
+                    uint32_t(tile_rows),
+                    bk * elt == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_map(map, p, elt, rows, k, ld, batch, batch_stride, uint32_t(128 / elt), uint32_t(bk),
+                  elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Per-device caches (a process may drive several GPUs from one or more host
+// threads): the SM count and, per kernel instantiation, whether its dynamic
+// shared-memory limit has been raised on that device.  Racing first calls
+// only repeat an idempotent query or attribute call.
+constexpr int kMaxDevices = 64;
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  return dev;
 }
 
 int sm_count() {
-  static int count = 0;
+  static std::atomic<int> counts[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0) return kSMs;
+  int count = counts[dev].load(std::memory_order_relaxed);
   if (!count) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         count <= 0)
       count = kSMs;
+    counts[dev].store(count, std::memory_order_relaxed);
   }
   return count;
 }
@@ -620,15 +674,17 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
            int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
            int causal, int clen, const RemoteOut& remote, cudaStream_t stream) {
   using C = Cfg<BN, BK, PREC>;
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<bool> configured[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0) return MR_ERR_DEVICE;
+  if (!configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BK, PREC>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) {
       set_cuda_error(e);
       return MR_ERR_LAUNCH;
     }
-    configured = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   const int64_t tiles = int64_t((m + BM - 1) / BM) * ((n + BN - 1) / BN) * batch;
   if (tiles > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
@@ -646,22 +702,29 @@ using namespace mr;
 
 namespace {
 
-int gemm_impl(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int64_t stride_a,
-              int a_kmajor, const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb,
+// precision 1..3: bf16 operands (hi, optional lo); 4: one tf32 product of
+// float32 operands (a_hi / b_hi point at float32 data; the lo parts are unused).
+int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
+              int a_kmajor, const void* b_hi, const void* b_lo, int64_t ldb,
               int64_t stride_b, int b_kmajor, float* c, int64_t ldc, int64_t stride_c,
               const float* bias, int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
               int precision, int causal, int64_t seq, const RemoteOut& remote, void* stream) {
   if (!a_hi || !b_hi || !c || m <= 0 || n <= 0 || k <= 0 || batch <= 0) return MR_ERR_ARGUMENT;
   if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1 || batch > 65535)
     return MR_ERR_ARGUMENT;
-  if (precision < 1 || precision > 3) return MR_ERR_ARGUMENT;
-  if (precision >= 2 && !a_lo) return MR_ERR_ARGUMENT;
+  if (precision < 1 || precision > 4) return MR_ERR_ARGUMENT;
+  const bool tf32 = precision == 4;
+  const int elt = tf32 ? 4 : 2;
+  if (tf32) a_lo = b_lo = nullptr;
+  if ((precision == 2 || precision == 3) && !a_lo) return MR_ERR_ARGUMENT;
   if (precision == 3 && !b_lo) return MR_ERR_ARGUMENT;
   if (!aligned16(a_hi) || !aligned16(b_hi) || (a_lo && !aligned16(a_lo)) ||
       (b_lo && !aligned16(b_lo)))
     return MR_ERR_ALIGNMENT;
-  if ((lda % 8) || (ldb % 8)) return MR_ERR_ALIGNMENT;
-  if (batch > 1 && ((stride_a % 8) || (stride_b % 8))) return MR_ERR_ALIGNMENT;
+  // TMA: global strides are multiples of 16 bytes
+  const int per16 = 16 / elt;
+  if ((lda % per16) || (ldb % per16)) return MR_ERR_ALIGNMENT;
+  if (batch > 1 && ((stride_a % per16) || (stride_b % per16))) return MR_ERR_ALIGNMENT;
   if (a_kmajor ? lda < k : lda < m) return MR_ERR_ARGUMENT;
   if (b_kmajor ? ldb < k : ldb < n) return MR_ERR_ARGUMENT;
   if (ldc < n) return MR_ERR_ARGUMENT;
@@ -675,16 +738,19 @@ int gemm_impl(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int64_t s
   // narrow outputs (attention's head dimension) use 128-wide tiles; 32-wide K
   // slices (deeper pipelines) unless both operands are MN-major, whose 64-wide
   // boxes would then be split into many small TMA copies
+  // float32 (tf32) operands: 32-wide K slices (128-byte K-major rows, four
+  // 48 KB stages at BN = 256) for every majorness.
   const int BNsel = n <= 128 ? 128 : 256;
-  const int BKsel = (!a_kmajor && !b_kmajor) ? 64 : 32;
+  const int BKsel = tf32 ? 32 : (!a_kmajor && !b_kmajor) ? 64 : 32;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
-  bool good = operand_map(&maps.a_hi, a_hi, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel) &&
-              operand_map(&maps.b_hi, b_hi, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
-  if (good && precision >= 2)
-    good = operand_map(&maps.a_lo, a_lo, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel);
+  bool good =
+      operand_map(&maps.a_hi, a_hi, elt, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel) &&
+      operand_map(&maps.b_hi, b_hi, elt, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
+  if (good && (precision == 2 || precision == 3))
+    good = operand_map(&maps.a_lo, a_lo, elt, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel);
   if (good && precision == 3)
-    good = operand_map(&maps.b_lo, b_lo, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
+    good = operand_map(&maps.b_lo, b_lo, elt, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
   if (!good) return MR_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bt = int(batch);
@@ -697,6 +763,13 @@ int gemm_impl(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int64_t s
                                        a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);   \
     default: return launch<BN_, BK_, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,    \
                                         a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);  \
+  }
+  if (tf32) {
+    if (BNsel == 128)
+      return launch<128, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
+                                b_kmajor, bt, causal, int(seq), remote, s);
+    return launch<256, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
+                              b_kmajor, bt, causal, int(seq), remote, s);
   }
   if (BNsel == 128) {
     if (BKsel == 64) { MR_GEMM_LAUNCH(128, 64) }
@@ -715,6 +788,7 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
                                float* c, int64_t ldc, int64_t stride_c, const float* bias,
                                int accumulate, int64_t m, int64_t n, int64_t k, int64_t batch,
                                int precision, int causal, int64_t seq, void* stream) {
+  if (precision < 1 || precision > 3) return MR_ERR_ARGUMENT;  // tf32: mr_gemm_tf32
   RemoteOut none;
   memset(&none, 0, sizeof(none));
   return gemm_impl(a_hi, a_lo, lda, stride_a, a_kmajor, b_hi, b_lo, ldb, stride_b, b_kmajor, c,
@@ -722,11 +796,13 @@ extern "C" int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64
                    stream);
 }
 
-extern "C" int mr_gemm_rs(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
-                          const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
-                          int64_t m, int64_t n, int64_t k, int precision, float* const* dst,
-                          int64_t ldd, int64_t rows_per_rank, unsigned long long* const* flags,
-                          int world, unsigned int* done, unsigned long long epoch, void* stream) {
+namespace {
+
+int gemm_rs_impl(const void* a_hi, const void* a_lo, int64_t lda, int a_kmajor, const void* b_hi,
+                 const void* b_lo, int64_t ldb, int b_kmajor, int64_t m, int64_t n, int64_t k,
+                 int precision, float* const* dst, int64_t ldd, int64_t rows_per_rank,
+                 unsigned long long* const* flags, int world, unsigned int* done,
+                 unsigned long long epoch, void* stream) {
   if (!dst || !flags || !done || world < 1 || world > kMaxRanks || rows_per_rank <= 0 ||
       m != rows_per_rank * world || ldd < n || epoch == 0)
     return MR_ERR_ARGUMENT;
@@ -750,12 +826,42 @@ extern "C" int mr_gemm_rs(const uint16_t* a_hi, const uint16_t* a_lo, int64_t ld
                    nullptr, 0, m, n, k, 1, precision, 0, 0, remote, stream);
 }
 
+}  // namespace
+
+extern "C" int mr_gemm_rs(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
+                          const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
+                          int64_t m, int64_t n, int64_t k, int precision, float* const* dst,
+                          int64_t ldd, int64_t rows_per_rank, unsigned long long* const* flags,
+                          int world, unsigned int* done, unsigned long long epoch, void* stream) {
+  if (precision < 1 || precision > 3) return MR_ERR_ARGUMENT;  // tf32: mr_gemm_rs_tf32
+  return gemm_rs_impl(a_hi, a_lo, lda, a_kmajor, b_hi, b_lo, ldb, b_kmajor, m, n, k, precision,
+                      dst, ldd, rows_per_rank, flags, world, done, epoch, stream);
+}
+
 extern "C" int mr_gemm(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int a_kmajor,
                        const uint16_t* b_hi, const uint16_t* b_lo, int64_t ldb, int b_kmajor,
                        float* c, int64_t ldc, const float* bias, int accumulate, int64_t m,
                        int64_t n, int64_t k, int precision, void* stream) {
   return mr_gemm_batched(a_hi, a_lo, lda, 0, a_kmajor, b_hi, b_lo, ldb, 0, b_kmajor, c, ldc, 0,
                          bias, accumulate, m, n, k, 1, precision, 0, 0, stream);
+}
+
+extern "C" int mr_gemm_tf32(const float* a, int64_t lda, int a_kmajor, const float* b,
+                            int64_t ldb, int b_kmajor, float* c, int64_t ldc, const float* bias,
+                            int accumulate, int64_t m, int64_t n, int64_t k, void* stream) {
+  RemoteOut none;
+  memset(&none, 0, sizeof(none));
+  return gemm_impl(a, nullptr, lda, 0, a_kmajor, b, nullptr, ldb, 0, b_kmajor, c, ldc, 0, bias,
+                   accumulate, m, n, k, 1, 4, 0, 0, none, stream);
+}
+
+extern "C" int mr_gemm_rs_tf32(const float* a, int64_t lda, int a_kmajor, const float* b,
+                               int64_t ldb, int b_kmajor, int64_t m, int64_t n, int64_t k,
+                               float* const* dst, int64_t ldd, int64_t rows_per_rank,
+                               unsigned long long* const* flags, int world, unsigned int* done,
+                               unsigned long long epoch, void* stream) {
+  return gemm_rs_impl(a, nullptr, lda, a_kmajor, b, nullptr, ldb, b_kmajor, m, n, k, 4, dst, ldd,
+                      rows_per_rank, flags, world, done, epoch, stream);
 }
 
 // Device status word of the GEMM (0 ok, MR_ERR_TIMEOUT after a wait gave up).

@@ -182,9 +182,15 @@ using namespace mr;
 
 extern "C" size_t mr_loss_workspace_bytes(void) { return sizeof(Workspace); }
 
+// The histogram bins count with 32-bit integers: inputs of 2^32 elements or
+// more are refused rather than miscounted (every entry point that selects a
+// threshold checks this).
+constexpr int64_t kMaxSelectElements = int64_t(0xFFFFFFFFll);
+
 extern "C" int mr_loss_hist_pass(const float* pred, const float* target, int64_t n, int pass,
                                  const void* state, uint32_t* hist, void* stream) {
   if (!pred || !target || !hist || n <= 0 || pass < 0 || pass > 2) return MR_ERR_ARGUMENT;
+  if (n > kMaxSelectElements) return MR_ERR_ARGUMENT;
   if (pass > 0 && !state) return MR_ERR_WORKSPACE;
   if (check_vec(pred) || check_vec(target)) return MR_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -226,6 +232,7 @@ extern "C" int mr_loss_outlier(const float* pred, const float* target, int64_t n
                                int suppress, double denom, float thr_in, float* grad,
                                double* loss, float* thr_out, void* workspace, void* stream) {
   if (!pred || !target || !loss || n <= 0 || !(denom > 0.0)) return MR_ERR_ARGUMENT;
+  if (n > kMaxSelectElements) return MR_ERR_ARGUMENT;
   if (!workspace) return MR_ERR_WORKSPACE;
   if (check_vec(pred) || check_vec(target) || (grad && check_vec(grad))) return MR_ERR_ALIGNMENT;
   Workspace* ws = static_cast<Workspace*>(workspace);
@@ -308,10 +315,22 @@ extern "C" int mr_loss_outlier_noalloc(const float* pred, const float* target, i
                                        int64_t k, int suppress, double denom, float thr_in,
                                        float* grad, double* loss, float* thr_out, void* stream) {
   // histogram counters are 32-bit: larger inputs are refused rather than miscounted
-  if (n > int64_t(0xFFFFFFFFll)) return MR_ERR_ARGUMENT;
+  if (n > kMaxSelectElements) return MR_ERR_ARGUMENT;
   void* scratch = nullptr;
   int st = mr::scratch_for_current_device(&scratch);
   if (st) return st;
+  // the scratch address belongs to the current device: a stream of another
+  // device would have its kernels read a different GPU's array
+  if (stream) {
+    int dev = 0, sdev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MR_ERR_DEVICE;
+    cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return MR_ERR_ARGUMENT;
+    }
+    if (sdev != dev) return MR_ERR_DEVICE;
+  }
   // Every field of the scratch that is read is first written by this call:
   // the histogram is cleared by each pass, the selection state is reset by
   // pass 0, and the partial sums are overwritten -- stale contents from an

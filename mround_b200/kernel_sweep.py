@@ -25,7 +25,17 @@ to the position, writes dS hi+lo up to the band limit), RoPE with the head
 re-layout and its backward (4 B read + 4 B of hi+lo written per q/k/v element),
 and the head merge of the attention output (the same per element).
 
-Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick | --attention]
+Other modes (measurement drivers of the profiles):
+  --gemm SHAPE TOKENS [--tf32]  one weight GEMM of the 7B step, three launches
+                                (the driver of a K3 ncu capture);
+  --gemm-table TOKENS           every weight GEMM of the 7B step timed as the
+                                bf16 split and as one tf32 product;
+  --step STEPS                  tuning steps of a 7B block, the last between
+                                cudaProfilerStart/Stop (a one-step launch list);
+  --exchange [--tf32]           the block's weight-gradient exchange, under
+                                torch.distributed.run.
+
+Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick | --attention | ...]
 Prints one JSON line per case, then a summary line.
 """
 
@@ -202,14 +212,251 @@ def attention(reps: int = 5, batch: int = 8, heads: int = 28, seq: int = 2048) -
     return results
 
 
+# ----------------------------------------------------------------- K3 shapes
+# The weight GEMMs of one Qwen2.5-7B block step at ``tokens`` rows of
+# activation (16384 = the 8 x 2048 batch on one GPU; 2048 = one sequence per
+# GPU at eight): name -> (m, n, k, A K-major, B K-major).
+H7, KV7, I7 = 3584, 512, 18944
+
+
+def gemm_shapes(tokens: int) -> dict[str, tuple[int, int, int, bool, bool]]:
+    out = {}
+    for name, rows, cols in (("qkv", H7 + 2 * KV7, H7), ("o", H7, H7), ("gu", 2 * I7, H7),
+                             ("down", H7, I7)):
+        out[f"fwd_{name}"] = (tokens, rows, cols, True, True)
+        if name != "qkv":  # the tuning step does not form the block-input gradient
+            out[f"dX_{name}"] = (tokens, cols, rows, True, False)
+        out[f"dW_{name}"] = (rows, cols, tokens, False, False)
+    return out
+
+
+def _gemm_operands(m, n, k, ak, bk, tf32: bool, device):
+    a_shape = (m, k) if ak else (k, m)
+    b_shape = (n, k) if bk else (k, n)
+    a = torch.randn(a_shape, device=device)
+    b = torch.randn(b_shape, device=device)
+    if tf32:
+        return (kernels.round_tf32(a, out=a),), (kernels.round_tf32(b, out=b),), a_shape, b_shape
+    ops = kernels.split_bf16(a), kernels.split_bf16(b)
+    del a, b
+    return ops[0], ops[1], a_shape, b_shape
+
+
+def _launch(aop, bop, c, m, n, k, ak, bk, a_shape, b_shape, tf32: bool):
+    if tf32:
+        kernels.gemm_tf32(aop[0], bop[0], c, m=m, n=n, k=k, a_kmajor=ak, b_kmajor=bk,
+                          lda=a_shape[1], ldb=b_shape[1], ldc=n)
+    else:
+        kernels.gemm(aop[0], aop[1], bop[0], bop[1], c, m=m, n=n, k=k, a_kmajor=ak, b_kmajor=bk,
+                     lda=a_shape[1], ldb=b_shape[1], ldc=n, precision=3)
+
+
+def gemm_probe(name: str, tokens: int, tf32: bool) -> None:
+    """One weight-GEMM shape launched three times: the driver of an ncu
+    capture of K3 (``-k regex:gemm_kernel -s 2 -c 1`` takes the third)."""
+    m, n, k, ak, bk = gemm_shapes(tokens)[name]
+    aop, bop, a_shape, b_shape = _gemm_operands(m, n, k, ak, bk, tf32, "cuda")
+    c = torch.empty(m, n, device="cuda")
+    for _ in range(3):
+        _launch(aop, bop, c, m, n, k, ak, bk, a_shape, b_shape, tf32)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": name, "tokens": tokens, "tf32": tf32}), flush=True)
+
+
+def gemm_table(tokens: int, reps: int = 5) -> list[dict]:
+    """Every weight GEMM of the 7B step, as the three-product bf16 split and
+    as one tf32 product: device time (CUDA events, median of ``reps``, after
+    a warm-up launch), algorithmic TF/s (2 m n k per launch) and executed
+    TF/s in bf16-product units (3 for the split, 2 for tf32)."""
+    peak = None
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    try:
+        with open(os.path.join(here, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        peak = 1590.0
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    out = []
+    for name, (m, n, k, ak, bk) in gemm_shapes(tokens).items():
+        for tf32 in (False, True):
+            aop, bop, a_shape, b_shape = _gemm_operands(m, n, k, ak, bk, tf32, "cuda")
+            c = torch.empty(m, n, device="cuda")
+            fn = lambda: _launch(aop, bop, c, m, n, k, ak, bk, a_shape, b_shape, tf32)  # noqa: E731
+            fn()
+            torch.cuda.synchronize()
+            ms = _time(fn, flush, reps)
+            alg = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+            cost = kernels.TF32_PRODUCT_COST if tf32 else 3
+            rec = {"gemm": name, "form": "tf32" if tf32 else "bf16x3", "m": m, "n": n, "k": k,
+                   "ms": ms, "alg_tflops": alg, "executed_tflops": alg * cost,
+                   "executed_frac_burst": alg * cost / peak}
+            out.append(rec)
+            print(json.dumps(rec), flush=True)
+            del aop, bop, c
+    return out
+
+
+# ----------------------------------------------------------------- one step
+def step_probe(steps: int, arch_name: str = "qwen2.5-7b", tokens: int = 2048,
+               batch: int = 8) -> None:
+    """``steps`` tuning steps of one block (W2 asym g64, the runner's default
+    precision) on random block-0 inputs, the last one between
+    cudaProfilerStart/Stop -- the launch list of one step under
+    ``ncu --profile-from-start off``."""
+    from mround_b200.pipeline.arch import get_arch
+    from mround_b200.pipeline.block import DeviceBlock
+    from mround_b200.pipeline.model import SyntheticModel
+    from mround_b200.pipeline.runner import QuantizationRunner
+    from mround_b200.schemes import QuantScheme, TuningConfig
+
+    arch = get_arch(arch_name)
+    block = DeviceBlock(arch, SyntheticModel(arch, seed=0).block(0), "cuda")
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(batch, tokens, arch.hidden, device="cuda", generator=g) * 0.02
+    runner = QuantizationRunner(QuantScheme(bits=2, group_size=64, symmetry="asym"),
+                                TuningConfig(iters=200))
+    tuner = runner.tuner_for(block, "model.layers.0")
+    target = tuner.output(x) + 1e-3
+    for i in range(steps - 1):
+        tuner.step(x, target, i, 200)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    tuner.step(x, target, steps - 1, 200)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"probe": "step", "arch": arch_name, "steps": steps,
+                      "precision": str(runner.precision)}), flush=True)
+
+
+# ----------------------------------------------------------------- exchange
+def exchange_probe(tf32: bool = False) -> None:
+    """The weight-gradient exchange of one Qwen2.5-7B block across ranks
+    (run under ``torch.distributed.run``).  For the block's four fused weight
+    gradients at the step's per-rank token count (16384 / N), four ways, each
+    averaged over 10 iterations after 3 warm-up ones, CUDA events, max over
+    ranks: ``gemm`` (the dW GEMMs alone, the lower bound), ``nccl`` (dW GEMM,
+    then an async NCCL reduce-scatter), ``p2p`` (the dW GEMM stores its rows
+    into the owners' slots over NVLink, then each owner's ordered sum) and
+    ``copy`` (dW GEMM locally, the copy engines move each owner's rows, the
+    same sum).  Rank 0 prints one line per way."""
+    import torch.distributed as tdist
+
+    from mround_b200.pipeline.dist import init_from_env
+    from mround_b200.pipeline.peer import PeerExchange
+
+    shapes = [(H7 + 2 * KV7, H7), (H7, H7), (2 * I7, H7), (H7, I7)]
+    dist = init_from_env("nccl", timeout_s=120.0)
+    world, rank = dist.world, dist.rank
+    dev = torch.device("cuda", torch.cuda.current_device())
+    t = 16384 // world
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    ins = []
+    for rows, cols in shapes:
+        dy = torch.randn(t, rows, device=dev, generator=gen)
+        x = torch.randn(t, cols, device=dev, generator=gen)
+        if tf32:
+            ins.append(((None, None, kernels.round_tf32(dy)), (None, None, kernels.round_tf32(x))))
+        else:
+            ins.append(((*kernels.split_bf16(dy), None), (*kernels.split_bf16(x), None)))
+    grads = [torch.empty(r, c, device=dev) for r, c in shapes]
+    shards = [torch.empty(r // world, c, device=dev) for r, c in shapes]
+    peer = PeerExchange(dist, shapes, dev) if world > 1 else None
+    copier = PeerExchange(dist, shapes, dev, copy_engine=True) if world > 1 else None
+    epoch = 0
+
+    def dw(dy, x, g, rows, cols):
+        if tf32:
+            kernels.gemm_tf32(dy[2], x[2], g, m=rows, n=cols, k=t, a_kmajor=False, b_kmajor=False,
+                              lda=rows, ldb=cols, ldc=cols)
+        else:
+            kernels.gemm(dy[0], dy[1], x[0], x[1], g, m=rows, n=cols, k=t, a_kmajor=False,
+                         b_kmajor=False, lda=rows, ldb=cols, ldc=cols, precision=3)
+
+    def step(way: str) -> None:
+        nonlocal epoch
+        if way == "p2p":
+            epoch += 1
+            for (rows, cols), (dy, x), ex in zip(shapes, ins, peer.layers):
+                kw = dict(m=rows, n=cols, k=t, a_kmajor=False, b_kmajor=False, lda=rows, ldb=cols,
+                          dst_ptrs=ex.dst_ptrs, ldd=cols, rows_per_rank=ex.rows_per_rank,
+                          flag_ptrs=ex.flag_ptrs, done=ex.done, epoch=epoch)
+                if tf32:
+                    kernels.gemm_rs_tf32(dy[2], x[2], **kw)
+                else:
+                    kernels.gemm_rs(dy[0], dy[1], x[0], x[1], precision=3, **kw)
+            for ex, out in zip(peer.layers, shards):
+                kernels.reduce_slots(ex.slots, ex.flags, epoch, out)
+            return
+        if way == "copy":
+            epoch += 1
+            for (rows, cols), (dy, x), g, ex in zip(shapes, ins, grads, copier.layers):
+                dw(dy, x, g, rows, cols)
+                ex.epoch = epoch
+                ex.send(g)
+            for ex in copier.layers:
+                ex.wait_copies()
+            for ex, out in zip(copier.layers, shards):
+                kernels.reduce_slots(ex.slots, ex.flags, epoch, out)
+            return
+        works = []
+        for (rows, cols), (dy, x), g, out in zip(shapes, ins, grads, shards):
+            dw(dy, x, g, rows, cols)
+            if way == "nccl" and world > 1:
+                works.append(tdist.reduce_scatter_tensor(out, g, async_op=True))
+        for w in works:
+            w.wait()
+
+    ways = ("gemm", "nccl", "p2p", "copy") if world > 1 else ("gemm",)
+    for way in ways:
+        for _ in range(3):
+            step(way)
+        dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(10):
+            step(way)
+        end.record()
+        torch.cuda.synchronize()
+        ms = dist.max_scalar(start.elapsed_time(end) / 10, dev)
+        status = int(kernels.lib().mr_peer_status(1))
+        if rank == 0:
+            print(json.dumps({"probe": "exchange", "world": world, "way": way,
+                              "form": "tf32" if tf32 else "bf16x3", "ms_per_block": ms,
+                              "peer_status": status}), flush=True)
+    dist.barrier()
+    if peer is not None:
+        peer.close()
+        copier.close()
+    if world > 1:
+        tdist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--quick", action="store_true")
-    ap.add_argument("--attention", action="store_true")
+    ap.add_argument("--attention", action="store_true", help="K7 attention-side kernels")
+    ap.add_argument("--gemm", nargs=2, metavar=("SHAPE", "TOKENS"),
+                    help="launch one 7B weight GEMM three times (ncu driver)")
+    ap.add_argument("--gemm-table", type=int, metavar="TOKENS",
+                    help="time every 7B weight GEMM as bf16x3 and tf32")
+    ap.add_argument("--tf32", action="store_true", help="--gemm / --exchange: tf32 operands")
+    ap.add_argument("--step", type=int, metavar="STEPS",
+                    help="7B tuning steps, the last between cudaProfilerStart/Stop")
+    ap.add_argument("--exchange", action="store_true",
+                    help="weight-gradient exchange of a 7B block (under torch.distributed.run)")
     args = ap.parse_args()
     if args.attention:
         attention(args.reps)
+    elif args.gemm:
+        gemm_probe(args.gemm[0], int(args.gemm[1]), args.tf32)
+    elif args.gemm_table:
+        gemm_table(args.gemm_table, args.reps)
+    elif args.step:
+        step_probe(args.step)
+    elif args.exchange:
+        exchange_probe(args.tf32)
     else:
         run(args.reps, args.quick)
 

@@ -20,11 +20,13 @@ __all__ = [
     "fq_forward",
     "gemm",
     "gemm_batched",
+    "gemm_tf32",
     "loss_apply",
     "loss_hist_pass",
     "loss_outlier",
     "loss_select_digit",
     "pack_mlx",
+    "round_tf32",
     "scale_search",
     "split_bf16",
     "ste_signsgd",
@@ -34,7 +36,9 @@ DEVICE_GROUPS = (8, 16, 32, 64, 128, 256)
 
 # Kernel launches issued through this module (bench.py reports them), and an
 # optional timing hook for GEMM launches: when ``GEMM_EVENTS`` is a list, each
-# K3 launch appends ``(start_event, end_event, algorithmic_flops)``.
+# K3 launch appends ``(start_event, end_event, algorithmic_flops, cost)``, cost
+# being the launch's tensor work in bf16 products per algorithmic product
+# (1-3 for the bf16 splits, TF32_PRODUCT_COST for one tf32 product).
 LAUNCHES = [0]
 GEMM_EVENTS: list | None = None
 
@@ -85,8 +89,10 @@ def _scheme_args(symmetric: bool, init_scale, ng: int):
 
 
 def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=None, wq_lo=None,
-               wq_f32=None, scale=None, zp=None, symmetric: bool = False, init_scale=None) -> None:
-    """K1: write the fake-quantized weight (bf16 hi/lo split and/or float32).
+               wq_f32=None, wq_t32=None, scale=None, zp=None, symmetric: bool = False,
+               init_scale=None) -> None:
+    """K1: write the fake-quantized weight (bf16 hi/lo split, float32 and/or
+    its tf32 rounding -- the backward GEMMs' operand).
 
     ``symmetric`` selects the symmetric code range; ``init_scale`` (float32,
     one per group) the searched scale.
@@ -97,7 +103,8 @@ def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=No
     status = lib().mr_fq_forward(
         pw, pv, pa, pb, rows, cols, group, bits, sym, pinit, eps,
         _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
-        _ptr(wq_f32, torch.float32, "wq_f32", n), _ptr(scale, torch.float32, "scale", ng),
+        _ptr(wq_f32, torch.float32, "wq_f32", n), _ptr(wq_t32, torch.float32, "wq_t32", n),
+        _ptr(scale, torch.float32, "scale", ng),
         _ptr(zp, torch.float32, "zp", ng), _stream())
     check(status, "mr_fq_forward")
     _count()
@@ -105,8 +112,10 @@ def fq_forward(w, v, alpha, beta, *, bits: int, group: int, eps: float, wq_hi=No
 
 def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr: float,
                 lo: float, hi: float, update: bool = True, gv=None, galpha=None, gbeta=None,
-                wq_hi=None, wq_lo=None, symmetric: bool = False, init_scale=None) -> None:
-    """K2: straight-through gradients, then (if ``update``) the signed step in place."""
+                wq_hi=None, wq_lo=None, wq_t32=None, symmetric: bool = False,
+                init_scale=None) -> None:
+    """K2: straight-through gradients, then (if ``update``) the signed step in
+    place and the next step's operands (bf16 hi/lo, tf32)."""
     rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
     n, ng = rows * cols, rows * (cols // group)
     sym, pinit = _scheme_args(symmetric, init_scale, ng)
@@ -116,7 +125,7 @@ def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr:
         hi, int(bool(update)), _ptr(gv, torch.float32, "gv", n),
         _ptr(galpha, torch.float32, "galpha", ng), _ptr(gbeta, torch.float32, "gbeta", ng),
         _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
-        _stream())
+        _ptr(wq_t32, torch.float32, "wq_t32", n), _stream())
     check(status, "mr_ste_signsgd")
     _count()
 
@@ -349,6 +358,56 @@ def gemm_rs(a_hi, a_lo, b_hi, b_lo, *, m: int, n: int, k: int, a_kmajor: bool, b
         GEMM_EVENTS.append((start, end, 2.0 * m * n * k, precision))
 
 
+# tensor time of one tf32 product, in bf16 products (tf32 runs at half the rate)
+TF32_PRODUCT_COST = 2
+
+
+def gemm_tf32(a, b, c, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool, lda: int,
+              ldb: int, ldc: int, bias=None, accumulate: bool = False) -> None:
+    """K3, one tf32 product: ``C[m, n] (+)= sum_k A[m, k] B[n, k]`` with float32
+    operands already rounded to tf32 (``round_tf32`` or a kernel's t32 output)."""
+    timing = GEMM_EVENTS is not None
+    if timing:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+    status = lib().mr_gemm_tf32(
+        _ptr(a, torch.float32, "a"), lda, int(a_kmajor), _ptr(b, torch.float32, "b"), ldb,
+        int(b_kmajor), _ptr(c, torch.float32, "c"), ldc, _ptr(bias, torch.float32, "bias"),
+        int(bool(accumulate)), m, n, k, _stream())
+    check(status, "mr_gemm_tf32")
+    _count()
+    if timing:
+        end.record()
+        GEMM_EVENTS.append((start, end, 2.0 * m * n * k, TF32_PRODUCT_COST))
+
+
+def gemm_rs_tf32(a, b, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool, lda: int,
+                 ldb: int, dst_ptrs, ldd: int, rows_per_rank: int, flag_ptrs, done,
+                 epoch: int) -> None:
+    """``gemm_rs`` with one tf32 product of float32 operands."""
+    import ctypes
+
+    world = len(dst_ptrs)
+    if len(flag_ptrs) != world:
+        raise SchemeError("one flag per destination rank")
+    timing = GEMM_EVENTS is not None
+    if timing:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+    dsts = (ctypes.c_void_p * world)(*dst_ptrs)
+    flags = (ctypes.c_void_p * world)(*flag_ptrs)
+    status = lib().mr_gemm_rs_tf32(
+        _ptr(a, torch.float32, "a"), lda, int(a_kmajor), _ptr(b, torch.float32, "b"), ldb,
+        int(b_kmajor), m, n, k, ctypes.cast(dsts, ctypes.c_void_p), ldd, rows_per_rank,
+        ctypes.cast(flags, ctypes.c_void_p), world, _ptr(done, torch.int32, "done", 1), int(epoch),
+        _stream())
+    check(status, "mr_gemm_rs_tf32")
+    _count()
+    if timing:
+        end.record()
+        GEMM_EVENTS.append((start, end, 2.0 * m * n * k, TF32_PRODUCT_COST))
+
+
 def reduce_slots(slots, flags, epoch: int, out) -> None:
     """Wait for every source's flag to reach ``epoch``, then out = sum of the
     ``slots`` (world, ...) in rank order."""
@@ -425,32 +484,40 @@ def _pair(shape, device):
             torch.empty(shape, dtype=torch.bfloat16, device=device))
 
 
-def rmsnorm_split(x, w, eps: float):
-    """x (T, h) float32, w (h,) bf16 -> (hi, lo, rstd)."""
+def _t32(shape, device, want: bool):
+    return torch.empty(shape, dtype=torch.float32, device=device) if want else None
+
+
+def rmsnorm_split(x, w, eps: float, *, t32: bool = False):
+    """x (T, h) float32, w (h,) bf16 -> (hi, lo, rstd, tf32 copy or None)."""
     t, h = x.shape
     hi, lo = _pair((t, h), x.device)
+    tt = _t32((t, h), x.device, t32)
     rstd = torch.empty(t, dtype=torch.float32, device=x.device)
     st = lib().mr_rmsnorm_split(_ptr(x, torch.float32, "x"), _ptr(w, torch.bfloat16, "w", h), t, h,
-                                eps, hi.data_ptr(), lo.data_ptr(), rstd.data_ptr(), _stream())
+                                eps, hi.data_ptr(), lo.data_ptr(),
+                                _ptr(tt, torch.float32, "t32", t * h), rstd.data_ptr(), _stream())
     check(st, "mr_rmsnorm_split")
     _count()
-    return hi, lo, rstd
+    return hi, lo, rstd, tt
 
 
-def rmsnorm_bwd_split(dy, x, w, rstd, resid, *, split: bool = True, out=None):
+def rmsnorm_bwd_split(dy, x, w, rstd, resid, *, split: bool = True, t32: bool = False, out=None):
     """RMSNorm backward plus ``resid`` (or None): ``(hi, lo)`` when ``split``,
-    and the float32 gradient written to ``out`` when given.  Returns (hi, lo)
-    or (None, None)."""
+    the tf32-rounded copy when ``t32``, and the float32 gradient written to
+    ``out`` when given.  Returns (hi, lo, t32) with None for what was not asked."""
     t, h = x.shape
     hi, lo = _pair((t, h), x.device) if split else (None, None)
+    tt = _t32((t, h), x.device, t32)
     st = lib().mr_rmsnorm_bwd_split(
         _ptr(dy, torch.float32, "dy", t * h), _ptr(x, torch.float32, "x"),
         _ptr(w, torch.bfloat16, "w", h), _ptr(rstd, torch.float32, "rstd", t),
         _ptr(resid, torch.float32, "resid", t * h), t, h, None if hi is None else hi.data_ptr(),
-        None if lo is None else lo.data_ptr(), _ptr(out, torch.float32, "out", t * h), _stream())
+        None if lo is None else lo.data_ptr(), _ptr(tt, torch.float32, "t32", t * h),
+        _ptr(out, torch.float32, "out", t * h), _stream())
     check(st, "mr_rmsnorm_bwd_split")
     _count()
-    return hi, lo
+    return hi, lo, tt
 
 
 def rope_split(qkv, cos, sin, b: int, s: int, hq: int, hkv: int, d: int):
@@ -468,44 +535,71 @@ def rope_split(qkv, cos, sin, b: int, s: int, hq: int, hkv: int, d: int):
     return q, k, v
 
 
-def rope_bwd_split(dq, dk, dv, cos, sin, b: int, s: int, hq: int, hkv: int, d: int):
-    hi, lo = _pair((b * s, (hq + 2 * hkv) * d), dq.device)
+def rope_bwd_split(dq, dk, dv, cos, sin, b: int, s: int, hq: int, hkv: int, d: int, *,
+                   split: bool = True, t32: bool = False):
+    """The qkv-row gradient as (hi, lo, tf32 copy), None for what was not asked."""
+    shape = (b * s, (hq + 2 * hkv) * d)
+    hi, lo = _pair(shape, dq.device) if split else (None, None)
+    tt = _t32(shape, dq.device, t32)
     st = lib().mr_rope_bwd_split(_ptr(dq, torch.float32, "dq"), _ptr(dk, torch.float32, "dk"),
                                  _ptr(dv, torch.float32, "dv"), _ptr(cos, torch.float32, "cos"),
-                                 _ptr(sin, torch.float32, "sin"), b, s, hq, hkv, d, hi.data_ptr(),
-                                 lo.data_ptr(), _stream())
+                                 _ptr(sin, torch.float32, "sin"), b, s, hq, hkv, d,
+                                 None if hi is None else hi.data_ptr(),
+                                 None if lo is None else lo.data_ptr(),
+                                 _ptr(tt, torch.float32, "t32", shape[0] * shape[1]), _stream())
     check(st, "mr_rope_bwd_split")
     _count()
-    return hi, lo
+    return hi, lo, tt
 
 
-def heads_split(src, b: int, s: int, h: int, d: int, *, merge: bool):
+def heads_split(src, b: int, s: int, h: int, d: int, *, merge: bool, t32: bool = False):
+    """Head layout change as (hi, lo, tf32 copy or None)."""
     shape = (b * s, h * d) if merge else (b, h, s, d)
     hi, lo = _pair(shape, src.device)
+    tt = _t32(shape, src.device, t32)
     st = lib().mr_heads_split(_ptr(src, torch.float32, "src", b * s * h * d), b, s, h, d, int(merge),
-                              hi.data_ptr(), lo.data_ptr(), _stream())
+                              hi.data_ptr(), lo.data_ptr(),
+                              _ptr(tt, torch.float32, "t32", b * s * h * d), _stream())
     check(st, "mr_heads_split")
     _count()
-    return hi, lo
+    return hi, lo, tt
 
 
-def swiglu_split(gu, t: int, i: int):
+def swiglu_split(gu, t: int, i: int, *, t32: bool = False):
+    """silu(g) * u as (hi, lo, tf32 copy or None)."""
     hi, lo = _pair((t, i), gu.device)
+    tt = _t32((t, i), gu.device, t32)
     st = lib().mr_swiglu_split(_ptr(gu, torch.float32, "gu", t * 2 * i), t, i, hi.data_ptr(),
-                               lo.data_ptr(), _stream())
+                               lo.data_ptr(), _ptr(tt, torch.float32, "t32", t * i), _stream())
     check(st, "mr_swiglu_split")
     _count()
-    return hi, lo
+    return hi, lo, tt
 
 
-def swiglu_bwd_split(dact, gu, t: int, i: int):
-    hi, lo = _pair((t, 2 * i), gu.device)
+def swiglu_bwd_split(dact, gu, t: int, i: int, *, split: bool = True, t32: bool = False):
+    """The gate|up gradient as (hi, lo, tf32 copy), None for what was not asked."""
+    hi, lo = _pair((t, 2 * i), gu.device) if split else (None, None)
+    tt = _t32((t, 2 * i), gu.device, t32)
     st = lib().mr_swiglu_bwd_split(_ptr(dact, torch.float32, "dact", t * i),
-                                   _ptr(gu, torch.float32, "gu", t * 2 * i), t, i, hi.data_ptr(),
-                                   lo.data_ptr(), _stream())
+                                   _ptr(gu, torch.float32, "gu", t * 2 * i), t, i,
+                                   None if hi is None else hi.data_ptr(),
+                                   None if lo is None else lo.data_ptr(),
+                                   _ptr(tt, torch.float32, "t32", t * 2 * i), _stream())
     check(st, "mr_swiglu_bwd_split")
     _count()
-    return hi, lo
+    return hi, lo, tt
+
+
+def round_tf32(x, out=None):
+    """float32 -> its tf32 rounding (round to nearest, ties away), float32."""
+    n = x.numel()
+    if out is None:
+        out = torch.empty_like(x)
+    st = lib().mr_round_tf32(_ptr(x, torch.float32, "x"), n, _ptr(out, torch.float32, "out", n),
+                             _stream())
+    check(st, "mr_round_tf32")
+    _count()
+    return out
 
 
 def softmax_causal_split(scores, rows: int, s: int, scale: float, band: bool = False):

@@ -40,7 +40,7 @@ from mround_b200.pipeline.arch import Arch
 from mround_b200.pipeline.attention import attention
 from mround_b200.pipeline.model import BlockParams
 
-__all__ = ["FusedLinear", "DeviceBlock", "Precision", "FUSION"]
+__all__ = ["FusedLinear", "DeviceBlock", "Precision", "FUSION", "TF32", "TUNING_PRECISION"]
 
 # fused GEMM groups: name -> member linears (row order)
 FUSION: dict[str, tuple[str, ...]] = {
@@ -51,13 +51,35 @@ FUSION: dict[str, tuple[str, ...]] = {
 }
 
 
+# Precision code of one tf32 product (float32 operands rounded to tf32).
+TF32 = 4
+
+
 @dataclasses.dataclass(frozen=True)
 class Precision:
-    """Products per GEMM role: 3 = float32-faithful split, 1 = plain bf16."""
+    """Tensor-core form per GEMM role: 1-3 bf16 products (3 = the
+    float32-faithful hi/lo split, 1 = plain bf16), or ``TF32`` (one tf32
+    product of tf32-rounded float32 operands, 11 significant bits each, at the
+    tensor time of two bf16 products).  The forward stays at 3 in every
+    configuration: the loss is a small difference of two large outputs."""
 
     forward: int = 3
     grad_input: int = 3
     grad_weight: int = 3
+
+    def __post_init__(self) -> None:
+        if self.forward not in (1, 2, 3):
+            raise ValueError(f"forward precision must be 1, 2 or 3, got {self.forward}")
+        for role in (self.grad_input, self.grad_weight):
+            if role not in (1, 2, 3, TF32):
+                raise ValueError(f"gradient precision must be 1, 2, 3 or TF32 ({TF32}), got {role}")
+
+
+# The tuning step's default: the forward as the three-product split, both
+# backward products as one tf32 product each.  Measured at the Qwen2.5-7B
+# block shapes: weight gradients within 3.4e-4 (max-normalised) of float64,
+# against 2.5e-5 with three bf16 products everywhere; the bar is 1e-3.
+TUNING_PRECISION = Precision(3, TF32, TF32)
 
 
 class FusedLinear:
@@ -69,6 +91,8 @@ class FusedLinear:
         bias: float32 (out,) or None (Qwen2 q/k/v carry a bias).
         wq_hi / wq_lo: the operand the forward uses (bf16 hi/lo parts of the
             fake-quantized weight; ``wq_lo`` None means ``wq_hi`` is exact).
+        wq_t32: the same weight rounded to tf32 (float32), the operand of a
+            tf32 input-gradient GEMM, or None.
         grad: float32 (out, in) buffer the weight-gradient GEMM writes, or None.
     """
 
@@ -80,6 +104,7 @@ class FusedLinear:
         self.bias = bias
         self.wq_hi: torch.Tensor = w
         self.wq_lo: torch.Tensor | None = None
+        self.wq_t32: torch.Tensor | None = None  # tf32 operand of the input-gradient GEMM
         self.grad: torch.Tensor | None = None
         self.accumulate_grad = False
         self.grad_ready: list = []  # callbacks run right after this layer's weight gradient
@@ -96,7 +121,17 @@ class FusedLinear:
 
     def use_dense(self) -> None:
         self.ready()
-        self.wq_hi, self.wq_lo = self.w, None
+        self.wq_hi, self.wq_lo, self.wq_t32 = self.w, None, None
+
+    def operand_t32(self) -> torch.Tensor:
+        """The weight operand as tf32 values.  A bf16 weight (dense or
+        committed) is exact in tf32 and is widened once; a tunable weight's
+        copy is kept current by K1/K2."""
+        if self.wq_t32 is None:
+            if self.wq_lo is not None:
+                raise RuntimeError(f"{self.name}: no tf32 operand of the fake-quantized weight")
+            self.wq_t32 = self.wq_hi.float()
+        return self.wq_t32
 
     def ready(self) -> None:
         """Order the current stream after the collectives still writing the operands."""
@@ -114,6 +149,8 @@ class _LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, anchor, layer: FusedLinear, prec: Precision):
+        if TF32 in (prec.grad_input, prec.grad_weight):
+            raise ValueError("the autograd form of the block runs bf16 products only")
         layer.ready()
         lead = x.shape[:-1]
         x2 = x.reshape(-1, layer.in_features)
@@ -269,6 +306,8 @@ def _bmm(a, b, c, *, m, n, k, batch, a_kmajor, b_kmajor, lda, ldb, sa, sb, sc, c
 
 
 def _wprec(layer: FusedLinear, want: int) -> int:
+    if want == TF32:
+        return TF32
     return want if layer.wq_lo is not None else min(want, 2)
 
 
@@ -276,7 +315,10 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
                    collect: dict[str, torch.Tensor] | None = None):
     """Block forward.  ``collect`` maps fused-layer names to float32 (in_features,)
     accumulators: each receives the summed squared input its GEMM sees (the
-    importance statistics of the searched scale)."""
+    importance statistics of the searched scale).  With ``save`` and a tf32
+    weight-gradient precision, the linears' inputs are also kept as tf32
+    copies (the weight-gradient GEMMs' B operands), written by the same
+    element-wise kernels."""
     a = self.arch
 
     def stats(name, op):
@@ -288,9 +330,11 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     hq, hkv, d, inter = a.heads, a.kv_heads, a.head_dim, a.intermediate
     rep, nb = hq // hkv, b * hkv
     scale = 1.0 / math.sqrt(d)
+    t32 = save and prec.grad_weight == TF32
     x2 = x.reshape(t, h)
     L = self.layers
-    h1 = kernels.rmsnorm_split(x2, self.input_norm, a.rms_eps)
+    h1_hi, h1_lo, rstd1, h1_t = kernels.rmsnorm_split(x2, self.input_norm, a.rms_eps, t32=t32)
+    h1 = (h1_hi, h1_lo, h1_t)
     qkv_l = L["qkv"]
     stats("qkv", h1)
     L["qkv"].ready()
@@ -311,7 +355,7 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     o = torch.empty((b, hq, s, d), dtype=torch.float32, device=x.device)
     _bmm(probs, v, o, m=rep * s, n=d, k=s, batch=nb, a_kmajor=True, b_kmajor=False, lda=s, ldb=d,
          sa=rep * s * s, sb=s * d, sc=rep * s * d, causal=c2, seq=s)
-    att = kernels.heads_split(o, b, s, hq, d, merge=True)
+    att = kernels.heads_split(o, b, s, hq, d, merge=True, t32=t32)
     del o
     o_l = L["o"]
     stats("o", att)
@@ -319,14 +363,14 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
     hres = x2.clone()
     _mm(att, (o_l.wq_hi, o_l.wq_lo), hres, m=t, n=h, k=hq * d, a_kmajor=True, b_kmajor=True,
         lda=hq * d, ldb=hq * d, prec=_wprec(o_l, prec.forward), accumulate=True)
-    h2_hi, h2_lo, rstd2 = kernels.rmsnorm_split(hres, self.post_norm, a.rms_eps)
+    h2_hi, h2_lo, rstd2, h2_t = kernels.rmsnorm_split(hres, self.post_norm, a.rms_eps, t32=t32)
     gu_l = L["gate_up"]
     stats("gate_up", (h2_hi, h2_lo))
     gu_l.ready()
     gu = torch.empty((t, 2 * inter), dtype=torch.float32, device=x.device)
     _mm((h2_hi, h2_lo), (gu_l.wq_hi, gu_l.wq_lo), gu, m=t, n=2 * inter, k=h, a_kmajor=True,
         b_kmajor=True, lda=h, ldb=h, prec=_wprec(gu_l, prec.forward))
-    act = kernels.swiglu_split(gu, t, inter)
+    act = kernels.swiglu_split(gu, t, inter, t32=t32)
     dn_l = L["down"]
     stats("down", act)
     dn_l.ready()
@@ -335,9 +379,8 @@ def _fused_forward(self: DeviceBlock, x: torch.Tensor, prec: Precision, save: bo
         lda=inter, ldb=inter, prec=_wprec(dn_l, prec.forward), accumulate=True)
     saved = None
     if save:
-        saved = dict(shape=(b, s, h), h1=(h1[0], h1[1]), q=q, k=k, v=v, probs=probs,
-                     att=att, hres=hres, rstd2=rstd2, h2=(h2_hi, h2_lo), gu=gu, act=act,
-                     x=x2, rstd1=h1[2])
+        saved = dict(shape=(b, s, h), h1=h1, q=q, k=k, v=v, probs=probs, att=att, hres=hres,
+                     rstd2=rstd2, h2=(h2_hi, h2_lo, h2_t), gu=gu, act=act, x=x2, rstd1=rstd1)
     return out.view(b, s, h), saved
 
 
@@ -346,7 +389,11 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     """Weight gradients of every fused linear that has a ``grad`` buffer, and,
     with ``want_dx``, the gradient of the block input (float32, the shape of
     ``dout``) -- the whole-model backward of the DeltaLoss scoring needs it;
-    the tuning step does not."""
+    the tuning step does not.
+
+    Every gradient operand of a linear's GEMMs is produced as an operand
+    triple (hi, lo, t32): the bf16 split when a bf16 product reads it, the
+    tf32-rounded copy when a tf32 product does."""
     a = self.arch
     b, s, h = saved["shape"]
     t = b * s
@@ -354,50 +401,69 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
     rep, nb = hq // hkv, b * hkv
     scale = 1.0 / math.sqrt(d)
     L = self.layers
+    tf_w, tf_x = prec.grad_weight == TF32, prec.grad_input == TF32
+    need_t32 = tf_w or tf_x
+    need_split = not (tf_w and tf_x)
     dout2 = dout.reshape(t, h)
-    g_out = kernels.split_bf16(dout2)
+    g_out = (*(kernels.split_bf16(dout2) if need_split else (None, None)),
+             kernels.round_tf32(dout2) if need_t32 else None)
 
     def weight_grad(layer, dy, x_in, n_out, n_in):
         if layer.grad is None:
             return
         ex = layer.exchange
+        # dW[o, i] = sum_t dy[t, o] x[t, i]: both operands M/N-major
+        kw = dict(m=n_out, n=n_in, k=t, a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in)
         if ex is not None and ex.active and not layer.accumulate_grad and ex.copy_engine:
             # the whole gradient locally, then the copy engines move each
             # owner's rows over NVLink while the backward goes on
-            kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, m=n_out, n=n_in, k=t,
-                         a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in,
-                         precision=prec.grad_weight)
+            if tf_w:
+                kernels.gemm_tf32(dy[2], x_in[2], layer.grad, ldc=n_in, **kw)
+            else:
+                kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, ldc=n_in,
+                             precision=prec.grad_weight, **kw)
             ex.send(layer.grad)
         elif ex is not None and ex.active and not layer.accumulate_grad:
             # rows go straight to their owner ranks over NVLink
-            kernels.gemm_rs(dy[0], dy[1], x_in[0], x_in[1], m=n_out, n=n_in, k=t, a_kmajor=False,
-                            b_kmajor=False, lda=n_out, ldb=n_in, precision=prec.grad_weight,
-                            dst_ptrs=ex.dst_ptrs, ldd=n_in, rows_per_rank=ex.rows_per_rank,
-                            flag_ptrs=ex.flag_ptrs, done=ex.done, epoch=ex.epoch)
+            rs = dict(dst_ptrs=ex.dst_ptrs, ldd=n_in, rows_per_rank=ex.rows_per_rank,
+                      flag_ptrs=ex.flag_ptrs, done=ex.done, epoch=ex.epoch)
+            if tf_w:
+                kernels.gemm_rs_tf32(dy[2], x_in[2], **kw, **rs)
+            else:
+                kernels.gemm_rs(dy[0], dy[1], x_in[0], x_in[1], precision=prec.grad_weight,
+                                **kw, **rs)
+        elif tf_w:
+            kernels.gemm_tf32(dy[2], x_in[2], layer.grad, ldc=n_in,
+                              accumulate=layer.accumulate_grad, **kw)
         else:
-            kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, m=n_out, n=n_in, k=t,
-                         a_kmajor=False, b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in,
-                         precision=prec.grad_weight, accumulate=layer.accumulate_grad)
+            kernels.gemm(dy[0], dy[1], x_in[0], x_in[1], layer.grad, ldc=n_in,
+                         precision=prec.grad_weight, accumulate=layer.accumulate_grad, **kw)
         for hook in layer.grad_ready:
             hook(layer)
 
     def input_grad(layer, dy, n_out, n_in):
+        # dx[t, i] = sum_o dy[t, o] W[o, i]: B is N-major
         out = torch.empty((t, n_in), dtype=torch.float32, device=dout.device)
-        _mm(dy, (layer.wq_hi, layer.wq_lo), out, m=t, n=n_in, k=n_out, a_kmajor=True,
-            b_kmajor=False, lda=n_out, ldb=n_in, prec=_wprec(layer, prec.grad_input))
+        if tf_x:
+            kernels.gemm_tf32(dy[2], layer.operand_t32(), out, m=t, n=n_in, k=n_out, a_kmajor=True,
+                              b_kmajor=False, lda=n_out, ldb=n_in, ldc=n_in)
+        else:
+            _mm(dy, (layer.wq_hi, layer.wq_lo), out, m=t, n=n_in, k=n_out, a_kmajor=True,
+                b_kmajor=False, lda=n_out, ldb=n_in, prec=_wprec(layer, prec.grad_input))
         return out
 
     dn_l, gu_l, o_l, qkv_l = L["down"], L["gate_up"], L["o"], L["qkv"]
     weight_grad(dn_l, g_out, saved["act"], h, inter)
     dact = input_grad(dn_l, g_out, h, inter)
-    g_gu = kernels.swiglu_bwd_split(dact, saved["gu"], t, inter)
+    del g_out
+    g_gu = kernels.swiglu_bwd_split(dact, saved["gu"], t, inter, split=need_split, t32=need_t32)
     del dact
     weight_grad(gu_l, g_gu, saved["h2"], 2 * inter, h)
     dh2 = input_grad(gu_l, g_gu, 2 * inter, h)
     del g_gu
     g_h_f32 = torch.empty_like(dout2) if want_dx else None
     g_h = kernels.rmsnorm_bwd_split(dh2, saved["hres"], self.post_norm, saved["rstd2"], dout2,
-                                    out=g_h_f32)
+                                    split=need_split, t32=need_t32, out=g_h_f32)
     del dh2
     weight_grad(o_l, g_h, saved["att"], h, hq * d)
     datt = input_grad(o_l, g_h, h, hq * d)
@@ -422,7 +488,8 @@ def _fused_backward(self: DeviceBlock, saved: dict, dout: torch.Tensor, prec: Pr
          ldb=d, sa=rep * s * s, sb=rep * s * d, sc=s * d, causal=c3, seq=s)
     del g_s
     cos, sin = self._tables(s)
-    g_qkv = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)
+    g_qkv = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d, split=need_split,
+                                   t32=need_t32)
     del dq, dk, dv
     weight_grad(qkv_l, g_qkv, saved["h1"], qkv_l.out_features, h)
     if not want_dx:

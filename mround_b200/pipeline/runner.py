@@ -28,7 +28,7 @@ from typing import Any
 import torch
 
 from mround_b200.exceptions import ArchitectureError, CalibrationError, ResumeError
-from mround_b200.pipeline.block import DeviceBlock, Precision
+from mround_b200.pipeline.block import TUNING_PRECISION, DeviceBlock, Precision
 from mround_b200.pipeline.dist import DistContext
 from mround_b200.pipeline.model import SyntheticModel
 from mround_b200.pipeline.resume import ResumeStore
@@ -199,7 +199,7 @@ class QuantizationRunner:
         self.quantized_inputs = quantized_inputs
         self.holdout_batches = holdout_batches
         self.per_layer_recipe = per_layer_recipe
-        self.precision = precision or Precision()
+        self.precision = precision or TUNING_PRECISION
         self.dist = dist or DistContext()
         self.device = torch.device(device or "cuda")
         self.keep_codes = keep_codes

@@ -177,7 +177,7 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
             x, saved = blk.forward_fused(x, prec, True)
             saved_all.append(saved)
         x2 = x.reshape(b * sp, hidden)
-        n_hi, n_lo, rstd_f = kernels.rmsnorm_split(x2, final_norm, arch.rms_eps)
+        n_hi, n_lo, rstd_f, _ = kernels.rmsnorm_split(x2, final_norm, arch.rms_eps)
         t = b * s
         real = n_hi.view(b, sp, hidden)[:, :s].reshape(t, hidden), \
             n_lo.view(b, sp, hidden)[:, :s].reshape(t, hidden)

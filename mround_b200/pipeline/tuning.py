@@ -30,7 +30,7 @@ import torch
 from mround_b200 import kernels
 from mround_b200.core.quantizer import require_device_scheme
 from mround_b200.core.scale_search import search_scales
-from mround_b200.pipeline.block import DeviceBlock, FusedLinear, Precision
+from mround_b200.pipeline.block import TF32, DeviceBlock, FusedLinear, Precision
 from mround_b200.pipeline.dist import DistContext
 from mround_b200.schemes import QuantScheme, ScaleInit, Symmetry
 
@@ -86,7 +86,10 @@ class TunableLayer:
     ``BlockTuner.search``) and the operand is formed only once it is set.
     """
 
-    def __init__(self, layer: FusedLinear, members: list[Member], eps: float) -> None:
+    def __init__(self, layer: FusedLinear, members: list[Member], eps: float, *,
+                 tf32: bool = False) -> None:
+        """``tf32``: also keep the operand as tf32 values (``layer.wq_t32``),
+        the B operand of a tf32 input-gradient GEMM."""
         self.layer = layer
         self.members = members
         self.eps = eps
@@ -113,6 +116,8 @@ class TunableLayer:
         else:  # rows of untuned members stay exact
             layer.wq_hi = layer.w.clone()
             layer.wq_lo = torch.zeros_like(layer.w)
+        # bf16 weights are exact in tf32: untuned rows keep the weight itself
+        layer.wq_t32 = layer.w.float() if tf32 else None
         layer.grad = torch.empty((out, inn), dtype=torch.float32, device=dev)
         if not self.searched:
             self.requantize()
@@ -134,7 +139,11 @@ class TunableLayer:
             r0, r1 = m.rows
             kernels.fq_forward(w, v, a, b, bits=m.scheme.bits, group=m.group, eps=self.eps,
                                wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1],
-                               **self._scheme_kw(m))
+                               wq_t32=self._t32_rows(r0, r1), **self._scheme_kw(m))
+
+    def _t32_rows(self, r0: int, r1: int):
+        t32 = self.layer.wq_t32
+        return None if t32 is None else t32[r0:r1]
 
     def update(self, step: int, iters: int) -> None:
         """K2 on every member with the linearly decayed rate of this step."""
@@ -146,13 +155,14 @@ class TunableLayer:
             kernels.ste_signsgd(self.layer.grad[r0:r1], w, v, a, b, bits=m.scheme.bits,
                                 group=m.group, eps=self.eps, lr=lr, lo=lo, hi=hi, update=True,
                                 wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1],
-                                **self._scheme_kw(m))
+                                wq_t32=self._t32_rows(r0, r1), **self._scheme_kw(m))
 
     def update_rows(self, step: int, iters: int, s0: int, s1: int, grad: torch.Tensor,
-                    hi: torch.Tensor, lo: torch.Tensor) -> None:
+                    hi: torch.Tensor, lo: torch.Tensor, t32: torch.Tensor | None = None) -> None:
         """K2 on rows [s0, s1) only: ``grad`` holds the summed gradient of those
-        rows, and the next step's operand rows go to ``hi``/``lo`` (this rank's
-        part of the all-gather).  V/alpha/beta of other rows are left as they are."""
+        rows, and the next step's operand rows go to ``hi``/``lo`` (and ``t32``)
+        -- this rank's part of the all-gather.  V/alpha/beta of other rows are
+        left as they are."""
         for m in self.members:
             r0, r1 = max(m.rows[0], s0), min(m.rows[1], s1)
             if r0 >= r1:
@@ -164,6 +174,7 @@ class TunableLayer:
                                 self.alpha[r0:r1], self.beta[r0:r1], bits=m.scheme.bits,
                                 group=m.group, eps=self.eps, lr=lr, lo=lo_b, hi=hi_b, update=True,
                                 wq_hi=hi[r0 - s0:r1 - s0], wq_lo=lo[r0 - s0:r1 - s0],
+                                wq_t32=None if t32 is None else t32[r0 - s0:r1 - s0],
                                 symmetric=self.symmetric, init_scale=init)
 
     def gradients(self) -> dict[str, tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
@@ -220,7 +231,21 @@ class TunableLayer:
                                          (r1 - r0, w.shape[1]),
                                          None if codes is None else codes.cpu())
         self.layer.wq_hi, self.layer.wq_lo, self.layer.grad = committed, None, None
+        self.layer.wq_t32 = None
         return out
+
+
+@dataclasses.dataclass
+class _Shard:
+    """This rank's rows [s0, s1) of a fused weight under the row-sharded update:
+    the summed gradient and the next operands (the all-gather's send buffers)."""
+
+    s0: int
+    s1: int
+    grad: torch.Tensor
+    hi: torch.Tensor
+    lo: torch.Tensor
+    t32: torch.Tensor | None
 
 
 class BlockTuner:
@@ -256,7 +281,8 @@ class BlockTuner:
                     continue
                 members.append(Member(path, (r0, r1), scheme, group, lrs[path]))
             if members:
-                self.tunables.append(TunableLayer(layer, members, eps))
+                self.tunables.append(TunableLayer(layer, members, eps,
+                                                  tf32=precision.grad_input == TF32))
                 if dist.world > 1:
                     layer.grad_ready.append(self._reduce_hook)
         self.ws = kernels.LossWorkspace(block.device)
@@ -270,7 +296,7 @@ class BlockTuner:
                                               for t in self.tunables)
         self._sharded_step = False
         self._dirty = False  # V/alpha/beta rows of other ranks are stale
-        self._shards: dict[int, tuple[int, int, torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+        self._shards: dict[int, _Shard] = {}
         if self.sharded:
             for t in self.tunables:
                 out, inn = t.layer.w.shape
@@ -278,8 +304,10 @@ class BlockTuner:
                 s0, s1 = dist.rank * per, (dist.rank + 1) * per
                 grad = torch.empty((per, inn), dtype=torch.float32, device=block.device)
                 # untuned rows of a partly tuned fused weight keep their exact operand
-                self._shards[id(t.layer)] = (s0, s1, grad, t.layer.wq_hi[s0:s1].clone(),
-                                             t.layer.wq_lo[s0:s1].clone())
+                t32 = t.layer.wq_t32
+                self._shards[id(t.layer)] = _Shard(
+                    s0, s1, grad, t.layer.wq_hi[s0:s1].clone(), t.layer.wq_lo[s0:s1].clone(),
+                    None if t32 is None else t32[s0:s1].clone())
         # Fused GEMM -> reduce-scatter over NVLink peer memory (one piece per
         # step; at most 8 ranks; every rank agrees before it is used).
         self.peer = None
@@ -313,7 +341,7 @@ class BlockTuner:
         collect = {}
         for t in self.tunables:
             layer = t.layer
-            stash[layer.name] = (layer.wq_hi, layer.wq_lo)
+            stash[layer.name] = (layer.wq_hi, layer.wq_lo, layer.wq_t32)
             layer.use_dense()
         for t in searching:
             collect[t.layer.name] = torch.zeros(t.layer.in_features, dtype=torch.float32,
@@ -324,7 +352,7 @@ class BlockTuner:
                     self.block.forward_fused(x, self.precision, False, collect)
         finally:
             for t in self.tunables:
-                t.layer.wq_hi, t.layer.wq_lo = stash[t.layer.name]
+                t.layer.wq_hi, t.layer.wq_lo, t.layer.wq_t32 = stash[t.layer.name]
         for name in sorted(collect):
             self.dist.all_reduce_(collect[name])
         self.importance = collect
@@ -344,7 +372,7 @@ class BlockTuner:
         if layer.exchange is not None and layer.exchange.active:
             return  # the GEMM has already stored the rows with their owners
         if self._sharded_step:
-            _, _, grad, _, _ = self._shards[id(layer)]
+            grad = self._shards[id(layer)].grad
             self._pending[id(layer)] = self.dist.reduce_scatter_async(grad, layer.grad)
         else:
             self._pending[id(layer)] = self.dist.all_reduce_async(layer.grad)
@@ -366,18 +394,20 @@ class BlockTuner:
         # rows of this rank, then the operands' all-gather; qkv first, so the
         # next forward's first GEMM waits on the smallest gather only
         for t in self.tunables:
-            s0, s1, grad, hi, lo = self._shards[id(t.layer)]
+            sh = self._shards[id(t.layer)]
             ex = t.layer.exchange
             if ex is not None and ex.active:
                 # every source's rows are in this rank's slots once its flag
                 # carries this step's epoch; sum them in rank order
-                kernels.reduce_slots(ex.slots, ex.flags, ex.epoch, grad)
+                kernels.reduce_slots(ex.slots, ex.flags, ex.epoch, sh.grad)
                 ex.active = False
             else:
                 self._wait(t.layer)
-            t.update_rows(step, iters, s0, s1, grad, hi, lo)
-            t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_hi, hi))
-            t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_lo, lo))
+            t.update_rows(step, iters, sh.s0, sh.s1, sh.grad, sh.hi, sh.lo, sh.t32)
+            t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_hi, sh.hi))
+            t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_lo, sh.lo))
+            if sh.t32 is not None:
+                t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_t32, sh.t32))
         self._dirty = True
 
     def sync_params(self) -> None:
@@ -386,7 +416,7 @@ class BlockTuner:
             return
         for t in self.tunables:
             t.layer.ready()
-            s0, s1, _, _, _ = self._shards[id(t.layer)]
+            s0, s1 = self._shards[id(t.layer)].s0, self._shards[id(t.layer)].s1
             works = [self.dist.all_gather_async(buf, buf[s0:s1].clone())
                      for buf in (t.v, t.alpha, t.beta)]
             for w in works:

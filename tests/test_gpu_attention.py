@@ -107,7 +107,7 @@ def test_rope_and_head_layout_kernels_match_float64(b, s, hq, hkv, d):
     dq = torch.randn(b, hq, s, d, device="cuda", generator=g)
     dk = torch.randn(b, hkv, s, d, device="cuda", generator=g)
     dv = torch.randn(b, hkv, s, d, device="cuda", generator=g)
-    hi, lo = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)
+    hi, lo, _ = kernels.rope_bwd_split(dq, dk, dv, cos, sin, b, s, hq, hkv, d)
     dd = torch.cat([dq, dk, dv], 1).double()  # (b, h, s, d)
     g1 = dd[..., :half] * c + dd[..., half:] * sn
     g2 = dd[..., half:] * c - dd[..., :half] * sn
@@ -119,13 +119,13 @@ def test_rope_and_head_layout_kernels_match_float64(b, s, hq, hkv, d):
 
     if d % 4 == 0:
         heads = torch.randn(b, h, s, d, device="cuda", generator=g)
-        mh, ml = kernels.heads_split(heads, b, s, h, d, merge=True)
+        mh, ml, _ = kernels.heads_split(heads, b, s, h, d, merge=True)
         ref = heads.permute(0, 2, 1, 3).reshape(b * s, h * d)
         assert torch.equal(mh.float() + ml.float(), (ref.to(torch.bfloat16).float()
                                                       + (ref - ref.to(torch.bfloat16).float())
                                                       .to(torch.bfloat16).float()))
         rows = torch.randn(b * s, h * d, device="cuda", generator=g)
-        sh, sl = kernels.heads_split(rows, b, s, h, d, merge=False)
+        sh, sl, _ = kernels.heads_split(rows, b, s, h, d, merge=False)
         ref = rows.view(b, s, h, d).permute(0, 2, 1, 3)
         assert torch.equal(sh.float() + sl.float(), (ref.to(torch.bfloat16).float()
                                                       + (ref - ref.to(torch.bfloat16).float())

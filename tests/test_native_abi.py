@@ -52,7 +52,7 @@ def test_argument_errors_are_refused_before_any_launch():
     lib = _native.lib()
     # group 12 is not a device group: refused on the host side of the ABI
     st = lib.mr_fq_forward(None, None, None, None, 4, 48, 12, 2, 0, None, 1e-8, None, None, None,
-                           None, None, None)
+                           None, None, None, None)
     assert st == -1
     st = lib.mr_pack_mlx(None, None, None, None, 4, 64, 64, 9, 0, None, 1e-8, None, None, None,
                          None, None)
@@ -61,10 +61,36 @@ def test_argument_errors_are_refused_before_any_launch():
     buf = (ctypes.c_uint8 * 4096)()
     p = ctypes.addressof(buf)
     st = lib.mr_fq_forward(p, p, p, p, 4, 64, 64, 2, 0, p, 1e-8, None, None, None, None, None,
-                           None)
+                           None, None)
     assert st == -1
     cands = (ctypes.c_float * 1)(2.0)
     st = lib.mr_scale_search(p, 4, 64, 12, 2, cands, 1, None, p, None)
     assert st == -1
     st = lib.mr_scale_search(p, 4, 64, 64, 2, cands, 0, None, p, None)
     assert st == -1
+
+
+def test_selection_refuses_inputs_beyond_its_32bit_counters():
+    """Every K4 entry point that selects a threshold refuses n >= 2^32 before
+    touching a pointer (the histogram bins count in 32 bits); the pointers
+    here are never dereferenced."""
+    lib = _native.lib()
+    fake = 1 << 12  # aligned, non-null stand-ins
+    n = 1 << 33
+    assert lib.mr_loss_outlier(fake, fake, n, 1, 1, float(n), -1.0, None, fake, None, fake,
+                               None) == -1
+    assert lib.mr_loss_hist_pass(fake, fake, n, 0, None, fake, None) == -1
+    assert lib.mr_loss_outlier_noalloc(fake, fake, n, 1, 1, float(n), -1.0, None, fake, None,
+                                       None) == -1
+
+
+def test_gemm_entry_points_refuse_bad_precision_and_alignment():
+    """The bf16 GEMM entry points take products 1-3 only (tf32 has its own
+    entry points); float32 operands need leading dimensions in 16-byte units.
+    Refused on the host, before any launch."""
+    lib = _native.lib()
+    p = 1 << 12
+    assert lib.mr_gemm(p, p, 64, 1, p, p, 64, 1, p, 64, None, 0, 128, 128, 64, 4, None) == -1
+    assert lib.mr_gemm(p, p, 64, 1, p, p, 64, 1, p, 64, None, 0, 128, 128, 64, 0, None) == -1
+    assert lib.mr_gemm_tf32(p, 66, 1, p, 64, 1, p, 64, None, 0, 128, 128, 64, None) == -2
+    assert lib.mr_gemm_tf32(None, 64, 1, p, 64, 1, p, 64, None, 0, 128, 128, 64, None) == -1

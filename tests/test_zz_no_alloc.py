@@ -19,17 +19,18 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _call_workspace(lib, pred, tgt, grad, loss, thr, ws, k, suppress):
+def _call_workspace(lib, pred, tgt, grad, loss, thr, ws, k, suppress, thr_in):
     n = pred.numel()
-    st = lib.mr_loss_outlier(pred.data_ptr(), tgt.data_ptr(), n, k, int(suppress), float(n), -1.0,
-                             grad.data_ptr(), loss.data_ptr(), thr.data_ptr(), ws.data_ptr(), None)
+    st = lib.mr_loss_outlier(pred.data_ptr(), tgt.data_ptr(), n, k, int(suppress), float(n),
+                             thr_in, grad.data_ptr(), loss.data_ptr(), thr.data_ptr(),
+                             ws.data_ptr(), None)
     assert st == 0
 
 
-def _call_noalloc(lib, pred, tgt, grad, loss, thr, k, suppress):
+def _call_noalloc(lib, pred, tgt, grad, loss, thr, k, suppress, thr_in):
     n = pred.numel()
     st = lib.mr_loss_outlier_noalloc(pred.data_ptr(), tgt.data_ptr(), n, k, int(suppress),
-                                     float(n), -1.0, grad.data_ptr(), loss.data_ptr(),
+                                     float(n), thr_in, grad.data_ptr(), loss.data_ptr(),
                                      thr.data_ptr(), None)
     assert st == 0
 
@@ -44,24 +45,28 @@ def test_noalloc_loss_matches_workspace_entry_point_twice():
     torch.cuda.synchronize()
     ws = torch.zeros(int(lib.mr_loss_workspace_bytes()), dtype=torch.uint8, device="cuda")
     g = torch.Generator(device="cuda").manual_seed(7)
-    cases = [((3, 129, 96), True), ((8, 64, 576), True), ((2, 16, 64), False)]
-    for shape, suppress in cases[:2] + cases[2:]:
+    # (shape, suppress, caller threshold): the selected threshold on two sizes,
+    # plain MSE, an element count that is not a multiple of 4 (the kernels'
+    # scalar tail), and a caller-given threshold that skips the selection
+    cases = [((3, 129, 96), True, -1.0), ((8, 64, 576), True, -1.0), ((2, 16, 64), False, -1.0),
+             ((3, 7, 13), False, -1.0), ((5, 11, 9), True, -1.0), ((4, 33, 64), True, 0.07)]
+    for shape, suppress, thr_in in cases:
         pred = torch.randn(shape, device="cuda", generator=g)
         tgt = pred + 0.05 * torch.randn(shape, device="cuda", generator=g)
         n = pred.numel()
         k = max(1, int(n * 0.001))
         want = [torch.empty_like(pred), torch.zeros((), dtype=torch.float64, device="cuda"),
                 torch.zeros((), device="cuda")]
-        _call_workspace(lib, pred, tgt, *want, ws, k, suppress)
+        _call_workspace(lib, pred, tgt, *want, ws, k, suppress, thr_in)
         for _ in range(2):  # two calls in a row share (and overwrite) the static scratch
             got = [torch.full_like(pred, float("nan")),
                    torch.zeros((), dtype=torch.float64, device="cuda"),
                    torch.zeros((), device="cuda")]
-            _call_noalloc(lib, pred, tgt, *got, k, suppress)
+            _call_noalloc(lib, pred, tgt, *got, k, suppress, thr_in)
             torch.cuda.synchronize()
             assert got[1].item() == pytest.approx(want[1].item(), rel=1e-12)
             assert torch.equal(got[0], want[0])
-            if suppress:
+            if suppress and thr_in < 0:
                 assert got[2].item() == want[2].item()
 
 
