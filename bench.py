@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "copy", "nccl"],
                     help="weight-gradient exchange at N > 1 (default: fused GEMM peer stores)")
+    ap.add_argument("--precision", default="tuning", choices=["tuning", "bf16x3"],
+                    help="tuning: the runner's default (tf32 backward GEMMs); bf16x3: three "
+                         "bf16 products in every GEMM")
     return ap.parse_args()
 
 
@@ -200,9 +203,12 @@ def make_tuner(args, block, dist):
     from mround_b200.pipeline.runner import QuantizationRunner
     from mround_b200.schemes import QuantScheme, TuningConfig
 
+    from mround_b200.pipeline.block import Precision
+
     scheme = QuantScheme(bits=args.bits, group_size=args.group, symmetry="asym")
     runner = QuantizationRunner(scheme, TuningConfig(iters=ITERS), dist=dist,
-                                exchange=args.exchange)
+                                exchange=args.exchange,
+                                precision=Precision() if args.precision == "bf16x3" else None)
     return runner.tuner_for(block, "model.layers.0")
 
 

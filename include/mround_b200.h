@@ -265,6 +265,17 @@ int mr_selftest_division(const float* a, const float* b, int64_t n, unsigned int
 int mr_split_bf16(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, void* stream);
 
 /*
+ * Gradient of the mean shifted cross-entropy in the DeltaLoss scoring
+ * backward (mround/pipeline/scoring.py:183-192, _causal_loss): for each of
+ * `rows` rows of `vocab` float32 logits and its int64 label,
+ *   g = (softmax(logits) - onehot(label)) * scale     (scale = 1 / rows)
+ * written as bf16 hi/lo, the operand of the LM-head input-gradient GEMM.
+ * vocab % 4 == 0; labels in [0, vocab).
+ */
+int mr_ce_grad_split(const float* logits, const int64_t* labels, int64_t rows, int vocab,
+                     float scale, uint16_t* hi, uint16_t* lo, void* stream);
+
+/*
  * Operand preparation for the tf32 GEMM: out = x rounded to tf32 (round to
  * nearest, ties away from zero; the low 13 bits cleared), n elements of
  * float32; out may equal x.

@@ -83,6 +83,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_swiglu_split": (_I, [_P, _I64, _I, _P, _P, _P, _P]),
     "mr_swiglu_bwd_split": (_I, [_P, _P, _I64, _I, _P, _P, _P, _P]),
     "mr_round_tf32": (_I, [_P, _I64, _P, _P]),
+    "mr_ce_grad_split": (_I, [_P, _P, _I64, _I, _F, _P, _P, _P]),
     "mr_softmax_causal_split": (_I, [_P, _I64, _I, _F, _I, _P, _P, _P]),
     "mr_softmax_bwd_split": (_I, [_P, _P, _P, _I64, _I, _F, _I, _P, _P, _P]),
 }

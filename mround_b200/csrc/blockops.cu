@@ -877,3 +877,87 @@ extern "C" int mr_round_tf32(const float* x, int64_t n, float* out, void* stream
                                                                                              out);
   return launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// Cross-entropy gradient of the scoring backward: for each of `rows` logit
+// rows of `vocab` float32 values and its label,
+//   g = (softmax(x) - onehot(label)) * scale
+// written as bf16 hi/lo (the next GEMM's operand).  One block per row: an
+// online max / sum of exponentials over the row (16-byte loads), then a
+// second pass that writes g.  The row is read twice (the second read mostly
+// from L2) and nothing else is materialised.
+namespace mr {
+namespace {
+
+constexpr int kCeThreads = 512;
+
+__device__ __forceinline__ void lse_combine(float& m, float& s, float m2, float s2) {
+  if (m2 > m) {
+    s = s * expf(m - m2) + s2;
+    m = m2;
+  } else if (m2 != -INFINITY) {
+    s += s2 * expf(m2 - m);
+  }
+}
+
+__global__ void __launch_bounds__(kCeThreads) ce_grad_split_kernel(
+    const float* __restrict__ logits, const int64_t* __restrict__ labels, int vocab, float scale,
+    uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
+  __shared__ float sm[kCeThreads / 32], ss[kCeThreads / 32];
+  const int64_t row = blockIdx.x;
+  const float4* x4 = reinterpret_cast<const float4*>(logits + row * vocab);
+  const int n4 = vocab / 4;
+  float m = -INFINITY, s = 0.f;
+  for (int i = threadIdx.x; i < n4; i += kCeThreads) {
+    const float4 v = x4[i];
+    const float mv = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+    if (mv > m) {
+      s *= expf(m - mv);
+      m = mv;
+    }
+    s += expf(v.x - m) + expf(v.y - m) + expf(v.z - m) + expf(v.w - m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    lse_combine(m, s, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o));
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sm[w] = m;
+    ss[w] = s;
+  }
+  __syncthreads();
+  float M = sm[0], S = ss[0];
+  for (int i = 1; i < kCeThreads / 32; ++i) lse_combine(M, S, sm[i], ss[i]);
+  const float inv = 1.f / S;
+  const int64_t label = labels[row];
+  for (int i = threadIdx.x; i < n4; i += kCeThreads) {
+    const float4 v = x4[i];
+    float4 g = make_float4(expf(v.x - M) * inv, expf(v.y - M) * inv, expf(v.z - M) * inv,
+                           expf(v.w - M) * inv);
+    const int64_t c = int64_t(i) * 4;
+    if (label >= c && label < c + 4) {
+      const int j = int(label - c);
+      if (j == 0) g.x -= 1.f;
+      if (j == 1) g.y -= 1.f;
+      if (j == 2) g.z -= 1.f;
+      if (j == 3) g.w -= 1.f;
+    }
+    put_split4(hi, lo, row * vocab + c,
+               make_float4(g.x * scale, g.y * scale, g.z * scale, g.w * scale));
+  }
+}
+
+}  // namespace
+}  // namespace mr
+
+extern "C" int mr_ce_grad_split(const float* logits, const int64_t* labels, int64_t rows,
+                                int vocab, float scale, uint16_t* hi, uint16_t* lo,
+                                void* stream) {
+  if (!logits || !labels || !hi || !lo || rows <= 0 || rows > 0x7fffffff || vocab <= 0 ||
+      vocab % 4)
+    return MR_ERR_ARGUMENT;
+  if (!aligned16(logits) || !aligned8(hi) || !aligned8(lo)) return MR_ERR_ALIGNMENT;
+  ce_grad_split_kernel<<<unsigned(rows), kCeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      logits, labels, vocab, scale, hi, lo);
+  return launch_status();
+}

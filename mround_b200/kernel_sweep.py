@@ -30,6 +30,8 @@ Other modes (measurement drivers of the profiles):
                                 (the driver of a K3 ncu capture);
   --gemm-table TOKENS           every weight GEMM of the 7B step timed as the
                                 bf16 split and as one tf32 product;
+  --gemm-all TOKENS             every weight GEMM in the tuning step's form, two
+                                launches each (the driver of per-shape ncu counters);
   --step STEPS                  tuning steps of a 7B block, the last between
                                 cudaProfilerStart/Stop (a one-step launch list);
   --exchange [--tf32]           the block's weight-gradient exchange, under
@@ -263,6 +265,23 @@ def gemm_probe(name: str, tokens: int, tf32: bool) -> None:
     print(json.dumps({"probe": name, "tokens": tokens, "tf32": tf32}), flush=True)
 
 
+def gemm_all(tokens: int) -> None:
+    """Every weight GEMM of the 7B step in the tuning step's form (forward as
+    the bf16 split, dX and dW as one tf32 product), two launches each in the
+    order of ``gemm_shapes``: under ncu with ``-k regex:gemm_kernel`` the
+    second launch of each pair is the warm one, ``2 * i + 1`` for shape i."""
+    for name, (m, n, k, ak, bk) in gemm_shapes(tokens).items():
+        tf32 = not name.startswith("fwd")
+        aop, bop, a_shape, b_shape = _gemm_operands(m, n, k, ak, bk, tf32, "cuda")
+        c = torch.empty(m, n, device="cuda")
+        for _ in range(2):
+            _launch(aop, bop, c, m, n, k, ak, bk, a_shape, b_shape, tf32)
+        torch.cuda.synchronize()
+        print(json.dumps({"probe": name, "tokens": tokens, "tf32": tf32, "m": m, "n": n, "k": k}),
+              flush=True)
+        del aop, bop, c
+
+
 def gemm_table(tokens: int, reps: int = 5) -> list[dict]:
     """Every weight GEMM of the 7B step, as the three-product bf16 split and
     as one tf32 product: device time (CUDA events, median of ``reps``, after
@@ -441,6 +460,8 @@ def main() -> None:
                     help="launch one 7B weight GEMM three times (ncu driver)")
     ap.add_argument("--gemm-table", type=int, metavar="TOKENS",
                     help="time every 7B weight GEMM as bf16x3 and tf32")
+    ap.add_argument("--gemm-all", type=int, metavar="TOKENS",
+                    help="every 7B weight GEMM in the tuning form, two launches each (ncu driver)")
     ap.add_argument("--tf32", action="store_true", help="--gemm / --exchange: tf32 operands")
     ap.add_argument("--step", type=int, metavar="STEPS",
                     help="7B tuning steps, the last between cudaProfilerStart/Stop")
@@ -453,6 +474,8 @@ def main() -> None:
         gemm_probe(args.gemm[0], int(args.gemm[1]), args.tf32)
     elif args.gemm_table:
         gemm_table(args.gemm_table, args.reps)
+    elif args.gemm_all:
+        gemm_all(args.gemm_all)
     elif args.step:
         step_probe(args.step)
     elif args.exchange:

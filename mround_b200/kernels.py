@@ -590,6 +590,19 @@ def swiglu_bwd_split(dact, gu, t: int, i: int, *, split: bool = True, t32: bool 
     return hi, lo, tt
 
 
+def ce_grad_split(logits, labels, scale: float):
+    """(softmax(logits) - onehot(labels)) * scale per row, as bf16 (hi, lo)."""
+    rows, vocab = logits.shape
+    hi, lo = _pair((rows, vocab), logits.device)
+    if labels.dtype != torch.int64 or not labels.is_contiguous() or labels.numel() != rows:
+        raise SchemeError("labels must be a contiguous int64 tensor of one label per row")
+    st = lib().mr_ce_grad_split(_ptr(logits, torch.float32, "logits"), labels.data_ptr(), rows,
+                                vocab, float(scale), hi.data_ptr(), lo.data_ptr(), _stream())
+    check(st, "mr_ce_grad_split")
+    _count()
+    return hi, lo
+
+
 def round_tf32(x, out=None):
     """float32 -> its tf32 rounding (round to nearest, ties away), float32."""
     n = x.numel()

@@ -185,12 +185,8 @@ def score_widths(model: SyntheticModel, batches: Sequence[np.ndarray], widths: S
         logits = torch.empty((t, vocab), dtype=torch.float32, device=dev)
         kernels.gemm(real[0], real[1], head, None, logits, m=t, n=vocab, k=hidden, a_kmajor=True,
                      b_kmajor=True, lda=hidden, ldb=hidden, ldc=vocab, precision=2)
-        # d(mean CE)/dlogits = (softmax - onehot) / t, formed in place
-        lse = torch.logsumexp(logits, dim=-1, keepdim=True)
-        logits.sub_(lse).exp_()
-        logits[torch.arange(t, device=dev), labels.reshape(-1)] -= 1.0
-        logits.div_(t)
-        g_hi, g_lo = kernels.split_bf16(logits)
+        # d(mean CE)/dlogits = (softmax - onehot) / t, one row-wise kernel
+        g_hi, g_lo = kernels.ce_grad_split(logits, labels.reshape(-1).contiguous(), 1.0 / t)
         del logits
         dh = torch.empty((t, hidden), dtype=torch.float32, device=dev)
         kernels.gemm(g_hi, g_lo, head, None, dh, m=t, n=hidden, k=vocab, a_kmajor=True,

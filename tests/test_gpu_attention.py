@@ -130,3 +130,22 @@ def test_rope_and_head_layout_kernels_match_float64(b, s, hq, hkv, d):
         assert torch.equal(sh.float() + sl.float(), (ref.to(torch.bfloat16).float()
                                                       + (ref - ref.to(torch.bfloat16).float())
                                                       .to(torch.bfloat16).float()))
+
+
+@pytest.mark.parametrize("rows,vocab", [(7, 512), (64, 151936), (3, 49152)])
+def test_ce_grad_split_matches_float64(rows, vocab):
+    """The scoring backward's cross-entropy gradient kernel against a float64
+    softmax minus the one-hot labels, scaled by 1/rows (hi + lo to 2^-15)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from mround_b200 import kernels
+
+    g = torch.Generator(device="cuda").manual_seed(rows)
+    logits = torch.randn(rows, vocab, device="cuda", generator=g) * 4.0
+    labels = torch.randint(0, vocab, (rows,), device="cuda", generator=g)
+    hi, lo = kernels.ce_grad_split(logits, labels, 1.0 / rows)
+    ref = torch.softmax(logits.double(), -1)
+    ref[torch.arange(rows, device="cuda"), labels] -= 1.0
+    ref /= rows
+    got = hi.double() + lo.double()
+    assert (got - ref).abs().max().item() <= 2.0 ** -15 * ref.abs().max().item()

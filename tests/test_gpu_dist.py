@@ -47,19 +47,24 @@ def _setup(device):
     return arch, DeviceBlock(arch, params, device), x, tgt
 
 
-def _tuner(block, dist, exchange="p2p"):
-    from mround_b200.pipeline.block import Precision
+def _precision(name):
+    from mround_b200.pipeline.block import TUNING_PRECISION, Precision
+
+    return Precision() if name == "bf16x3" else TUNING_PRECISION
+
+
+def _tuner(block, dist, exchange="p2p", prec="bf16x3"):
     from mround_b200.pipeline.tuning import BlockTuner
     from mround_b200.schemes import QuantScheme
     from oracle.block_tuner import LINEARS
 
     scheme = QuantScheme(bits=2, group_size=32, symmetry="asym")
     return BlockTuner(block, {p: scheme for p in LINEARS}, {p: 0.05 for p in LINEARS},
-                      suppress=True, eps=1e-8, precision=Precision(), dist=dist,
+                      suppress=True, eps=1e-8, precision=_precision(prec), dist=dist,
                       exchange=exchange)
 
 
-def _rank(rank, world, port, q, exchange="p2p"):
+def _rank(rank, world, port, q, exchange="p2p", prec="bf16x3"):
     import torch.distributed as tdist
 
     from mround_b200.pipeline.dist import DistContext
@@ -75,7 +80,7 @@ def _rank(rank, world, port, q, exchange="p2p"):
         dev = torch.device("cuda", rank)
         _, block, x, tgt = _setup(dev)
         rows = ctx.shard(SHAPE[0])
-        tuner = _tuner(block, ctx, exchange)
+        tuner = _tuner(block, ctx, exchange, prec)
         assert tuner.sharded, "tiny-qwen2's fused rows divide by 2: the row-sharded update runs"
         assert (tuner.peer is not None) == (exchange in ("p2p", "copy"))
         loss = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 0, 10)
@@ -94,11 +99,11 @@ def _rank(rank, world, port, q, exchange="p2p"):
         tdist.destroy_process_group()
 
 
-def _run_ranks(exchange):
+def _run_ranks(exchange, prec="bf16x3"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, exchange)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, exchange, prec)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
@@ -108,14 +113,16 @@ def _run_ranks(exchange):
     return res
 
 
-def test_two_gpu_fused_exchange_equals_nccl_reduce_scatter():
+@pytest.mark.parametrize("prec", ["bf16x3", "tuning"])
+def test_two_gpu_fused_exchange_equals_nccl_reduce_scatter(prec):
     """The weight-gradient GEMM storing rows into their owners' slots over NVLink
     gives the same parameters, bit for bit, as the GEMM plus an NCCL
-    reduce-scatter (two summands: the order cannot differ)."""
+    reduce-scatter (two summands: the order cannot differ) -- with the bf16
+    split and with the tuning default's tf32 products (mr_gemm_rs_tf32)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    fused = _run_ranks("p2p")
-    nccl = _run_ranks("nccl")
+    fused = _run_ranks("p2p", prec)
+    nccl = _run_ranks("nccl", prec)
     for a, b in zip(fused, nccl):
         assert a[1] == b[1] and a[2] == b[2]
         for x, y in zip(a[3] + a[4], b[3] + b[4]):
@@ -136,16 +143,17 @@ def test_two_gpu_copy_engine_exchange_equals_nccl_reduce_scatter():
             assert np.array_equal(x, y)
 
 
-def test_two_gpu_step_matches_single_process():
+@pytest.mark.parametrize("prec", ["bf16x3", "tuning"])
+def test_two_gpu_step_matches_single_process(prec):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from mround_b200.pipeline.dist import DistContext
 
-    res = _run_ranks("p2p")
+    res = _run_ranks("p2p", prec)
     # single process, whole batch, on GPU 0
     dev = torch.device("cuda", 0)
     _, block, x, tgt = _setup(dev)
-    tuner = _tuner(block, DistContext())
+    tuner = _tuner(block, DistContext(), prec=prec)
     loss = tuner.step(x.to(dev), tgt.to(dev), 0, 10)
     loss2 = tuner.step(x.to(dev), tgt.to(dev), 1, 10)
     torch.cuda.synchronize(dev)
