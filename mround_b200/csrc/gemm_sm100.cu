@@ -61,6 +61,9 @@ constexpr int BM = 128;
 // K per stage (BK): 32 (K-major rows of 64 B, SWIZZLE_64B) or 64 (128 B rows,
 // SWIZZLE_128B); MN-major tiles always have 128-byte rows (64 M or N values).
 constexpr int kThreads = 192;
+// K slice of the tf32 GEMM (float32 operands): 32 -- four 48 KB stages at
+// BN = 256, four MMAs per stage, each operand part one TMA instruction.
+constexpr int kTf32BK = 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
 __device__ int g_gemm_status = 0;
@@ -121,6 +124,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Tiled 4-D TMA load (x innermost, w = batch); no multicast.  The chunked
+// operand maps put a 128-byte chunk of the contiguous dimension in x, so one
+// instruction fills a whole operand tile of a stage.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
 
@@ -230,8 +245,13 @@ struct Cfg {
   static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
 };
 
+// Operand maps of one launch.  a_chunked / b_chunked: the map is 4-D with a
+// 128-byte chunk of the contiguous dimension innermost (one TMA instruction
+// per operand part and stage); otherwise 3-D (K-major: one box; MN-major: one
+// box per 128-byte MN chunk).
 struct Maps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;
+  int a_chunked, b_chunked;
 };
 
 // Fused reduce-scatter epilogue (mr_gemm_rs): row r of C belongs to rank
@@ -251,29 +271,48 @@ struct RemoteOut {
   int active;
 };
 
-// Load one operand part (rows x BK) of a stage.  K-major: one box {BK, rows}.
-// MN-major: one box {128 / ELT, BK} per 128-byte MN chunk, 128 * BK bytes apart.
+// Shared-memory tile of one operand part (ROWS x BK):
+//   K-major:  [BK*ELT/128 K-chunks][ROWS][one K-chunk of 64 or 128 bytes]
+//   MN-major: [ROWS*ELT/128 MN-chunks][BK][128 bytes of MN]
+template <int BK, int ELT>
+struct KRow {
+  static constexpr int kBytes = BK * ELT > 128 ? 128 : BK * ELT;  // K-major row width
+  static constexpr int kElems = kBytes / ELT;
+};
+
+// Load one operand part of a stage.  Chunked maps: one instruction.  3-D maps:
+// K-major one box {BK, ROWS}; MN-major one box {128 / ELT, BK} per MN chunk.
 template <int ROWS, int BK, int ELT>
 __device__ __forceinline__ void load_part(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
-                                          bool kmajor, int row0, int k0, int z) {
+                                          bool kmajor, int chunked, int row0, int k0, int z) {
+  constexpr int kChunkMN = 128 / ELT;
   if (kmajor) {
-    tma_load_3d(dst, map, bar, k0, row0, z);
+    if (chunked)
+      tma_load_4d(dst, map, bar, 0, row0, k0 / KRow<BK, ELT>::kElems, z);
+    else
+      tma_load_3d(dst, map, bar, k0, row0, z);
+  } else if (chunked) {
+    tma_load_4d(dst, map, bar, 0, k0, row0 / kChunkMN, z);
   } else {
-    constexpr int kChunk = 128 / ELT;
 #pragma unroll
-    for (int c = 0; c < ROWS / kChunk; ++c)
-      tma_load_3d(dst + c * 128 * BK, map, bar, row0 + c * kChunk, k0, z);
+    for (int c = 0; c < ROWS / kChunkMN; ++c)
+      tma_load_3d(dst + c * 128 * BK, map, bar, row0 + c * kChunkMN, k0, z);
   }
 }
 
-template <int BK, int ELT>
+template <int ROWS, int BK, int ELT>
 __device__ __forceinline__ uint64_t part_desc(uint32_t base, bool kmajor, int kstep) {
-  // K-major: +32 B per MMA K step inside the swizzle row (BK * ELT bytes);
-  // 8-row groups 8 rows apart (SBO); SWIZZLE_64B or SWIZZLE_128B by row width.
+  // K-major: +32 B per MMA K step inside the swizzled row of a K-chunk, the
+  // next chunk ROWS rows further; 8-row groups 8 rows apart (SBO);
+  // SWIZZLE_64B or SWIZZLE_128B by row width.
   // bf16 MN-major: +2048 B (two 8-row K groups of 1024 B) per 16-deep K step;
-  // LBO = one MN box.  float32 MN-major (SWIZZLE_128B, 32-byte atoms): +1024 B
-  // (two 4-row K groups of 512 B) per 8-deep K step; LBO = one MN box.
-  if (kmajor) return smem_desc(base + kstep * 32, 16, 8 * BK * ELT, BK * ELT == 64 ? 4 : 2);
+  // LBO = one MN chunk.  float32 MN-major (SWIZZLE_128B, 32-byte atoms):
+  // +1024 B (two 4-row K groups of 512 B) per 8-deep K step; LBO = one MN chunk.
+  if (kmajor) {
+    constexpr int rb = KRow<BK, ELT>::kBytes;
+    const int off = kstep * 32;
+    return smem_desc(base + (off / rb) * ROWS * rb + (off % rb), 16, 8 * rb, rb == 64 ? 4 : 2);
+  }
   if (ELT == 2) return smem_desc(base + kstep * 2048, 128 * BK, 1024, 2);
   return smem_desc(base + kstep * 1024, 128 * BK, 512, 1);
 }
@@ -405,15 +444,17 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* st = smem + s * C::kStage;
           mbar_expect_tx(&full[s], C::kStage);
           const int k0 = kt * BK;
-          load_part<BM, BK, C::kElt>(st, &maps.a_hi, &full[s], a_kmajor, tl.m0, k0, tl.z);
+          load_part<BM, BK, C::kElt>(st, &maps.a_hi, &full[s], a_kmajor, maps.a_chunked, tl.m0,
+                                     k0, tl.z);
           if (C::kAParts == 2)
-            load_part<BM, BK, C::kElt>(st + C::kA, &maps.a_lo, &full[s], a_kmajor, tl.m0, k0,
-                                       tl.z);
+            load_part<BM, BK, C::kElt>(st + C::kA, &maps.a_lo, &full[s], a_kmajor,
+                                       maps.a_chunked, tl.m0, k0, tl.z);
           uint8_t* sb = st + C::kA * C::kAParts;
-          load_part<BN, BK, C::kElt>(sb, &maps.b_hi, &full[s], b_kmajor, tl.n0, k0, tl.z);
+          load_part<BN, BK, C::kElt>(sb, &maps.b_hi, &full[s], b_kmajor, maps.b_chunked, tl.n0,
+                                     k0, tl.z);
           if (C::kBParts == 2)
-            load_part<BN, BK, C::kElt>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor, tl.n0, k0,
-                                       tl.z);
+            load_part<BN, BK, C::kElt>(sb + C::kB, &maps.b_lo, &full[s], b_kmajor,
+                                       maps.b_chunked, tl.n0, k0, tl.z);
         }
       }
       if (!ok) {
@@ -454,16 +495,16 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int ks = 0; ks < BK / C::kMmaK; ++ks) {
             const uint32_t acc0 = (!first || ks > 0) ? 1u : 0u;
-            const uint64_t dah = part_desc<BK, C::kElt>(a_hi, a_kmajor, ks);
-            const uint64_t dbh = part_desc<BK, C::kElt>(b_hi, b_kmajor, ks);
+            const uint64_t dah = part_desc<BM, BK, C::kElt>(a_hi, a_kmajor, ks);
+            const uint64_t dbh = part_desc<BN, BK, C::kElt>(b_hi, b_kmajor, ks);
             if constexpr (C::kTf32) {
               umma_tf32(d, dah, dbh, idesc, acc0);
             } else {
               umma_bf16(d, dah, dbh, idesc, acc0);
               if (PREC == 3)
-                umma_bf16(d, dah, part_desc<BK, 2>(b_lo, b_kmajor, ks), idesc, 1u);
+                umma_bf16(d, dah, part_desc<BN, BK, 2>(b_lo, b_kmajor, ks), idesc, 1u);
               if (PREC >= 2)
-                umma_bf16(d, part_desc<BK, 2>(a_lo, a_kmajor, ks), dbh, idesc, 1u);
+                umma_bf16(d, part_desc<BM, BK, 2>(a_lo, a_kmajor, ks), dbh, idesc, 1u);
             }
           }
           umma_commit(&empty[s]);
@@ -629,18 +670,62 @@ bool make_map(CUtensorMap* map, const void* base, int elt, int64_t inner, int64_
   return r == CUDA_SUCCESS;
 }
 
-// Map for an operand with `rows` logical rows (M or N) and K columns.  K-major
-// boxes are {bk, tile_rows} swizzled at their row width (bk * elt bytes);
-// MN-major boxes are {128 bytes of rows, bk}: 128-byte swizzle for bf16, the
-// 32-byte-atom form of it for float32 (the layout kind::tf32 reads MN-major).
-bool operand_map(CUtensorMap* map, const void* p, int elt, bool kmajor, int64_t rows, int64_t k,
-                 int64_t ld, int64_t batch, int64_t batch_stride, int tile_rows, int bk) {
-  if (kmajor)
-    return make_map(map, p, elt, k, rows, ld, batch, batch_stride, uint32_t(bk),
-                    uint32_t(tile_rows),
-                    bk * elt == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
-  return make_map(map, p, elt, rows, k, ld, batch, batch_stride, uint32_t(128 / elt), uint32_t(bk),
-                  elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+// 4-D chunked map: x = a 128-byte chunk of the contiguous dimension, then the
+// other matrix dimension (stride ld), then the chunk index (stride 128 bytes),
+// then the batch.  One box {chunk, y_box, chunks, 1} lands in shared memory as
+// [chunks][y_box][128 bytes] -- the tile layout the UMMA descriptors describe.
+bool make_chunked_map(CUtensorMap* map, const void* base, int elt, int64_t contiguous,
+                      int64_t other, int64_t ld, int64_t batch, int64_t batch_stride,
+                      uint32_t box_other, uint32_t box_chunks, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn encode = encode_fn();
+  if (!encode) return false;
+  const int64_t chunk = 128 / elt;
+  const cuuint64_t dims[4] = {cuuint64_t(chunk), cuuint64_t(other), cuuint64_t(contiguous / chunk),
+                              cuuint64_t(batch)};
+  const cuuint64_t strides[3] = {cuuint64_t(ld) * elt, 128,
+                                 cuuint64_t(batch > 1 ? batch_stride : ld * other) * elt};
+  const cuuint32_t box[4] = {uint32_t(chunk), box_other, box_chunks, 1};
+  const cuuint32_t elem_strides[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, elt == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                      4, const_cast<void*>(base), dims, strides, box, elem_strides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Map for an operand with `rows` logical rows (M or N) and K columns, and
+// whether it is chunked (one TMA instruction per stage).  K-major rows of up
+// to 128 bytes: one box {bk, tile_rows} swizzled at its row width; wider rows
+// (float32 at bk = 64): chunked, two 128-byte K-chunks (K a multiple of 32).
+// MN-major: chunked when the rows divide into 128-byte chunks, else one box
+// {128 bytes, bk} per chunk; 128-byte swizzle for bf16, the 32-byte-atom form
+// of it for float32 (the layout kind::tf32 reads MN-major).
+bool operand_map(CUtensorMap* map, int* chunked, const void* p, int elt, bool kmajor,
+                 int64_t rows, int64_t k, int64_t ld, int64_t batch, int64_t batch_stride,
+                 int tile_rows, int bk) {
+  const int chunk = 128 / elt;
+  if (kmajor) {
+    if (bk * elt <= 128) {
+      *chunked = 0;
+      return make_map(map, p, elt, k, rows, ld, batch, batch_stride, uint32_t(bk),
+                      uint32_t(tile_rows),
+                      bk * elt == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (k % chunk) return false;
+    *chunked = 1;
+    return make_chunked_map(map, p, elt, k, rows, ld, batch, batch_stride, uint32_t(tile_rows),
+                            uint32_t(bk / chunk), CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  const CUtensorMapSwizzle swz =
+      elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  if (rows % chunk) {
+    *chunked = 0;
+    return make_map(map, p, elt, rows, k, ld, batch, batch_stride, uint32_t(chunk), uint32_t(bk),
+                    swz);
+  }
+  *chunked = 1;
+  return make_chunked_map(map, p, elt, rows, k, ld, batch, batch_stride, uint32_t(bk),
+                          uint32_t(tile_rows / chunk), swz);
 }
 
 // Per-device caches (a process may drive several GPUs from one or more host
@@ -738,19 +823,25 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
   // narrow outputs (attention's head dimension) use 128-wide tiles; 32-wide K
   // slices (deeper pipelines) unless both operands are MN-major, whose 64-wide
   // boxes would then be split into many small TMA copies
-  // float32 (tf32) operands: 32-wide K slices (128-byte K-major rows, four
-  // 48 KB stages at BN = 256) for every majorness.
+  // float32 (tf32) operands: kTf32BK-wide K slices (a 64-wide slice takes
+  // K-major rows as two 128-byte chunks, so it needs K a multiple of 32),
+  // else 32-wide.
   const int BNsel = n <= 128 ? 128 : 256;
-  const int BKsel = tf32 ? 32 : (!a_kmajor && !b_kmajor) ? 64 : 32;
+  const bool k_chunks = k % 32 == 0 || (!a_kmajor && !b_kmajor);
+  const int BKsel = tf32 ? (k_chunks ? kTf32BK : 32) : (!a_kmajor && !b_kmajor) ? 64 : 32;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
-  bool good =
-      operand_map(&maps.a_hi, a_hi, elt, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel) &&
-      operand_map(&maps.b_hi, b_hi, elt, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
+  int a_lo_chunked = 0, b_lo_chunked = 0;
+  bool good = operand_map(&maps.a_hi, &maps.a_chunked, a_hi, elt, a_kmajor, m, k, lda, batch,
+                          stride_a, BM, BKsel) &&
+              operand_map(&maps.b_hi, &maps.b_chunked, b_hi, elt, b_kmajor, n, k, ldb, batch,
+                          stride_b, BNsel, BKsel);
   if (good && (precision == 2 || precision == 3))
-    good = operand_map(&maps.a_lo, a_lo, elt, a_kmajor, m, k, lda, batch, stride_a, BM, BKsel);
+    good = operand_map(&maps.a_lo, &a_lo_chunked, a_lo, elt, a_kmajor, m, k, lda, batch, stride_a,
+                       BM, BKsel);
   if (good && precision == 3)
-    good = operand_map(&maps.b_lo, b_lo, elt, b_kmajor, n, k, ldb, batch, stride_b, BNsel, BKsel);
+    good = operand_map(&maps.b_lo, &b_lo_chunked, b_lo, elt, b_kmajor, n, k, ldb, batch, stride_b,
+                       BNsel, BKsel);
   if (!good) return MR_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bt = int(batch);
@@ -765,6 +856,13 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
                                         a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);  \
   }
   if (tf32) {
+    if (BKsel == kTf32BK) {
+      if (BNsel == 128)
+        return launch<128, kTf32BK, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,
+                                       a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);
+      return launch<256, kTf32BK, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,
+                                     a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);
+    }
     if (BNsel == 128)
       return launch<128, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
                                 b_kmajor, bt, causal, int(seq), remote, s);
