@@ -61,8 +61,9 @@ def parse():
     ap.add_argument("--group", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "copy", "nccl"],
-                    help="weight-gradient exchange at N > 1 (default: fused GEMM peer stores)")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "copy", "nccl"],
+                    help="weight-gradient exchange at N > 1 (default: the runner's choice by "
+                         "rank count -- fused GEMM peer stores up to 4 ranks, NCCL at 8)")
     ap.add_argument("--precision", default="tuning", choices=["tuning", "bf16x3"],
                     help="tuning: the runner's default (tf32 backward GEMMs); bf16x3: three "
                          "bf16 products in every GEMM")

@@ -185,11 +185,12 @@ class QuantizationRunner:
                  holdout_batches: int = 0, per_layer_recipe: bool = False,
                  precision: Precision | None = None, dist: DistContext | None = None,
                  device: torch.device | str | None = None, keep_codes: bool = False,
-                 exchange: str = "p2p") -> None:
+                 exchange: str = "auto") -> None:
         """``exchange``: the data-parallel weight-gradient exchange of the
         row-sharded update -- "p2p" (GEMM epilogue stores into the owners'
-        memory over NVLink), "copy" (copy engines) or "nccl" (reduce-scatter);
-        see :class:`~mround_b200.pipeline.tuning.BlockTuner`."""
+        memory over NVLink), "copy" (copy engines), "nccl" (reduce-scatter)
+        or "auto" (by rank count, as measured); see
+        :class:`~mround_b200.pipeline.tuning.BlockTuner`."""
         if holdout_batches < 0:
             raise CalibrationError(f"holdout_batches must be zero or more, got {holdout_batches}")
         self.scheme = scheme

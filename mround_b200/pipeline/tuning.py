@@ -34,7 +34,7 @@ from mround_b200.pipeline.block import TF32, DeviceBlock, FusedLinear, Precision
 from mround_b200.pipeline.dist import DistContext
 from mround_b200.schemes import QuantScheme, ScaleInit, Symmetry
 
-__all__ = ["BlockTuner", "Member", "QuantizedLayer", "TunableLayer", "piece_bounds"]
+__all__ = ["BlockTuner", "Member", "QuantizedLayer", "TunableLayer", "auto_exchange", "piece_bounds"]
 
 OUTLIER_FRACTION = 0.001
 
@@ -235,6 +235,17 @@ class TunableLayer:
         return out
 
 
+def auto_exchange(world: int) -> str:
+    """The weight-gradient exchange measured fastest inside the 7B tuning step
+    on one 8-GPU B200 box (tf32 backward): the fused GEMM -> NVLink peer-store
+    form up to four ranks (2 ranks: 6.25 ms of exchange against 7.38 with
+    NCCL for the block's four weight gradients; 4 ranks: 16.72 / 16.61 ms
+    steps), the NCCL reduce-scatter at eight (10.30 ms steps against 11.10:
+    the epilogue's stores to seven peers hold the dW GEMMs back while NCCL's
+    transfer overlaps the rest of the backward)."""
+    return "p2p" if world <= 4 else "nccl"
+
+
 @dataclasses.dataclass
 class _Shard:
     """This rank's rows [s0, s1) of a fused weight under the row-sharded update:
@@ -253,14 +264,17 @@ class BlockTuner:
 
     def __init__(self, block: DeviceBlock, schemes: dict[str, QuantScheme], lrs: dict[str, float],
                  *, suppress: bool, eps: float, precision: Precision, dist: DistContext,
-                 pieces: int = 1, exchange: str = "p2p") -> None:
+                 pieces: int = 1, exchange: str = "auto") -> None:
         """``exchange``: how the row-sharded update gathers each rank's rows of
         the gradient -- "p2p" (the weight-gradient GEMM stores them into their
         owners' slots over NVLink), "copy" (the GEMM writes locally and the
-        copy engines move the rows into the same slots) or "nccl" (a
-        reduce-scatter after the GEMM)."""
+        copy engines move the rows into the same slots), "nccl" (a
+        reduce-scatter after the GEMM) or "auto" (``auto_exchange``)."""
+        if exchange == "auto":
+            exchange = auto_exchange(dist.world)
         if exchange not in ("p2p", "copy", "nccl"):
-            raise ValueError(f"exchange must be 'p2p', 'copy' or 'nccl', got {exchange!r}")
+            raise ValueError(f"exchange must be 'p2p', 'copy', 'nccl' or 'auto', got {exchange!r}")
+        self.exchange = exchange
         self.block = block
         self.suppress = suppress
         self.precision = precision

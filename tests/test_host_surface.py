@@ -182,3 +182,11 @@ def test_export_refuses_unrepresentable(tmp_path):
 
     with pytest.raises(ExportError):
         export_mlx(tmp_path, {}, {}, {})
+
+
+def test_exchange_default_follows_the_measured_rank_count():
+    """The fused peer-store exchange up to four ranks, NCCL at eight (measured
+    inside the 7B step); an unknown name is refused."""
+    from mround_b200.pipeline.tuning import auto_exchange
+
+    assert [auto_exchange(n) for n in (1, 2, 4, 8)] == ["p2p", "p2p", "p2p", "nccl"]
