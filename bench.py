@@ -168,13 +168,14 @@ class ClockSampler:
                 "source": "nvml" if self.handle is not None else "nvidia-smi"}
 
 
-# DRAM bytes (read + write) per K3 launch, averaged over the 17 GEMM launches of
-# one 7B step (8 x 2048 tokens, N=1), from one ncu capture of this workload:
+# DRAM bytes (read + write) per K3 launch, averaged over the 11 weight GEMMs of
+# one 7B step (16384 tokens, N=1, the tuning form: forward bf16x3, backward
+# tf32), from one ncu capture of each shape's warm launch:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
-#       --clock-control none -k regex:gemm_kernel -s 96 -c 36
-#       python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-e2e
-# (60.9 GB read + 10.9 GB written per step).
-GEMM_TRAFFIC_7B = 4.22e9
+#       --clock-control none -k regex:gemm_kernel --csv
+#       python -m mround_b200.kernel_sweep --gemm-all 16384
+# (51.8 GB per step for 17.8 GB of operands and outputs).
+GEMM_TRAFFIC_7B = 4.71e9
 
 
 # ----------------------------------------------------------------- workload
@@ -436,7 +437,7 @@ def main():
                      "executed_frac": (exe_flops / (gemm_ms / 1e3) / 1e12) / peak if gemm_ms else 0.0,
                      "gemm_share_of_step": gemm_ms / t_step if t_step else None,
                      "traffic": GEMM_TRAFFIC_7B if args.arch == "qwen2.5-7b" and dist.world == 1 else None,
-                     "traffic_unit": "bytes per K3 launch (DRAM read + write), ncu capture"},
+                     "traffic_unit": "bytes per weight-GEMM K3 launch (DRAM read + write), ncu capture of each shape"},
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
