@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "copy", "nccl"],
                     help="weight-gradient exchange at N > 1 (default: the runner's choice by "
                          "rank count -- fused GEMM peer stores up to 4 ranks, NCCL at 8)")
+    ap.add_argument("--gather", default="codes", choices=["codes", "operands"],
+                    help="what the ranks all-gather after the row-sharded step at N > 1: "
+                         "codes and per-group scale / zero point (default) or the operands")
     ap.add_argument("--precision", default="tuning", choices=["tuning", "bf16x3"],
                     help="tuning: the runner's default (tf32 backward GEMMs); bf16x3: three "
                          "bf16 products in every GEMM")
@@ -209,7 +212,7 @@ def make_tuner(args, block, dist):
 
     scheme = QuantScheme(bits=args.bits, group_size=args.group, symmetry="asym")
     runner = QuantizationRunner(scheme, TuningConfig(iters=ITERS), dist=dist,
-                                exchange=args.exchange,
+                                exchange=args.exchange, gather=args.gather,
                                 precision=Precision() if args.precision == "bf16x3" else None)
     return runner.tuner_for(block, "model.layers.0")
 
@@ -427,6 +430,11 @@ def main():
                                          "dW GEMM, then copy-engine transfers of each owner's rows"
                                          if tuner.peer.streams is not None else
                                          "fused dW GEMM -> reduce-scatter over NVLink peer stores"),
+                   "operand_gather": ("none" if dist.world == 1 else
+                                      "codes + per-group scale/zero point"
+                                      if any(sh.codes is not None
+                                             for sh in tuner._shards.values()) else
+                                      "bf16 hi/lo + tf32 operands"),
                    "l2": "inputs larger than L2 (235 MB per batch input)"},
         "ms_forward_batch": t_fwd, "block_seconds": blk_s, "wall_s_model": blk_s * arch.layers,
         "gpu_launches": launches,

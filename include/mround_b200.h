@@ -116,6 +116,35 @@ int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alp
                    void* stream);
 
 /*
+ * K2 for the row-sharded data-parallel update: the same straight-through
+ * step as mr_ste_signsgd with update = 1, writing the NEXT step's integer
+ * codes (one byte each: unsigned under the asymmetric scheme, two's
+ * complement under the symmetric ones) and per-group float32 scale and zero
+ * point (qzp only under the asymmetric scheme; may be NULL otherwise)
+ * instead of the operands.  These are what the ranks exchange (about 1.1
+ * bytes per weight instead of 8); mr_dequant_split rebuilds the operands
+ * from them, bit for bit as mr_ste_signsgd writes them.  Same reference call
+ * sites as mr_ste_signsgd (mround/pipeline/runner.py:926-931).  codes 8-byte
+ * aligned.
+ */
+int mr_ste_signsgd_codes(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
+                         float* beta, int64_t rows, int64_t cols, int group, int bits,
+                         int symmetric, const float* init_scale, float eps, float lr,
+                         float coef_lo, float coef_hi, uint8_t* codes, float* qscale,
+                         float* qzp, void* stream);
+
+/*
+ * Operands from codes (the receiving side of the exchange above):
+ *   wq = qscale * (code - qzp)  (symmetric = 0)   or   qscale * code  (symmetric = 1)
+ * in float32 -- the fake-quant reconstruction of mround/core/quantizer.py:
+ * 341-347 given its codes -- written as bf16 hi/lo and the tf32 copy (any may
+ * be NULL).
+ */
+int mr_dequant_split(const uint8_t* codes, const float* qscale, const float* qzp, int64_t rows,
+                     int64_t cols, int group, int symmetric, uint16_t* wq_hi, uint16_t* wq_lo,
+                     float* wq_t32, void* stream);
+
+/*
  * K5 -- commit and MLX packing in one pass.
  * Replaces quantize_codes (mround/core/quantizer.py:350-398), narrow_codes
  * (mround/formats/mlx_export.py:109-125), the symmetric offset and pack_codes
@@ -370,6 +399,16 @@ int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int
                     int64_t stride_b, int b_kmajor, float* c, int64_t ldc, int64_t stride_c,
                     const float* bias, int accumulate, int64_t m, int64_t n, int64_t k,
                     int64_t batch, int precision, int causal, int64_t seq, void* stream);
+
+/*
+ * The output tile width (128, 224 or 256 columns) mr_gemm / mr_gemm_tf32 /
+ * mr_gemm_batched / mr_gemm_rs use for this shape on the current device:
+ * 128 for n <= 128, else the width of 224 and 256 with the shorter
+ * persistent schedule (whole waves of tiles over the SMs).  A query; launches
+ * nothing.  Negative status on bad arguments.
+ */
+int mr_gemm_tile_n(int64_t m, int64_t n, int64_t k, int64_t batch, int precision, int a_kmajor,
+                   int b_kmajor, int causal);
 
 /* Device status word of K3: 0, or MR_ERR_TIMEOUT.  Synchronizes the device;
  * reset != 0 clears it. */

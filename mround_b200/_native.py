@@ -45,6 +45,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
                            _P, _P]),
     "mr_ste_signsgd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _F, _F, _F, _I,
                             _P, _P, _P, _P, _P, _P, _P]),
+    "mr_ste_signsgd_codes": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _F, _F, _F,
+                                  _P, _P, _P, _P]),
+    "mr_dequant_split": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P, _P, _P]),
     "mr_pack_mlx": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _P, _P, _P, _P, _P]),
     "mr_loss_workspace_bytes": (ctypes.c_size_t, []),
     "mr_loss_outlier": (_I, [_P, _P, _I64, _I64, _I, _D, _F, _P, _P, _P, _P, _P]),
@@ -62,6 +65,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
                      _I, _P]),
     "mr_gemm_batched": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _I64, _I64, _I, _P, _I64, _I64, _P,
                              _I, _I64, _I64, _I64, _I64, _I, _I, _I64, _P]),
+    "mr_gemm_tile_n": (_I, [_I64, _I64, _I64, _I64, _I, _I, _I, _I]),
     "mr_gemm_status": (_I, [_I]),
     "mr_gemm_rs": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I64, _I64, _I64, _I, _P, _I64, _I64,
                         _P, _I, _P, ctypes.c_uint64, _P]),

@@ -167,12 +167,20 @@ __device__ __forceinline__ void store_f8(float* p, const float (&x)[8]) {
   reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
 }
 
+// Operand values are written with zeros as +0 (x + 0 under round-to-nearest):
+// a product's sign of zero (rint(-0.3) * scale = -0) cannot survive the
+// exchange of integer codes, and the operands rebuilt from codes
+// (mr_dequant_split) must equal these bit for bit.  Only the sign of a zero
+// changes; no product or nonzero sum can see it.
+__device__ __forceinline__ float operand_value(float x) { return __fadd_rn(x, 0.f); }
+
 // The tf32-rounded copy of 8 values (the backward GEMMs' float32 operand).
 __device__ __forceinline__ void store_t8(float* p, const float (&x)[8]) {
-  reinterpret_cast<float4*>(p)[0] =
-      make_float4(tf32_rna(x[0]), tf32_rna(x[1]), tf32_rna(x[2]), tf32_rna(x[3]));
-  reinterpret_cast<float4*>(p)[1] =
-      make_float4(tf32_rna(x[4]), tf32_rna(x[5]), tf32_rna(x[6]), tf32_rna(x[7]));
+  float t[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t[i] = tf32_rna(operand_value(x[i]));
+  reinterpret_cast<float4*>(p)[0] = make_float4(t[0], t[1], t[2], t[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(t[4], t[5], t[6], t[7]);
 }
 
 __device__ __forceinline__ void store_split(const float (&wq)[8], int64_t e, uint16_t* hi,
@@ -180,8 +188,9 @@ __device__ __forceinline__ void store_split(const float (&wq)[8], int64_t e, uin
   uint16_t h[8], l[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    h[i] = f32_to_bf16(wq[i]);
-    l[i] = f32_to_bf16(__fsub_rn(wq[i], bf16_to_f32(h[i])));
+    const float x = operand_value(wq[i]);
+    h[i] = f32_to_bf16(x);
+    l[i] = f32_to_bf16(__fsub_rn(x, bf16_to_f32(h[i])));
   }
   if (hi) *reinterpret_cast<uint4*>(hi + e) = pack8(h);
   if (lo) *reinterpret_cast<uint4*>(lo + e) = pack8(l);
@@ -261,7 +270,8 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
     float* __restrict__ alpha, float* __restrict__ beta, const float* __restrict__ init_scale,
     int64_t n, int group, float maxq, float eps, float lr, float lo, float hi, int update,
     float* __restrict__ gv_out, float* __restrict__ ga_out, float* __restrict__ gb_out,
-    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo, float* __restrict__ wq_t32) {
+    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo, float* __restrict__ wq_t32,
+    uint8_t* __restrict__ codes_out, float* __restrict__ qscale_out, float* __restrict__ qzp_out) {
   const int lane = threadIdx.x & 31;
   const int64_t tiles = (n + kTile - 1) / kTile;
   for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
@@ -340,14 +350,30 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
       alpha[gi] = an;
       beta[gi] = bn;
     }
-    if (wq_hi || wq_lo || wq_t32) {
+    if (wq_hi || wq_lo || wq_t32 || codes_out) {
       const GroupQ qn = group_params<MODE>(gmax, gmin, an, bn, base, maxq, eps);
-      float wq[8];
+      float wq[8], code[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        wq[i] = dequant<MODE>(clamp_code<MODE>(unclamped_code<MODE>(wf[i], vn[i], qn), maxq), qn);
+      for (int i = 0; i < 8; ++i) {
+        code[i] = clamp_code<MODE>(unclamped_code<MODE>(wf[i], vn[i], qn), maxq);
+        wq[i] = dequant<MODE>(code[i], qn);
+      }
       store_split(wq, e, wq_hi, wq_lo);
       if (wq_t32) store_t8(wq_t32 + e, wq);
+      if (codes_out) {
+        // one byte per code: unsigned under kAsym, two's complement otherwise
+        uint32_t lo4 = 0, hi4 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          lo4 |= (uint32_t(int(code[i])) & 0xFFu) << (8 * i);
+          hi4 |= (uint32_t(int(code[i + 4])) & 0xFFu) << (8 * i);
+        }
+        *reinterpret_cast<uint2*>(codes_out + e) = make_uint2(lo4, hi4);
+        if (leader) {
+          if (qscale_out) qscale_out[gi] = qn.scale;
+          if (qzp_out) qzp_out[gi] = qn.zp;
+        }
+      }
     }
   }
 }
@@ -551,7 +577,82 @@ extern "C" int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, init_scale, n,
               group, maxq, eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo,
-              wq_t32);
+              wq_t32, nullptr, nullptr, nullptr);
+  return launch_status();
+}
+
+extern "C" int mr_ste_signsgd_codes(const float* gq, const uint16_t* w_bf16, float* v,
+                                    float* alpha, float* beta, int64_t rows, int64_t cols,
+                                    int group, int bits, int symmetric, const float* init_scale,
+                                    float eps, float lr, float coef_lo, float coef_hi,
+                                    uint8_t* codes, float* qscale, float* qzp, void* stream) {
+  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  if (st) return st;
+  const int mode = scheme_mode(symmetric, init_scale);
+  if (!gq || !alpha || !beta || !codes || !qscale || mode < 0) return MR_ERR_ARGUMENT;
+  if (mode == kAsym && !qzp) return MR_ERR_ARGUMENT;
+  if (!aligned16(gq) || (reinterpret_cast<uintptr_t>(codes) & 7u)) return MR_ERR_ALIGNMENT;
+  const int64_t n = rows * cols;
+  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
+  const float maxq = mode_maxq(mode, bits);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, init_scale, n,
+              group, maxq, eps, lr, coef_lo, coef_hi, 1, nullptr, nullptr, nullptr, nullptr,
+              nullptr, nullptr, codes, qscale, mode == kAsym ? qzp : nullptr);
+  return launch_status();
+}
+
+namespace mr {
+namespace {
+
+// Operands from codes: wq = scale * (code - zp) (asymmetric) or scale * code
+// (symmetric, codes as two's complement bytes) -- the same float32 operations
+// as dequant<MODE> -- written as bf16 hi/lo and the tf32 copy.
+template <bool SYM>
+__global__ void __launch_bounds__(kThreads) dequant_split_kernel(
+    const uint8_t* __restrict__ codes, const float* __restrict__ scale,
+    const float* __restrict__ zp, int64_t n, int group, uint16_t* __restrict__ hi,
+    uint16_t* __restrict__ lo, float* __restrict__ t32) {
+  for (int64_t e = (int64_t(blockIdx.x) * kThreads + threadIdx.x) * 8; e < n;
+       e += int64_t(gridDim.x) * kThreads * 8) {
+    const uint2 u = *reinterpret_cast<const uint2*>(codes + e);
+    const int64_t gi = e / group;
+    const float sc = scale[gi];
+    const float z = SYM ? 0.f : zp[gi];
+    float wq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t byte = ((i < 4 ? u.x : u.y) >> (8 * (i & 3))) & 0xFFu;
+      const float code = SYM ? float(int(int8_t(byte))) : float(byte);
+      wq[i] = SYM ? __fmul_rn(sc, code) : __fmul_rn(sc, __fsub_rn(code, z));
+    }
+    store_split(wq, e, hi, lo);
+    if (t32) store_t8(t32 + e, wq);
+  }
+}
+
+}  // namespace
+}  // namespace mr
+
+extern "C" int mr_dequant_split(const uint8_t* codes, const float* qscale, const float* qzp,
+                                int64_t rows, int64_t cols, int group, int symmetric,
+                                uint16_t* wq_hi, uint16_t* wq_lo, float* wq_t32, void* stream) {
+  if (!codes || !qscale || rows <= 0 || cols <= 0 || (!symmetric && !qzp)) return MR_ERR_ARGUMENT;
+  if (group != 8 && group != 16 && group != 32 && group != 64 && group != 128 && group != 256)
+    return MR_ERR_ARGUMENT;
+  if (cols % group) return MR_ERR_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(codes) & 7u) || (wq_hi && !aligned16(wq_hi)) ||
+      (wq_lo && !aligned16(wq_lo)) || (wq_t32 && !aligned16(wq_t32)))
+    return MR_ERR_ALIGNMENT;
+  const int64_t n = rows * cols;
+  const int grid = grid_for((n + 7) / 8, kThreads);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (symmetric)
+    dequant_split_kernel<true><<<grid, kThreads, 0, s>>>(codes, qscale, qzp, n, group, wq_hi, wq_lo,
+                                                          wq_t32);
+  else
+    dequant_split_kernel<false><<<grid, kThreads, 0, s>>>(codes, qscale, qzp, n, group, wq_hi,
+                                                           wq_lo, wq_t32);
   return launch_status();
 }
 

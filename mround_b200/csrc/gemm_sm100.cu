@@ -242,7 +242,12 @@ struct Cfg {
   // fused reduce-scatter turns row-per-lane values into row-contiguous stores
   static constexpr int kStaging = 4 * 32 * 33 * 4;
   static constexpr int kSmem = kStages * kStage + 1024 /* align */ + 256 /* barriers */ + kStaging;
-  static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
+  // TMEM: two accumulators of BN columns, the second at column kAccCols; the
+  // allocation is a power of two (224 -> 256 per accumulator, 512 in all)
+  static constexpr int kAccCols = BN <= 128 ? 128 : 256;
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static_assert(BN % 32 == 0 && BN <= kAccCols && kTmemCols <= 512,
+                "two accumulators must fit the 512 TMEM columns");
 };
 
 // Operand maps of one launch.  a_chunked / b_chunked: the map is 4-D with a
@@ -421,7 +426,7 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a_hi)));
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b_hi)));
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  if (warp == 1) tmem_alloc(tmem_slot, C::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -479,7 +484,7 @@ __global__ void __launch_bounds__(192, 1)
         if (j >= 2) ok = mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem + uint32_t(b * BN);
+        const uint32_t d = tmem + uint32_t(b * C::kAccCols);
         bool first = true;
         for (int kt = 0; kt < tl.kt_end; ++kt) {
           if (!k_active<BK>(sh, tl.m0, kt)) continue;
@@ -534,7 +539,8 @@ __global__ void __launch_bounds__(192, 1)
       if (!tl.skip) {
         float* cz = c + int64_t(tl.z) * stride_c;
         const int row = tl.m0 + quarter * 32 + lane;
-        const uint32_t lane_base = tmem + uint32_t(b * BN) + (uint32_t(quarter * 32) << 16);
+        const uint32_t lane_base =
+            tmem + uint32_t(b * C::kAccCols) + (uint32_t(quarter * 32) << 16);
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
           float v[32];
@@ -627,7 +633,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
@@ -787,6 +793,34 @@ using namespace mr;
 
 namespace {
 
+// Output tile width.  128 for narrow outputs (attention's head dimension);
+// otherwise 256, or 224 where that evens out the persistent schedule: every
+// tile of one launch costs the same, CTA i takes tiles i, i + grid, ..., so a
+// launch lasts ceil(tiles / SMs) tiles of BN columns each.  For N = 3584 at
+// M = 2048 (one 8-rank share of the 7B batch) 256-wide tiles make 224 tiles
+// -- 1.5 waves on 148 SMs, 2 tile-times of 256 columns -- and 224-wide ones
+// 256 tiles in 2 tile-times of 224 columns.  224 needs every B chunk whole:
+// B K-major, or MN-major tf32 (7 chunks of 32); the three-product bf16 form
+// only (the precisions the block step uses); no batch, no causal mode.
+int select_bn(int64_t m, int64_t n, int64_t batch, int precision, int b_kmajor, int causal,
+              int bk) {
+  if (n <= 128) return 128;
+  const bool can224 = batch == 1 && causal == 0 &&
+                      (precision == 4 || (precision == 3 && b_kmajor && bk == 32));
+  if (!can224) return 256;
+  const int64_t sms = sm_count();
+  const int64_t mt = (m + BM - 1) / BM;
+  const int64_t w256 = (mt * ((n + 255) / 256) + sms - 1) / sms;
+  const int64_t w224 = (mt * ((n + 223) / 224) + sms - 1) / sms;
+  // at least 3 % less: a 224-wide tile moves a little more A per flop
+  return w224 * 224 * 100 <= w256 * 256 * 97 ? 224 : 256;
+}
+
+int select_bk(int64_t k, int tf32, int a_kmajor, int b_kmajor) {
+  const bool k_chunks = k % 32 == 0 || (!a_kmajor && !b_kmajor);
+  return tf32 ? (k_chunks ? kTf32BK : 32) : (!a_kmajor && !b_kmajor) ? 64 : 32;
+}
+
 // precision 1..3: bf16 operands (hi, optional lo); 4: one tf32 product of
 // float32 operands (a_hi / b_hi point at float32 data; the lo parts are unused).
 int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
@@ -826,9 +860,8 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
   // float32 (tf32) operands: kTf32BK-wide K slices (a 64-wide slice takes
   // K-major rows as two 128-byte chunks, so it needs K a multiple of 32),
   // else 32-wide.
-  const int BNsel = n <= 128 ? 128 : 256;
-  const bool k_chunks = k % 32 == 0 || (!a_kmajor && !b_kmajor);
-  const int BKsel = tf32 ? (k_chunks ? kTf32BK : 32) : (!a_kmajor && !b_kmajor) ? 64 : 32;
+  const int BKsel = select_bk(k, tf32, a_kmajor, b_kmajor);
+  const int BNsel = select_bn(m, n, batch, precision, b_kmajor, causal, BKsel);
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   int a_lo_chunked = 0, b_lo_chunked = 0;
@@ -856,6 +889,10 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
                                         a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);  \
   }
   if (tf32) {
+    static_assert(kTf32BK == 32, "one 224-wide tf32 instantiation serves both K slices");
+    if (BNsel == 224)
+      return launch<224, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
+                                b_kmajor, bt, causal, int(seq), remote, s);
     if (BKsel == kTf32BK) {
       if (BNsel == 128)
         return launch<128, kTf32BK, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,
@@ -869,6 +906,9 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
     return launch<256, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
                               b_kmajor, bt, causal, int(seq), remote, s);
   }
+  if (BNsel == 224)  // precision 3, BK 32 (select_bn)
+    return launch<224, 32, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
+                              b_kmajor, bt, causal, int(seq), remote, s);
   if (BNsel == 128) {
     if (BKsel == 64) { MR_GEMM_LAUNCH(128, 64) }
     MR_GEMM_LAUNCH(128, 32)
@@ -960,6 +1000,15 @@ extern "C" int mr_gemm_rs_tf32(const float* a, int64_t lda, int a_kmajor, const 
                                unsigned long long epoch, void* stream) {
   return gemm_rs_impl(a, nullptr, lda, a_kmajor, b, nullptr, ldb, b_kmajor, m, n, k, 4, dst, ldd,
                       rows_per_rank, flags, world, done, epoch, stream);
+}
+
+// The output tile width a launch of this shape uses (128, 224 or 256).
+extern "C" int mr_gemm_tile_n(int64_t m, int64_t n, int64_t k, int64_t batch, int precision,
+                              int a_kmajor, int b_kmajor, int causal) {
+  if (m <= 0 || n <= 0 || k <= 0 || batch <= 0 || precision < 1 || precision > 4)
+    return MR_ERR_ARGUMENT;
+  return select_bn(m, n, batch, precision, b_kmajor, causal,
+                   select_bk(k, precision == 4, a_kmajor, b_kmajor));
 }
 
 // Device status word of the GEMM (0 ok, MR_ERR_TIMEOUT after a wait gave up).

@@ -130,6 +130,36 @@ def ste_signsgd(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr:
     _count()
 
 
+def ste_signsgd_codes(gq, w, v, alpha, beta, *, bits: int, group: int, eps: float, lr: float,
+                      lo: float, hi: float, codes, qscale, qzp=None, symmetric: bool = False,
+                      init_scale=None) -> None:
+    """K2's signed step, writing the next step's codes (uint8, one per weight)
+    and per-group scale / zero point instead of the operands."""
+    rows, cols, pw, pv, pa, pb = _weight_args(w, v, alpha, beta, group)
+    n, ng = rows * cols, rows * (cols // group)
+    sym, pinit = _scheme_args(symmetric, init_scale, ng)
+    status = lib().mr_ste_signsgd_codes(
+        _ptr(gq, torch.float32, "gq", n), pw, pv, pa, pb, rows, cols, group, bits, sym, pinit,
+        eps, lr, lo, hi, _ptr(codes, torch.uint8, "codes", n),
+        _ptr(qscale, torch.float32, "qscale", ng), _ptr(qzp, torch.float32, "qzp", ng), _stream())
+    check(status, "mr_ste_signsgd_codes")
+    _count()
+
+
+def dequant_split(codes, qscale, qzp, *, group: int, symmetric: bool, wq_hi=None, wq_lo=None,
+                  wq_t32=None) -> None:
+    """Operands (bf16 hi/lo, tf32) from codes and per-group scale / zero point."""
+    rows, cols = codes.shape
+    n, ng = rows * cols, rows * (cols // group)
+    status = lib().mr_dequant_split(
+        _ptr(codes, torch.uint8, "codes", n), _ptr(qscale, torch.float32, "qscale", ng),
+        _ptr(qzp, torch.float32, "qzp", ng), rows, cols, group, int(bool(symmetric)),
+        _ptr(wq_hi, torch.bfloat16, "wq_hi", n), _ptr(wq_lo, torch.bfloat16, "wq_lo", n),
+        _ptr(wq_t32, torch.float32, "wq_t32", n), _stream())
+    check(status, "mr_dequant_split")
+    _count()
+
+
 def pack_mlx(w, v, alpha, beta, *, bits: int, group: int, eps: float, want_codes: bool = False,
              symmetric: bool = False, init_scale=None):
     """K5: ``(packed uint32 as int32, scales bf16, biases bf16, codes or None)``.
@@ -360,6 +390,15 @@ def gemm_rs(a_hi, a_lo, b_hi, b_lo, *, m: int, n: int, k: int, a_kmajor: bool, b
 
 # tensor time of one tf32 product, in bf16 products (tf32 runs at half the rate)
 TF32_PRODUCT_COST = 2
+
+
+def gemm_tile_n(*, m: int, n: int, k: int, precision: int, a_kmajor: bool, b_kmajor: bool,
+                batch: int = 1, causal: int = 0) -> int:
+    """The output tile width (128, 224 or 256) K3 uses for this shape."""
+    width = int(lib().mr_gemm_tile_n(m, n, k, batch, precision, int(a_kmajor), int(b_kmajor),
+                                     causal))
+    check(min(width, 0), "mr_gemm_tile_n")
+    return width
 
 
 def gemm_tf32(a, b, c, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool, lda: int,

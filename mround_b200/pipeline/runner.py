@@ -185,11 +185,13 @@ class QuantizationRunner:
                  holdout_batches: int = 0, per_layer_recipe: bool = False,
                  precision: Precision | None = None, dist: DistContext | None = None,
                  device: torch.device | str | None = None, keep_codes: bool = False,
-                 exchange: str = "auto") -> None:
+                 exchange: str = "auto", gather: str = "codes") -> None:
         """``exchange``: the data-parallel weight-gradient exchange of the
         row-sharded update -- "p2p" (GEMM epilogue stores into the owners'
         memory over NVLink), "copy" (copy engines), "nccl" (reduce-scatter)
-        or "auto" (by rank count, as measured); see
+        or "auto" (by rank count, as measured); ``gather``: what the ranks
+        all-gather after the step -- "codes" (codes and per-group scale /
+        zero point) or "operands"; see
         :class:`~mround_b200.pipeline.tuning.BlockTuner`."""
         if holdout_batches < 0:
             raise CalibrationError(f"holdout_batches must be zero or more, got {holdout_batches}")
@@ -205,6 +207,7 @@ class QuantizationRunner:
         self.device = torch.device(device or "cuda")
         self.keep_codes = keep_codes
         self.exchange = exchange
+        self.gather = gather
 
     def _scheme_for(self, path: str, overrides: Mapping[str, QuantScheme] | None) -> QuantScheme:
         if overrides is None:
@@ -331,7 +334,8 @@ class QuantizationRunner:
                                        per_layer=self.per_layer_recipe)
         return BlockTuner(block, schemes, rates, suppress=suppress, eps=self.eps,
                           precision=self.precision, dist=self.dist,
-                          pieces=self.tuning.micro_batches, exchange=self.exchange)
+                          pieces=self.tuning.micro_batches, exchange=self.exchange,
+                          gather=self.gather)
 
     def quantize_block(self, block: DeviceBlock, name: str, inputs: list[torch.Tensor],
                        targets: list[torch.Tensor], *,

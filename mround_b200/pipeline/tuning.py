@@ -110,7 +110,8 @@ class TunableLayer:
         self.beta = torch.ones_like(self.alpha)
         self.init_scale = torch.zeros_like(self.alpha) if self.searched else None
         tuned_rows = sum(m.rows[1] - m.rows[0] for m in members)
-        if tuned_rows == out:
+        self.whole = tuned_rows == out  # every row is fake-quantized
+        if self.whole:
             layer.wq_hi = torch.empty_like(layer.w)
             layer.wq_lo = torch.empty_like(layer.w)
         else:  # rows of untuned members stay exact
@@ -176,6 +177,37 @@ class TunableLayer:
                                 wq_hi=hi[r0 - s0:r1 - s0], wq_lo=lo[r0 - s0:r1 - s0],
                                 wq_t32=None if t32 is None else t32[r0 - s0:r1 - s0],
                                 symmetric=self.symmetric, init_scale=init)
+
+    def update_rows_codes(self, step: int, iters: int, s0: int, s1: int, grad: torch.Tensor,
+                          codes: torch.Tensor, qscale: torch.Tensor,
+                          qzp: torch.Tensor | None) -> None:
+        """``update_rows`` writing the next step's codes and per-group scale /
+        zero point of rows [s0, s1) instead of their operands (every row of
+        the weight is tuned; ``dequant`` rebuilds the operands)."""
+        gpr = self.layer.in_features // self.group
+        for m in self.members:
+            r0, r1 = max(m.rows[0], s0), min(m.rows[1], s1)
+            if r0 >= r1:
+                continue
+            lr = m.lr0 * (1.0 - step / iters) if step < iters else 0.0
+            lo_b, hi_b = m.scheme.coefficient_bounds
+            init = None if self.init_scale is None else self.init_scale[r0:r1]
+            g0, g1 = (r0 - s0) * gpr, (r1 - s0) * gpr
+            kernels.ste_signsgd_codes(
+                grad[r0 - s0:r1 - s0], self.layer.w[r0:r1], self.v[r0:r1], self.alpha[r0:r1],
+                self.beta[r0:r1], bits=m.scheme.bits, group=m.group, eps=self.eps, lr=lr,
+                lo=lo_b, hi=hi_b, codes=codes[r0 - s0:r1 - s0],
+                qscale=qscale.view(-1)[g0:g1].view(r1 - r0, gpr),
+                qzp=None if qzp is None else qzp.view(-1)[g0:g1].view(r1 - r0, gpr),
+                symmetric=self.symmetric, init_scale=init)
+
+    def dequant(self, codes: torch.Tensor, qscale: torch.Tensor,
+                qzp: torch.Tensor | None) -> None:
+        """The whole weight's operands (bf16 hi/lo and the tf32 copy) from the
+        gathered codes and per-group scale / zero point."""
+        kernels.dequant_split(codes, qscale, qzp, group=self.group, symmetric=self.symmetric,
+                              wq_hi=self.layer.wq_hi, wq_lo=self.layer.wq_lo,
+                              wq_t32=self.layer.wq_t32)
 
     def gradients(self) -> dict[str, tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         """K2 without the update: (gV, galpha, gbeta) per member, from ``layer.grad``."""
@@ -254,9 +286,40 @@ class _Shard:
     s0: int
     s1: int
     grad: torch.Tensor
-    hi: torch.Tensor
-    lo: torch.Tensor
+    hi: torch.Tensor | None
+    lo: torch.Tensor | None
     t32: torch.Tensor | None
+    codes: _Codes | None = None  # the gather of codes instead of operands
+
+
+@dataclasses.dataclass
+class _Codes:
+    """The codes gather of one fused weight: this rank's rows (send buffers)
+    and every rank's (receive buffers), one byte per weight plus a float32
+    scale (and zero point) per group, against eight bytes per weight for the
+    operands (bf16 hi + lo, tf32)."""
+
+    codes: torch.Tensor
+    qscale: torch.Tensor
+    qzp: torch.Tensor | None
+    all_codes: torch.Tensor
+    all_qscale: torch.Tensor
+    all_qzp: torch.Tensor | None
+
+
+class _Dequant:
+    """A pending entry of a fused weight (``FusedLinear.pending``): waits for
+    the codes gather, then rebuilds the operands on the waiting stream."""
+
+    def __init__(self, tunable: TunableLayer, codes: _Codes, works: list) -> None:
+        self.tunable, self.codes, self.works = tunable, codes, works
+
+    def wait(self) -> None:
+        for w in self.works:
+            if w is not None:
+                w.wait()
+        c = self.codes
+        self.tunable.dequant(c.all_codes, c.all_qscale, c.all_qzp)
 
 
 class BlockTuner:
@@ -264,12 +327,18 @@ class BlockTuner:
 
     def __init__(self, block: DeviceBlock, schemes: dict[str, QuantScheme], lrs: dict[str, float],
                  *, suppress: bool, eps: float, precision: Precision, dist: DistContext,
-                 pieces: int = 1, exchange: str = "auto") -> None:
+                 pieces: int = 1, exchange: str = "auto", gather: str = "codes") -> None:
         """``exchange``: how the row-sharded update gathers each rank's rows of
         the gradient -- "p2p" (the weight-gradient GEMM stores them into their
         owners' slots over NVLink), "copy" (the GEMM writes locally and the
         copy engines move the rows into the same slots), "nccl" (a
-        reduce-scatter after the GEMM) or "auto" (``auto_exchange``)."""
+        reduce-scatter after the GEMM) or "auto" (``auto_exchange``).
+        ``gather``: what the ranks all-gather after their rows' signed step --
+        "codes" (codes and per-group scale / zero point, rebuilt into operands
+        on every rank; used for fused weights whose every row is tuned and
+        whose width is a multiple of 8) or "operands" (bf16 hi/lo and tf32)."""
+        if gather not in ("codes", "operands"):
+            raise ValueError(f"gather must be 'codes' or 'operands', got {gather!r}")
         if exchange == "auto":
             exchange = auto_exchange(dist.world)
         if exchange not in ("p2p", "copy", "nccl"):
@@ -318,6 +387,10 @@ class BlockTuner:
                 s0, s1 = dist.rank * per, (dist.rank + 1) * per
                 grad = torch.empty((per, inn), dtype=torch.float32, device=block.device)
                 # untuned rows of a partly tuned fused weight keep their exact operand
+                if gather == "codes" and t.whole and inn % 8 == 0:
+                    self._shards[id(t.layer)] = _Shard(s0, s1, grad, None, None, None,
+                                                       self._codes_buffers(t, per))
+                    continue
                 t32 = t.layer.wq_t32
                 self._shards[id(t.layer)] = _Shard(
                     s0, s1, grad, t.layer.wq_hi[s0:s1].clone(), t.layer.wq_lo[s0:s1].clone(),
@@ -334,6 +407,20 @@ class BlockTuner:
                                      block.device, copy_engine=exchange == "copy")
             for t, ex in zip(self.tunables, self.peer.layers):
                 t.layer.exchange = ex
+
+    def _codes_buffers(self, t: TunableLayer, per: int) -> _Codes:
+        out, inn = t.layer.w.shape
+        dev = self.block.device
+        gpr = inn // t.group
+        asym = not t.symmetric
+
+        def f32(rows):
+            return torch.empty((rows, gpr), dtype=torch.float32, device=dev)
+
+        return _Codes(torch.empty((per, inn), dtype=torch.uint8, device=dev), f32(per),
+                      f32(per) if asym else None,
+                      torch.empty((out, inn), dtype=torch.uint8, device=dev), f32(out),
+                      f32(out) if asym else None)
 
     # ------------------------------------------------------------ search
     def search(self, inputs: list[torch.Tensor]) -> float:
@@ -417,6 +504,15 @@ class BlockTuner:
                 ex.active = False
             else:
                 self._wait(t.layer)
+            if sh.codes is not None:
+                c = sh.codes
+                t.update_rows_codes(step, iters, sh.s0, sh.s1, sh.grad, c.codes, c.qscale, c.qzp)
+                works = [self.dist.all_gather_async(c.all_codes, c.codes),
+                         self.dist.all_gather_async(c.all_qscale, c.qscale)]
+                if c.qzp is not None:
+                    works.append(self.dist.all_gather_async(c.all_qzp, c.qzp))
+                t.layer.pending.append(_Dequant(t, c, works))
+                continue
             t.update_rows(step, iters, sh.s0, sh.s1, sh.grad, sh.hi, sh.lo, sh.t32)
             t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_hi, sh.hi))
             t.layer.pending.append(self.dist.all_gather_async(t.layer.wq_lo, sh.lo))

@@ -53,7 +53,7 @@ def _precision(name):
     return Precision() if name == "bf16x3" else TUNING_PRECISION
 
 
-def _tuner(block, dist, exchange="p2p", prec="bf16x3"):
+def _tuner(block, dist, exchange="p2p", prec="bf16x3", gather="codes"):
     from mround_b200.pipeline.tuning import BlockTuner
     from mround_b200.schemes import QuantScheme
     from oracle.block_tuner import LINEARS
@@ -61,10 +61,10 @@ def _tuner(block, dist, exchange="p2p", prec="bf16x3"):
     scheme = QuantScheme(bits=2, group_size=32, symmetry="asym")
     return BlockTuner(block, {p: scheme for p in LINEARS}, {p: 0.05 for p in LINEARS},
                       suppress=True, eps=1e-8, precision=_precision(prec), dist=dist,
-                      exchange=exchange)
+                      exchange=exchange, gather=gather)
 
 
-def _rank(rank, world, port, q, exchange="p2p", prec="bf16x3"):
+def _rank(rank, world, port, q, exchange="p2p", prec="bf16x3", gather="codes"):
     import torch.distributed as tdist
 
     from mround_b200.pipeline.dist import DistContext
@@ -80,7 +80,7 @@ def _rank(rank, world, port, q, exchange="p2p", prec="bf16x3"):
         dev = torch.device("cuda", rank)
         _, block, x, tgt = _setup(dev)
         rows = ctx.shard(SHAPE[0])
-        tuner = _tuner(block, ctx, exchange, prec)
+        tuner = _tuner(block, ctx, exchange, prec, gather)
         assert tuner.sharded, "tiny-qwen2's fused rows divide by 2: the row-sharded update runs"
         assert (tuner.peer is not None) == (exchange in ("p2p", "copy"))
         loss = tuner.step(x[rows].to(dev), tgt[rows].to(dev), 0, 10)
@@ -90,20 +90,25 @@ def _rank(rank, world, port, q, exchange="p2p", prec="bf16x3"):
         total = torch.stack([loss, loss2])
         ctx.all_reduce_(total)
         torch.cuda.synchronize(dev)
+        operands = [x.view(torch.int16).cpu().numpy() if x.dtype == torch.bfloat16
+                    else x.cpu().numpy()
+                    for t in tuner.tunables
+                    for x in (t.layer.wq_hi, t.layer.wq_lo, t.layer.wq_t32) if x is not None]
         q.put((rank, total.tolist(), float(tuner.ws.thr.item()),
                [t.v.cpu().numpy() for t in tuner.tunables],
-               [t.alpha.cpu().numpy() for t in tuner.tunables]))
+               [t.alpha.cpu().numpy() for t in tuner.tunables], operands))
         tuner.close()
         tdist.barrier()
     finally:
         tdist.destroy_process_group()
 
 
-def _run_ranks(exchange, prec="bf16x3"):
+def _run_ranks(exchange, prec="bf16x3", gather="codes"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, exchange, prec)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, exchange, prec, gather))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
@@ -126,6 +131,22 @@ def test_two_gpu_fused_exchange_equals_nccl_reduce_scatter(prec):
     for a, b in zip(fused, nccl):
         assert a[1] == b[1] and a[2] == b[2]
         for x, y in zip(a[3] + a[4], b[3] + b[4]):
+            assert np.array_equal(x, y)
+
+
+@pytest.mark.parametrize("prec", ["bf16x3", "tuning"])
+def test_two_gpu_codes_gather_equals_operands_gather(prec):
+    """Gathering each rank's codes and per-group scale / zero point and
+    rebuilding the operands on every rank gives the same operands, losses
+    and parameters, bit for bit, as gathering the operands themselves."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    codes = _run_ranks("p2p", prec, "codes")
+    operands = _run_ranks("p2p", prec, "operands")
+    for a, b in zip(codes, operands):
+        assert a[1] == b[1] and a[2] == b[2]
+        assert len(a[5]) == len(b[5]) > 0
+        for x, y in zip(a[3] + a[4] + a[5], b[3] + b[4] + b[5]):
             assert np.array_equal(x, y)
 
 

@@ -92,6 +92,17 @@ def test_bias_and_accumulate(K):
     run_case(K, 128, 256, 64, True, False, 2, bias=True, accumulate=True)
 
 
+@pytest.mark.parametrize("a_kmajor", [True, False])
+@pytest.mark.parametrize("m,n", [(2048, 3584), (2000, 3488), (128, 896)])
+def test_224_wide_tiles(K, a_kmajor, m, n):
+    """Shapes whose persistent schedule is shorter with 224-wide output tiles
+    (the 8-rank share of the 7B batch against a 3584-wide output; a ragged
+    last tile; a 896-wide output) -- three products, B K-major."""
+    assert K.gemm_tile_n(m=m, n=n, k=192, precision=3, a_kmajor=a_kmajor, b_kmajor=True) == 224
+    run_case(K, m, n, 192, a_kmajor, True, 3, bias=True)
+    run_case(K, m, n, 96, a_kmajor, True, 3, accumulate=True, seed=1)
+
+
 def test_long_k(K):
     run_case(K, 256, 256, 8192, False, False, 3)
 

@@ -80,6 +80,19 @@ def test_ragged_edges(K, m, n, k):
         run_case(K, m, n, k, True, False)
 
 
+@pytest.mark.parametrize("a_kmajor", [True, False])
+@pytest.mark.parametrize("b_kmajor", [True, False])
+@pytest.mark.parametrize("m,n", [(2048, 3584), (2000, 3488)])
+def test_224_wide_tiles(K, a_kmajor, b_kmajor, m, n):
+    """224-wide output tiles (seven 128-byte chunks of an MN-major tf32 B
+    tile): the 8-rank share of the 7B batch against a 3584-wide output, and
+    a ragged last tile."""
+    assert K.gemm_tile_n(m=m, n=n, k=160, precision=4, a_kmajor=a_kmajor,
+                         b_kmajor=b_kmajor) == 224
+    run_case(K, m, n, 160, a_kmajor, b_kmajor, bias=True)
+    run_case(K, m, n, 64, a_kmajor, b_kmajor, accumulate=True, seed=1)
+
+
 def test_bias_and_accumulate(K):
     run_case(K, 256, 384, 192, True, True, bias=True)
     run_case(K, 256, 384, 192, False, False, accumulate=True)

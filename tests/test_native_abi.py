@@ -94,3 +94,28 @@ def test_gemm_entry_points_refuse_bad_precision_and_alignment():
     assert lib.mr_gemm(p, p, 64, 1, p, p, 64, 1, p, 64, None, 0, 128, 128, 64, 0, None) == -1
     assert lib.mr_gemm_tf32(p, 66, 1, p, 64, 1, p, 64, None, 0, 128, 128, 64, None) == -2
     assert lib.mr_gemm_tf32(None, 64, 1, p, 64, 1, p, 64, None, 0, 128, 128, 64, None) == -1
+
+
+def test_gemm_tile_width_follows_the_persistent_schedule():
+    """The tile-width query needs no GPU (148 SMs assumed without one): 224
+    where it shortens the schedule and the B tile divides into whole chunks,
+    256 otherwise, 128 for narrow outputs."""
+    from mround_b200 import kernels
+
+    def width(m, n, precision, b_kmajor=True, a_kmajor=True, batch=1, causal=0):
+        return kernels.gemm_tile_n(m=m, n=n, k=3584, precision=precision, a_kmajor=a_kmajor,
+                                   b_kmajor=b_kmajor, batch=batch, causal=causal)
+
+    assert width(2048, 3584, 3) == 224           # 224 tiles of 256: 1.5 waves
+    assert width(2048, 3584, 4, b_kmajor=False) == 224
+    assert width(2048, 3584, 3, b_kmajor=False) == 256  # bf16 MN-major: 3.5 chunks
+    assert width(2048, 3584, 1) == 256           # one- and two-product forms keep 256
+    assert width(2048, 3584, 3, batch=2) == 256
+    assert width(16384, 37888, 3) == 256         # 128 whole waves already
+    assert width(16384, 3584, 4) == 224          # 13 waves of 256 against 14 of 224
+    assert width(2048, 128, 3) == 128
+    assert width(2048, 4608, 3) == 256           # a ragged 224 tile would lengthen it
+    from mround_b200.exceptions import SchemeError
+
+    with pytest.raises(SchemeError):
+        width(0, 3584, 3)
