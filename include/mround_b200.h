@@ -116,6 +116,42 @@ int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alp
                    void* stream);
 
 /*
+ * K2 over several matrices in one launch (the members of a block, or this
+ * rank's rows of them): the signed step of mr_ste_signsgd with update = 1 on
+ * every segment, each writing its next operands (wq_hi / wq_lo / wq_t32, any
+ * may be NULL) or its next codes (codes, qscale, qzp as in
+ * mr_ste_signsgd_codes).  All segments share the group size, the scheme
+ * (symmetric; init_scale NULL on all or on none) and eps; bits, the rate and
+ * the coefficient bounds are per segment.  1 <= count <= 8.  Results are bit
+ * for bit those of one mr_ste_signsgd / mr_ste_signsgd_codes call per
+ * segment; the launch's warp tiles run over all segments, so small matrices
+ * share one ramp and tail.  Same reference call sites as mr_ste_signsgd.
+ */
+typedef struct mr_k2_segment {
+  const float* gq;
+  const uint16_t* w_bf16;
+  float* v;
+  float* alpha;
+  float* beta;
+  const float* init_scale;
+  int64_t rows;
+  int64_t cols;
+  int bits;
+  float lr;
+  float coef_lo;
+  float coef_hi;
+  uint16_t* wq_hi;
+  uint16_t* wq_lo;
+  float* wq_t32;
+  uint8_t* codes;
+  float* qscale;
+  float* qzp;
+} mr_k2_segment;
+
+int mr_ste_signsgd_segments(const mr_k2_segment* segs, int count, int group, int symmetric,
+                            float eps, void* stream);
+
+/*
  * K2 for the row-sharded data-parallel update: the same straight-through
  * step as mr_ste_signsgd with update = 1, writing the NEXT step's integer
  * codes (one byte each: unsigned under the asymmetric scheme, two's
@@ -403,9 +439,10 @@ int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int
 /*
  * The output tile width (128, 224 or 256 columns) mr_gemm / mr_gemm_tf32 /
  * mr_gemm_batched / mr_gemm_rs use for this shape on the current device:
- * 128 for n <= 128, else the width of 224 and 256 with the shorter
- * persistent schedule (whole waves of tiles over the SMs).  A query; launches
- * nothing.  Negative status on bad arguments.
+ * 128 for n <= 128; for one tf32 product (precision 4) the width of 224 and
+ * 256 with the shorter persistent schedule (whole waves of tiles over the
+ * SMs); 256 otherwise.  A query; launches nothing.  Negative status on bad
+ * arguments.
  */
 int mr_gemm_tile_n(int64_t m, int64_t n, int64_t k, int64_t batch, int precision, int a_kmajor,
                    int b_kmajor, int causal);

@@ -48,6 +48,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_ste_signsgd_codes": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _F, _F, _F,
                                   _P, _P, _P, _P]),
     "mr_dequant_split": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P, _P, _P]),
+    "mr_ste_signsgd_segments": (_I, [_P, _I, _I, _I, _F, _P]),
     "mr_pack_mlx": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P, _F, _P, _P, _P, _P, _P]),
     "mr_loss_workspace_bytes": (ctypes.c_size_t, []),
     "mr_loss_outlier": (_I, [_P, _P, _I64, _I64, _I, _D, _F, _P, _P, _P, _P, _P]),
@@ -91,6 +92,17 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_softmax_causal_split": (_I, [_P, _I64, _I, _F, _I, _P, _P, _P]),
     "mr_softmax_bwd_split": (_I, [_P, _P, _P, _I64, _I, _F, _I, _P, _P, _P]),
 }
+
+
+class K2Segment(ctypes.Structure):
+    """``mr_k2_segment``: one matrix of an ``mr_ste_signsgd_segments`` launch."""
+
+    _fields_ = [
+        ("gq", _P), ("w_bf16", _P), ("v", _P), ("alpha", _P), ("beta", _P),
+        ("init_scale", _P), ("rows", _I64), ("cols", _I64), ("bits", _I), ("lr", _F),
+        ("coef_lo", _F), ("coef_hi", _F), ("wq_hi", _P), ("wq_lo", _P), ("wq_t32", _P),
+        ("codes", _P), ("qscale", _P), ("qzp", _P),
+    ]
 
 
 def declared_symbols() -> list[str]:

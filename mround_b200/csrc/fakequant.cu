@@ -18,6 +18,7 @@
 // reconstructions are bit-exact against a float32 implementation of the same
 // formulas.
 
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
@@ -264,19 +265,60 @@ __global__ void __launch_bounds__(kThreads) fq_forward_kernel(
 //              gbeta = -gs * w_min_raw, gs = sum g*d / 2^(b-1)
 //   kSearched: same d; galpha = 0, gbeta = sum g*d * searched scale
 // with gs zeroed where the eps floor holds the scale.
+//
+// One launch steps up to kMaxK2Segs matrices of one scheme and group size
+// (the members of a block): their warp tiles form one list, segment s owning
+// tiles [tile0, tile0 + ceil(n / kTile)), so small matrices share one
+// launch's ramp and tail instead of paying one each.
+struct K2Seg {
+  const float* gq;
+  const uint16_t* w;
+  float* v;
+  float* alpha;
+  float* beta;
+  const float* init_scale;
+  float* gv_out;  // gradients (update = 0)
+  float* ga_out;
+  float* gb_out;
+  uint16_t* wq_hi;  // next operands (update = 1)
+  uint16_t* wq_lo;
+  float* wq_t32;
+  uint8_t* codes_out;  // or next codes, scale and zero point (update = 1)
+  float* qscale_out;
+  float* qzp_out;
+  int64_t n;
+  int64_t tile0;
+  float maxq, lr, lo, hi;
+};
+constexpr int kMaxK2Segs = 8;
+struct K2Launch {
+  K2Seg seg[kMaxK2Segs];
+  int64_t tiles;
+  int count;
+  int update;
+  float eps;
+};
+
 template <int LPG, int MODE>
-__global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
-    const float* __restrict__ gq, const uint16_t* __restrict__ w, float* __restrict__ v,
-    float* __restrict__ alpha, float* __restrict__ beta, const float* __restrict__ init_scale,
-    int64_t n, int group, float maxq, float eps, float lr, float lo, float hi, int update,
-    float* __restrict__ gv_out, float* __restrict__ ga_out, float* __restrict__ gb_out,
-    uint16_t* __restrict__ wq_hi, uint16_t* __restrict__ wq_lo, float* __restrict__ wq_t32,
-    uint8_t* __restrict__ codes_out, float* __restrict__ qscale_out, float* __restrict__ qzp_out) {
+__global__ void __launch_bounds__(kThreads)
+    ste_signsgd_kernel(const __grid_constant__ K2Launch L, int group) {
   const int lane = threadIdx.x & 31;
-  const int64_t tiles = (n + kTile - 1) / kTile;
-  for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < tiles;
+  const float eps = L.eps;
+  for (int64_t t = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < L.tiles;
        t += int64_t(gridDim.x) * kWarps) {
-    const int64_t e = t * kTile + lane * 8;
+    int s = 0;
+#pragma unroll 1
+    while (s + 1 < L.count && t >= L.seg[s + 1].tile0) ++s;
+    const K2Seg& S = L.seg[s];
+    const float* __restrict__ gq = S.gq;
+    const uint16_t* __restrict__ w = S.w;
+    float* __restrict__ v = S.v;
+    float* __restrict__ alpha = S.alpha;
+    float* __restrict__ beta = S.beta;
+    const float* __restrict__ init_scale = S.init_scale;
+    const int64_t n = S.n;
+    const float maxq = S.maxq, lr = S.lr, lo = S.lo, hi = S.hi;
+    const int64_t e = (t - S.tile0) * kTile + lane * 8;
     const bool in = e < n;
     float wf[8], vf[8], g[8];
     const int64_t gi = in ? e / group : 0;
@@ -333,12 +375,12 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
       gb = q.live ? __fmul_rn(sum_t, q.base) : 0.f;
     }
     const bool leader = (lane & (LPG - 1)) == 0;
-    if (gv_out) store_f8(gv_out + e, gv);
+    if (S.gv_out) store_f8(S.gv_out + e, gv);
     if (leader) {
-      if (ga_out) ga_out[gi] = ga;
-      if (gb_out) gb_out[gi] = gb;
+      if (S.ga_out) S.ga_out[gi] = ga;
+      if (S.gb_out) S.gb_out[gi] = gb;
     }
-    if (!update) continue;
+    if (!L.update) continue;
     float vn[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -350,6 +392,10 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
       alpha[gi] = an;
       beta[gi] = bn;
     }
+    uint16_t* __restrict__ wq_hi = S.wq_hi;
+    uint16_t* __restrict__ wq_lo = S.wq_lo;
+    float* __restrict__ wq_t32 = S.wq_t32;
+    uint8_t* __restrict__ codes_out = S.codes_out;
     if (wq_hi || wq_lo || wq_t32 || codes_out) {
       const GroupQ qn = group_params<MODE>(gmax, gmin, an, bn, base, maxq, eps);
       float wq[8], code[8];
@@ -370,8 +416,8 @@ __global__ void __launch_bounds__(kThreads) ste_signsgd_kernel(
         }
         *reinterpret_cast<uint2*>(codes_out + e) = make_uint2(lo4, hi4);
         if (leader) {
-          if (qscale_out) qscale_out[gi] = qn.scale;
-          if (qzp_out) qzp_out[gi] = qn.zp;
+          if (S.qscale_out) S.qscale_out[gi] = qn.scale;
+          if (S.qzp_out) S.qzp_out[gi] = qn.zp;
         }
       }
     }
@@ -558,27 +604,72 @@ extern "C" int mr_fq_forward(const uint16_t* w_bf16, const float* v, const float
   return launch_status();
 }
 
+namespace {
+
+// Checks one K2 matrix and appends it to a launch; the scheme mode of every
+// matrix of one launch must agree.
+int add_k2(K2Launch& L, int* mode, const float* gq, const uint16_t* w_bf16, float* v,
+           float* alpha, float* beta, int64_t rows, int64_t cols, int group, int bits,
+           int symmetric, const float* init_scale, float lr, float coef_lo, float coef_hi,
+           float* gv, float* galpha, float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo,
+           float* wq_t32, uint8_t* codes, float* qscale, float* qzp) {
+  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  if (st) return st;
+  const int m = scheme_mode(symmetric, init_scale);
+  if (!gq || !alpha || !beta || m < 0) return MR_ERR_ARGUMENT;
+  if (L.count && m != *mode) return MR_ERR_ARGUMENT;
+  if (L.count >= kMaxK2Segs) return MR_ERR_ARGUMENT;
+  if (codes && (!qscale || (m == kAsym && !qzp))) return MR_ERR_ARGUMENT;
+  if (!aligned16(gq) || (gv && !aligned16(gv)) || (wq_hi && !aligned16(wq_hi)) ||
+      (wq_lo && !aligned16(wq_lo)) || (wq_t32 && !aligned16(wq_t32)) ||
+      (reinterpret_cast<uintptr_t>(codes) & 7u))
+    return MR_ERR_ALIGNMENT;
+  *mode = m;
+  K2Seg& S = L.seg[L.count++];
+  memset(&S, 0, sizeof(S));
+  S.gq = gq; S.w = w_bf16; S.v = v; S.alpha = alpha; S.beta = beta; S.init_scale = init_scale;
+  S.gv_out = gv; S.ga_out = galpha; S.gb_out = gbeta;
+  S.wq_hi = wq_hi; S.wq_lo = wq_lo; S.wq_t32 = wq_t32;
+  S.codes_out = codes; S.qscale_out = codes ? qscale : nullptr;
+  S.qzp_out = codes && m == kAsym ? qzp : nullptr;
+  S.n = rows * cols;
+  S.tile0 = L.tiles;
+  S.maxq = mode_maxq(m, bits);
+  S.lr = lr; S.lo = coef_lo; S.hi = coef_hi;
+  L.tiles += (S.n + kTile - 1) / kTile;
+  return MR_OK;
+}
+
+int launch_k2(const K2Launch& L, int mode, int group, cudaStream_t s) {
+  if (L.count == 0 || L.tiles <= 0) return MR_ERR_ARGUMENT;
+  const int grid = grid_for(L.tiles, kWarps);
+  MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, L, group);
+  return launch_status();
+}
+
+K2Launch k2_launch(int update, float eps) {
+  K2Launch L;
+  memset(&L, 0, sizeof(L));
+  L.update = update;
+  L.eps = eps;
+  return L;
+}
+
+}  // namespace
+
 extern "C" int mr_ste_signsgd(const float* gq, const uint16_t* w_bf16, float* v, float* alpha,
                               float* beta, int64_t rows, int64_t cols, int group, int bits,
                               int symmetric, const float* init_scale, float eps, float lr,
                               float coef_lo, float coef_hi, int update, float* gv, float* galpha,
                               float* gbeta, uint16_t* wq_hi, uint16_t* wq_lo, float* wq_t32,
                               void* stream) {
-  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  K2Launch L = k2_launch(update ? 1 : 0, eps);
+  int mode = 0;
+  int st = add_k2(L, &mode, gq, w_bf16, v, alpha, beta, rows, cols, group, bits, symmetric,
+                  init_scale, lr, coef_lo, coef_hi, gv, galpha, gbeta, wq_hi, wq_lo, wq_t32,
+                  nullptr, nullptr, nullptr);
   if (st) return st;
-  const int mode = scheme_mode(symmetric, init_scale);
-  if (!gq || !alpha || !beta || mode < 0) return MR_ERR_ARGUMENT;
-  if (!aligned16(gq) || (gv && !aligned16(gv)) || (wq_hi && !aligned16(wq_hi)) ||
-      (wq_lo && !aligned16(wq_lo)) || (wq_t32 && !aligned16(wq_t32)))
-    return MR_ERR_ALIGNMENT;
-  const int64_t n = rows * cols;
-  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
-  const float maxq = mode_maxq(mode, bits);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, init_scale, n,
-              group, maxq, eps, lr, coef_lo, coef_hi, update, gv, galpha, gbeta, wq_hi, wq_lo,
-              wq_t32, nullptr, nullptr, nullptr);
-  return launch_status();
+  return launch_k2(L, mode, group, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mr_ste_signsgd_codes(const float* gq, const uint16_t* w_bf16, float* v,
@@ -586,20 +677,29 @@ extern "C" int mr_ste_signsgd_codes(const float* gq, const uint16_t* w_bf16, flo
                                     int group, int bits, int symmetric, const float* init_scale,
                                     float eps, float lr, float coef_lo, float coef_hi,
                                     uint8_t* codes, float* qscale, float* qzp, void* stream) {
-  int st = check_common(w_bf16, v, rows, cols, group, bits);
+  if (!codes) return MR_ERR_ARGUMENT;
+  K2Launch L = k2_launch(1, eps);
+  int mode = 0;
+  int st = add_k2(L, &mode, gq, w_bf16, v, alpha, beta, rows, cols, group, bits, symmetric,
+                  init_scale, lr, coef_lo, coef_hi, nullptr, nullptr, nullptr, nullptr, nullptr,
+                  nullptr, codes, qscale, qzp);
   if (st) return st;
-  const int mode = scheme_mode(symmetric, init_scale);
-  if (!gq || !alpha || !beta || !codes || !qscale || mode < 0) return MR_ERR_ARGUMENT;
-  if (mode == kAsym && !qzp) return MR_ERR_ARGUMENT;
-  if (!aligned16(gq) || (reinterpret_cast<uintptr_t>(codes) & 7u)) return MR_ERR_ALIGNMENT;
-  const int64_t n = rows * cols;
-  const int grid = grid_for((n + kTile - 1) / kTile, kWarps);
-  const float maxq = mode_maxq(mode, bits);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  MR_DISPATCH(mode, group, ste_signsgd_kernel, grid, s, gq, w_bf16, v, alpha, beta, init_scale, n,
-              group, maxq, eps, lr, coef_lo, coef_hi, 1, nullptr, nullptr, nullptr, nullptr,
-              nullptr, nullptr, codes, qscale, mode == kAsym ? qzp : nullptr);
-  return launch_status();
+  return launch_k2(L, mode, group, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mr_ste_signsgd_segments(const mr_k2_segment* segs, int count, int group,
+                                       int symmetric, float eps, void* stream) {
+  if (!segs || count < 1 || count > kMaxK2Segs) return MR_ERR_ARGUMENT;
+  K2Launch L = k2_launch(1, eps);
+  int mode = 0;
+  for (int i = 0; i < count; ++i) {
+    const mr_k2_segment& g = segs[i];
+    int st = add_k2(L, &mode, g.gq, g.w_bf16, g.v, g.alpha, g.beta, g.rows, g.cols, group,
+                    g.bits, symmetric, g.init_scale, g.lr, g.coef_lo, g.coef_hi, nullptr,
+                    nullptr, nullptr, g.wq_hi, g.wq_lo, g.wq_t32, g.codes, g.qscale, g.qzp);
+    if (st) return st;
+  }
+  return launch_k2(L, mode, group, static_cast<cudaStream_t>(stream));
 }
 
 namespace mr {

@@ -794,19 +794,21 @@ using namespace mr;
 namespace {
 
 // Output tile width.  128 for narrow outputs (attention's head dimension);
-// otherwise 256, or 224 where that evens out the persistent schedule: every
-// tile of one launch costs the same, CTA i takes tiles i, i + grid, ..., so a
-// launch lasts ceil(tiles / SMs) tiles of BN columns each.  For N = 3584 at
-// M = 2048 (one 8-rank share of the 7B batch) 256-wide tiles make 224 tiles
-// -- 1.5 waves on 148 SMs, 2 tile-times of 256 columns -- and 224-wide ones
-// 256 tiles in 2 tile-times of 224 columns.  224 needs every B chunk whole:
-// B K-major, or MN-major tf32 (7 chunks of 32); the three-product bf16 form
-// only (the precisions the block step uses); no batch, no causal mode.
+// otherwise 256, or 224 for the tf32 products where that evens out the
+// persistent schedule: every tile of one launch costs about the same, CTA i
+// takes tiles i, i + grid, ..., so a launch lasts ceil(tiles / SMs) tiles.
+// 224 needs every B chunk whole (MN-major tf32: 7 chunks of 32; K-major: any)
+// and no batch or causal mode.  Measured on the 7B step's shapes (CUDA
+// events, same box, against a 256-only build): tf32 dW through qkv 0.95-0.96x
+// the time and dX through o at 2048 tokens 0.97x, the long-K shapes
+// unchanged; the three-product bf16 forward at 224 ran up to 6 % slower at
+// 16384 tokens, so it keeps 256.
 int select_bn(int64_t m, int64_t n, int64_t batch, int precision, int b_kmajor, int causal,
               int bk) {
   if (n <= 128) return 128;
-  const bool can224 = batch == 1 && causal == 0 &&
-                      (precision == 4 || (precision == 3 && b_kmajor && bk == 32));
+  (void)b_kmajor;
+  (void)bk;
+  const bool can224 = batch == 1 && causal == 0 && precision == 4;
   if (!can224) return 256;
   const int64_t sms = sm_count();
   const int64_t mt = (m + BM - 1) / BM;
@@ -906,9 +908,6 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
     return launch<256, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
                               b_kmajor, bt, causal, int(seq), remote, s);
   }
-  if (BNsel == 224)  // precision 3, BK 32 (select_bn)
-    return launch<224, 32, 3>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
-                              b_kmajor, bt, causal, int(seq), remote, s);
   if (BNsel == 128) {
     if (BKsel == 64) { MR_GEMM_LAUNCH(128, 64) }
     MR_GEMM_LAUNCH(128, 32)

@@ -35,7 +35,10 @@ Other modes (measurement drivers of the profiles):
   --step STEPS                  tuning steps of a 7B block, the last between
                                 cudaProfilerStart/Stop (a one-step launch list);
   --exchange [--tf32]           the block's weight-gradient exchange, under
-                                torch.distributed.run.
+                                torch.distributed.run;
+  --block-k2                    K2 over the seven linears of a block of each
+                                benchmark architecture: one launch per member
+                                against one segmented launch.
 
 Usage: python -m mround_b200.kernel_sweep [--reps N] [--quick | --attention | ...]
 Prints one JSON line per case, then a summary line.
@@ -315,6 +318,51 @@ def gemm_table(tokens: int, reps: int = 5) -> list[dict]:
     return out
 
 
+# ----------------------------------------------------------------- block K2
+def block_k2(reps: int = 5, bits: int = 2, group: int = 64) -> list[dict]:
+    """K2 over the seven linears of one block of each benchmark architecture:
+    seven launches (one per member) against one segmented launch
+    (``ste_signsgd_segments``), each timed cold (after a 256 MB write), with
+    the configuration-2 byte count (18 B/weight + 16 B/group, hi/lo operands)."""
+    from mround_b200.pipeline.arch import get_arch
+
+    device = torch.device("cuda")
+    peak, src = _peak()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    out = []
+    for name in ("smollm2-135m", "qwen2.5-0.5b", "qwen2.5-3b", "qwen2.5-7b"):
+        shapes = get_arch(name).linear_shapes()
+        segs, nbytes = [], 0
+        for i, (rows, cols) in enumerate(shapes.values()):
+            w, v, a, b, gq = _case(rows, cols, group, 7 + i, device)
+            segs.append({"gq": gq, "w": w, "v": v, "alpha": a, "beta": b, "bits": bits,
+                         "lr": 1e-9, "lo": 0.1, "hi": 1.0, "wq_hi": torch.empty_like(w),
+                         "wq_lo": torch.empty_like(w)})
+            nbytes += 18 * rows * cols + 16 * rows * (cols // group)
+
+        def each():
+            for sg in segs:
+                kernels.ste_signsgd(sg["gq"], sg["w"], sg["v"], sg["alpha"], sg["beta"],
+                                    bits=bits, group=group, eps=1e-8, lr=sg["lr"], lo=0.1,
+                                    hi=1.0, wq_hi=sg["wq_hi"], wq_lo=sg["wq_lo"])
+
+        def grouped():
+            kernels.ste_signsgd_segments(segs, group=group, eps=1e-8)
+
+        for form, fn in (("per_member", each), ("segmented", grouped)):
+            fn()
+            torch.cuda.synchronize()
+            ms = _time(fn, flush, reps)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            rec = {"kernel": "K2_block", "arch": name, "form": form, "launches": 7 if form ==
+                   "per_member" else 1, "bytes": nbytes, "ms": ms, "gbs": gbs, "frac": gbs / peak,
+                   "peak_gbs": peak, "peak_source": src}
+            out.append(rec)
+            print(json.dumps(rec), flush=True)
+        del segs
+    return out
+
+
 # ----------------------------------------------------------------- one step
 def step_probe(steps: int, arch_name: str = "qwen2.5-7b", tokens: int = 2048,
                batch: int = 8) -> None:
@@ -467,6 +515,8 @@ def main() -> None:
                     help="7B tuning steps, the last between cudaProfilerStart/Stop")
     ap.add_argument("--exchange", action="store_true",
                     help="weight-gradient exchange of a 7B block (under torch.distributed.run)")
+    ap.add_argument("--block-k2", action="store_true",
+                    help="K2 over a block's seven linears: per-member against one launch")
     args = ap.parse_args()
     if args.attention:
         attention(args.reps)
@@ -480,6 +530,8 @@ def main() -> None:
         step_probe(args.step)
     elif args.exchange:
         exchange_probe(args.tf32)
+    elif args.block_k2:
+        block_k2(args.reps)
     else:
         run(args.reps, args.quick)
 

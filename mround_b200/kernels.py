@@ -146,6 +146,43 @@ def ste_signsgd_codes(gq, w, v, alpha, beta, *, bits: int, group: int, eps: floa
     _count()
 
 
+MAX_K2_SEGMENTS = 8
+
+
+def ste_signsgd_segments(segments: list[dict], *, group: int, eps: float,
+                         symmetric: bool = False) -> None:
+    """K2's signed step over up to ``MAX_K2_SEGMENTS`` matrices in one launch.
+
+    Each segment is a dict with ``gq, w, v, alpha, beta`` (tensors), ``bits``,
+    ``lr``, ``lo``, ``hi`` and optional ``init_scale``, and either the next
+    operands (``wq_hi``, ``wq_lo``, ``wq_t32``) or the next codes (``codes``,
+    ``qscale``, ``qzp``).  Bit for bit one ``ste_signsgd(update=True)`` /
+    ``ste_signsgd_codes`` per segment."""
+    from mround_b200._native import K2Segment
+
+    if not 1 <= len(segments) <= MAX_K2_SEGMENTS:
+        raise SchemeError(f"1 to {MAX_K2_SEGMENTS} segments per launch, got {len(segments)}")
+    table = (K2Segment * len(segments))()
+    for i, sg in enumerate(segments):
+        rows, cols, pw, pv, pa, pb = _weight_args(sg["w"], sg["v"], sg["alpha"], sg["beta"], group)
+        n, ng = rows * cols, rows * (cols // group)
+        init = sg.get("init_scale")
+        _, pinit = _scheme_args(symmetric, init, ng)
+        table[i] = K2Segment(
+            _ptr(sg["gq"], torch.float32, "gq", n), pw, pv, pa, pb, pinit, rows, cols, sg["bits"],
+            sg["lr"], sg["lo"], sg["hi"],
+            _ptr(sg.get("wq_hi"), torch.bfloat16, "wq_hi", n),
+            _ptr(sg.get("wq_lo"), torch.bfloat16, "wq_lo", n),
+            _ptr(sg.get("wq_t32"), torch.float32, "wq_t32", n),
+            _ptr(sg.get("codes"), torch.uint8, "codes", n),
+            _ptr(sg.get("qscale"), torch.float32, "qscale", ng),
+            _ptr(sg.get("qzp"), torch.float32, "qzp", ng))
+    status = lib().mr_ste_signsgd_segments(table, len(segments), group, int(bool(symmetric)), eps,
+                                           _stream())
+    check(status, "mr_ste_signsgd_segments")
+    _count()
+
+
 def dequant_split(codes, qscale, qzp, *, group: int, symmetric: bool, wq_hi=None, wq_lo=None,
                   wq_t32=None) -> None:
     """Operands (bf16 hi/lo, tf32) from codes and per-group scale / zero point."""

