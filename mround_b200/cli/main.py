@@ -10,6 +10,7 @@ calibration batch.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 
 from mround_b200 import __version__
@@ -89,9 +90,10 @@ def _quantize(args: argparse.Namespace) -> int:
                       memory_check=not args.skip_memory_check,
                       min_block_coverage=0.0 if args.allow_dense else MIN_BLOCK_COVERAGE,
                       resume_dir=args.resume_dir)
-    if result.summary is not None:
-        print(result.summary.describe())
-    print(result.describe())
+    if int(os.environ.get("RANK", "0")) == 0:
+        if result.summary is not None:
+            print(result.summary.describe())
+        print(result.describe())
     return 0
 
 
@@ -103,6 +105,10 @@ def main(argv: list[str] | None = None) -> int:
     except MRoundError as exc:
         print(f"mround-b200: {exc}", file=sys.stderr)
         return 2
+    finally:
+        from mround_b200.pipeline.dist import shutdown
+
+        shutdown()
     return 1
 
 

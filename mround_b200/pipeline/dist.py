@@ -88,3 +88,9 @@ def init_from_env(backend: str | None = None, timeout_s: float = 300.0) -> DistC
     if not tdist.is_initialized():
         tdist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
     return DistContext(rank, world, None)
+
+
+def shutdown() -> None:
+    """Destroy the process group (``init_from_env``'s), if one is open."""
+    if tdist.is_available() and tdist.is_initialized():
+        tdist.destroy_process_group()

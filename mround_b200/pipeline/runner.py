@@ -23,6 +23,7 @@ from __future__ import annotations
 import dataclasses
 import time
 from collections.abc import Callable, Mapping, Sequence
+from concurrent.futures import ThreadPoolExecutor
 from typing import Any
 
 import torch
@@ -251,12 +252,38 @@ class QuantizationRunner:
             reference_stream = self.entrance(model, calibration_batches)
         before_blocks = meter.take()
         quantized_stream = [t.clone() for t in reference_stream] if self.quantized_inputs else None
+        resuming = resume is not None
+        # The next block's host weights (synthesised or read from the
+        # checkpoint) are produced on a worker thread while this block tunes;
+        # torch and numpy release the GIL in that work, and an error surfaces
+        # when its block is reached, as it would without the prefetch.
+        prefetch = ThreadPoolExecutor(max_workers=1, thread_name_prefix="mround-block-prefetch")
+        upcoming = prefetch.submit(model.block, indices[0]) if indices else None
+        try:
+            results, exported, schemes = self._walk(
+                model, indices, prefetch, upcoming, meter, reference_stream, quantized_stream,
+                scheme_by_layer, resume, resuming)
+        finally:
+            prefetch.shutdown(wait=True, cancel_futures=True)
+        total = time.perf_counter() - started
+        return (
+            RunSummary(blocks=results, total_seconds=total, peak_memory_bytes=meter.peak,
+                       scheme_by_layer=schemes, before_blocks=before_blocks),
+            exported,
+        )
+
+    def _walk(self, model, indices, prefetch, upcoming, meter, reference_stream,
+              quantized_stream, scheme_by_layer, resume, resuming):
+        """The block loop of ``run``."""
         results: list[BlockResult] = []
         exported: dict[str, QuantizedLayer] = {}
         schemes: dict[str, QuantScheme] = {}
-        resuming = resume is not None
-        for index in indices:
-            block = DeviceBlock(model.arch, model.block(index), self.device)
+        for pos, index in enumerate(indices):
+            params = upcoming.result()
+            if pos + 1 < len(indices):
+                upcoming = prefetch.submit(model.block, indices[pos + 1])
+            block = DeviceBlock(model.arch, params, self.device)
+            del params
             name = model.block_name(index)
             # every rank takes the same decision, even if one sees the file late
             resuming = resuming and self.dist.max_scalar(0.0 if resume.has(index) else 1.0,
@@ -298,12 +325,7 @@ class QuantizationRunner:
             results.append(result)
             if self.progress is not None and self.dist.rank == 0:
                 self.progress(result)
-        total = time.perf_counter() - started
-        return (
-            RunSummary(blocks=results, total_seconds=total, peak_memory_bytes=meter.peak,
-                       scheme_by_layer=schemes, before_blocks=before_blocks),
-            exported,
-        )
+        return results, exported, schemes
 
     def _restore_block(self, block: DeviceBlock, resume: ResumeStore,
                        index: int) -> tuple[BlockResult, dict[str, QuantizedLayer]]:
