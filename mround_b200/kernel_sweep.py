@@ -349,6 +349,39 @@ def block_k2(reps: int = 5, bits: int = 2, group: int = 64) -> list[dict]:
         def grouped():
             kernels.ste_signsgd_segments(segs, group=group, eps=1e-8)
 
+        # K9: the whole block's operands (bf16 hi/lo + tf32) rebuilt from codes,
+        # as every rank does after the codes gather (9 B/weight + 8 B/group)
+        fused = [(sum(shapes[p][0] for p in ("self_attn.q_proj", "self_attn.k_proj",
+                                               "self_attn.v_proj")), shapes["self_attn.q_proj"][1]),
+                 shapes["self_attn.o_proj"],
+                 (2 * shapes["mlp.gate_proj"][0], shapes["mlp.gate_proj"][1]),
+                 shapes["mlp.down_proj"]]
+        bufs, k9_bytes = [], 0
+        for rows, cols in fused:
+            ng = rows * cols // group
+            bufs.append((torch.randint(0, 1 << bits, (rows, cols), dtype=torch.uint8,
+                                       device=device),
+                         torch.rand(ng, device=device) * 1e-2, torch.rand(ng, device=device) * 3,
+                         torch.empty(rows, cols, dtype=torch.bfloat16, device=device),
+                         torch.empty(rows, cols, dtype=torch.bfloat16, device=device),
+                         torch.empty(rows, cols, device=device)))
+            k9_bytes += 9 * rows * cols + 8 * ng
+
+        def dequant_block():
+            for codes, sc, zp, hi, lo, t32 in bufs:
+                kernels.dequant_split(codes, sc, zp, group=group, symmetric=False, wq_hi=hi,
+                                      wq_lo=lo, wq_t32=t32)
+
+        dequant_block()
+        torch.cuda.synchronize()
+        ms = _time(dequant_block, flush, reps)
+        gbs = k9_bytes / (ms * 1e-3) / 1e9
+        rec = {"kernel": "K9_dequant_block", "arch": name, "launches": len(bufs),
+               "bytes": k9_bytes, "ms": ms, "gbs": gbs, "frac": gbs / peak, "peak_gbs": peak,
+               "peak_source": src}
+        out.append(rec)
+        print(json.dumps(rec), flush=True)
+        del bufs
         for form, fn in (("per_member", each), ("segmented", grouped)):
             fn()
             torch.cuda.synchronize()

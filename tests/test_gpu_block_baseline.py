@@ -14,6 +14,10 @@ tiny-architecture tests in test_gpu_block.py check the same bars at hidden
 - Qwen2.5-7B (hidden 3584, 28/4 heads -- GQA ratio 7 --, SwiGLU 18944), W2
   asym g64, one 2048-token sequence (configuration 5);
 
+- Qwen2.5-3B (hidden 2048, 16/2 heads, SwiGLU 11008, QKV bias) under a mixed
+  {2,3,4}-bit symmetric plan with searched scales, one 2048-token sequence
+  (configuration 4's scheme at its architecture);
+
 and a tuning loop at configuration 1 (SmolLM2, 50 steps, 4 x 8 x 512 tokens).
 
 Sequences of 512 and 2048 tokens take the causal tile-skipping GEMM modes and
@@ -224,3 +228,82 @@ def test_tuning_loop_matches_oracle_at_benchmark_shape(env, name):
     assert final_err <= 0.02
     assert result.final_loss < result.initial_loss
     assert not ref["reverted"]
+
+
+# configuration 4's scheme at its architecture: Qwen2.5-3B (hidden 2048, 16/2
+# heads, SwiGLU 11008, QKV bias), symmetric with the searched scale, a mixed
+# plan over {2, 3, 4} bits (widths differ inside the fused qkv and gate_up)
+MIXED_BITS = {"self_attn.q_proj": 4, "self_attn.k_proj": 3, "self_attn.v_proj": 3,
+              "self_attn.o_proj": 2, "mlp.gate_proj": 3, "mlp.up_proj": 2, "mlp.down_proj": 4}
+
+
+def test_mixed_searched_step_matches_oracle_at_3b_shape(env):
+    """One tuning step (the runner's default precision) of a 3B block under a
+    mixed {2,3,4}-bit symmetric plan with searched scales: the device's
+    searched scales feed the oracle, then loss and V/beta gradients at the
+    oracle's outlier set within 1e-3 (alpha is inert under a searched scale)."""
+    A, SM = env
+    from mround_b200.pipeline.block import TUNING_PRECISION, DeviceBlock
+    from mround_b200.pipeline.dist import DistContext
+    from mround_b200.pipeline.tuning import BlockTuner
+    from mround_b200.schemes import QuantScheme
+
+    arch = A.get_arch("qwen2.5-3b")
+    params = SM(arch, seed=8).block(0)
+    x = block_inputs(arch, 1, 1, 2048, seed=4)[0]
+    schemes = {p: QuantScheme(bits=b, group_size=GROUP, symmetry="sym", scale_init="searched")
+               for p, b in MIXED_BITS.items()}
+    block = DeviceBlock(arch, params)
+    tuner = BlockTuner(block, schemes, {p: 0.01 for p in LINEARS}, suppress=True, eps=1e-8,
+                       precision=TUNING_PRECISION, dist=DistContext())
+    assert tuner.search([x.cuda()]) > 0.0
+    init = {}
+    for t in tuner.tunables:
+        for m in t.members:
+            r0, r1 = m.rows
+            init[m.path] = t.init_scale[r0:r1].cpu()
+    oracle = OracleBlock(arch, params, MIXED_BITS, GROUP, symmetric=True, init_scales=init)
+    with torch.no_grad():
+        target = OracleBlock(arch, params, MIXED_BITS, GROUP).forward(x)
+    g = torch.Generator().manual_seed(12)
+    qp = {}
+    for p in LINEARS:
+        v, a, b = oracle.init_params()[p]
+        qp[p] = ((torch.rand(v.shape, generator=g) - 0.5) * 0.6,
+                 0.5 + torch.rand(a.shape, generator=g),
+                 0.5 + torch.rand(b.shape, generator=g))
+    leaves = {p: tuple(t.clone().requires_grad_(True) for t in qp[p]) for p in LINEARS}
+    pred_o = oracle.forward(x, leaves)
+    loss_o, thr_o = loss_fn(pred_o, target, True)
+    loss_o.backward()
+    keep_o = (pred_o.detach() - target).abs() < thr_o
+    n = keep_o.numel()
+    for t in tuner.tunables:
+        for m in t.members:
+            v, a, b = qp[m.path]
+            t.load(m.path, v.cuda(), a.cuda(), b.cuda())
+    loss_d, _ = tuner.gradient_only(x.cuda(), target.cuda())
+    with torch.no_grad():
+        out, saved = block.forward_fused(x.cuda(), TUNING_PRECISION, True)
+        r_d = out - target.cuda()
+        grad = (2.0 * r_d * keep_o.cuda() / n).float().contiguous()
+        block.backward_fused(saved, grad, TUNING_PRECISION)
+        del saved
+    grads = {}
+    for t in tuner.tunables:
+        grads.update(t.gradients())
+    torch.cuda.synchronize()
+    loss_err = abs(loss_d.item() - loss_o.item()) / loss_o.item()
+    worst = {}
+    for p in LINEARS:
+        for i, nm in ((0, "v"), (2, "beta")):
+            worst[f"{p}.{nm}"] = relative_error(grads[p][i].cpu().numpy(),
+                                                leaves[p][i].grad.numpy())
+        assert not grads[p][1].any(), "alpha is inert under a searched scale"
+    top = max(worst, key=worst.__getitem__)
+    thr_err = abs(float(tuner.ws.thr.item()) - float(thr_o)) / float(thr_o)
+    print(f"[block parity] qwen2.5-3b mixed {{2,3,4}} sym searched g{GROUP} 1x2048: loss rel "
+          f"{loss_err:.2e}, threshold rel {thr_err:.1e}; worst gradient {worst[top]:.2e} ({top})")
+    assert loss_err <= 1e-3
+    assert thr_err < 1e-4
+    assert worst[top] < 1e-3, worst
