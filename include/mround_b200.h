@@ -437,14 +437,18 @@ int mr_gemm_batched(const uint16_t* a_hi, const uint16_t* a_lo, int64_t lda, int
                     int64_t batch, int precision, int causal, int64_t seq, void* stream);
 
 /*
- * The output tile width (128, 224 or 256 columns) mr_gemm / mr_gemm_tf32 /
- * mr_gemm_batched / mr_gemm_rs use for this shape on the current device:
- * 128 for n <= 128; for one tf32 product (precision 4) the width of 224 and
- * 256 with the shorter persistent schedule (whole waves of tiles over the
- * SMs); 256 otherwise.  A query; launches nothing.  Negative status on bad
- * arguments.
+ * The output tile K3 uses for this shape on the current device (a query;
+ * launches nothing; negative status on bad arguments): mr_gemm_tile_n its
+ * width (128, 224 or 256 columns), mr_gemm_tile_m its height (128 or 256
+ * rows).  128 x 128 for n <= 128; 128 x 256 for the bf16 products; for one
+ * tf32 product (precision 4, no batch, no causal mode) the shape of 128 or
+ * 256 rows by 224 or 256 columns with the shortest persistent schedule (whole
+ * waves of tiles over the SMs, each tile's time the larger of its staged
+ * operand bytes and its flops at one SM's rates).
  */
 int mr_gemm_tile_n(int64_t m, int64_t n, int64_t k, int64_t batch, int precision, int a_kmajor,
+                   int b_kmajor, int causal);
+int mr_gemm_tile_m(int64_t m, int64_t n, int64_t k, int64_t batch, int precision, int a_kmajor,
                    int b_kmajor, int causal);
 
 /* Device status word of K3: 0, or MR_ERR_TIMEOUT.  Synchronizes the device;

@@ -67,6 +67,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mr_gemm_batched": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _I64, _I64, _I, _P, _I64, _I64, _P,
                              _I, _I64, _I64, _I64, _I64, _I, _I, _I64, _P]),
     "mr_gemm_tile_n": (_I, [_I64, _I64, _I64, _I64, _I, _I, _I, _I]),
+    "mr_gemm_tile_m": (_I, [_I64, _I64, _I64, _I64, _I, _I, _I, _I]),
     "mr_gemm_status": (_I, [_I]),
     "mr_gemm_rs": (_I, [_P, _P, _I64, _I, _P, _P, _I64, _I, _I64, _I64, _I64, _I, _P, _I64, _I64,
                         _P, _I, _P, ctypes.c_uint64, _P]),

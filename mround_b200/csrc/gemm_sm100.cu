@@ -51,6 +51,7 @@
 #include <string.h>
 
 #include <atomic>
+#include <cmath>
 
 #include "common.cuh"
 
@@ -227,7 +228,12 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn, b
          | (uint32_t(BM >> 4) << 24);    // M
 }
 
-template <int BN, int BK, int PREC>
+// MP: M parts per tile.  1: a 128 x BN tile, two TMEM accumulators (the
+// epilogue of one tile overlaps the next tile's MMAs).  2 (tf32 only, BN of
+// 224 or 256): a 256 x BN tile as two 128-row MMAs per K step sharing one B
+// tile -- 1.5x the flops per staged byte of the 128 x 256 tile -- in the two
+// halves of TMEM, so one tile is in flight and its epilogue does not overlap.
+template <int BN, int BK, int PREC, int MP = 1>
 struct Cfg {
   static constexpr bool kTf32 = PREC == 4;
   static constexpr int kElt = kTf32 ? 4 : 2;              // operand element bytes
@@ -236,7 +242,7 @@ struct Cfg {
   static constexpr int kB = BN * BK * kElt;               // bytes of one B part per stage
   static constexpr int kAParts = (PREC == 2 || PREC == 3) ? 2 : 1;
   static constexpr int kBParts = PREC == 3 ? 2 : 1;
-  static constexpr int kStage = kA * kAParts + kB * kBParts;
+  static constexpr int kStage = kA * kAParts * MP + kB * kBParts;
   static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
   // per epilogue warp, a 32 x 32 float32 block (padded rows) through which the
   // fused reduce-scatter turns row-per-lane values into row-contiguous stores
@@ -246,8 +252,11 @@ struct Cfg {
   // allocation is a power of two (224 -> 256 per accumulator, 512 in all)
   static constexpr int kAccCols = BN <= 128 ? 128 : 256;
   static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kBufs = MP == 2 ? 1 : 2;  // tiles whose accumulators are in flight
   static_assert(BN % 32 == 0 && BN <= kAccCols && kTmemCols <= 512,
                 "two accumulators must fit the 512 TMEM columns");
+  static_assert(MP == 1 || (MP == 2 && kTf32 && kAccCols == 256),
+                "two M parts: tf32 with 224- or 256-wide tiles");
 };
 
 // Operand maps of one launch.  a_chunked / b_chunked: the map is 4-D with a
@@ -350,7 +359,7 @@ __device__ __forceinline__ bool k_active(const Shape& sh, int m0, int kt) {
 }
 
 // Grouped rasterization inside each batch entry: 16 M-tiles share a sweep over N.
-template <int BN, int BK>
+template <int BN, int BK, int MP = 1>
 __device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
   constexpr int G = 16;
   const int per_batch = sh.m_tiles * sh.n_tiles;
@@ -361,7 +370,7 @@ __device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
   const int first_m = group * G;
   const int gm = min(G, sh.m_tiles - first_m);
   const int r = tt - group * G * sh.n_tiles;
-  tl.m0 = (first_m + r % gm) * BM;
+  tl.m0 = (first_m + r % gm) * BM * MP;
   tl.n0 = (r / gm) * BN;
   tl.kt_end = sh.k_tiles;
   tl.skip = sh.causal == 1 && tl.n0 > (tl.m0 % sh.clen) + BM - 1;
@@ -386,13 +395,13 @@ __device__ __forceinline__ Tile tile_at(const Shape& sh, int t) {
 //                      MMAs of tile j + 1 run in the other; each warp reads the
 //                      32 TMEM lanes (warp % 4) it may access, stores float32
 //                      rows, then arrives on tmem_empty[j & 1].
-template <int BN, int BK, int PREC>
+template <int BN, int BK, int PREC, int MP>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ Maps maps, float* __restrict__ c, int64_t ldc,
                 int64_t stride_c, const float* __restrict__ bias, int accumulate, int m, int n,
                 int k, int a_kmajor, int b_kmajor, int causal, int clen, int total_tiles,
                 const __grid_constant__ RemoteOut remote) {
-  using C = Cfg<BN, BK, PREC>;
+  using C = Cfg<BN, BK, PREC, MP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStage);
@@ -406,7 +415,7 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   Shape sh;
   sh.m = m; sh.n = n; sh.k = k;
-  sh.m_tiles = (m + BM - 1) / BM;
+  sh.m_tiles = (m + BM * MP - 1) / (BM * MP);
   sh.n_tiles = (n + BN - 1) / BN;
   sh.k_tiles = (k + BK - 1) / BK;
   sh.causal = causal;
@@ -438,7 +447,7 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int it = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const Tile tl = tile_at<BN, BK>(sh, t);
+        const Tile tl = tile_at<BN, BK, MP>(sh, t);
         for (int kt = 0; kt < tl.kt_end; ++kt) {
           if (!k_active<BK>(sh, tl.m0, kt)) continue;
           const int s = it % C::kStages;
@@ -454,7 +463,10 @@ __global__ void __launch_bounds__(192, 1)
           if (C::kAParts == 2)
             load_part<BM, BK, C::kElt>(st + C::kA, &maps.a_lo, &full[s], a_kmajor,
                                        maps.a_chunked, tl.m0, k0, tl.z);
-          uint8_t* sb = st + C::kA * C::kAParts;
+          if (MP == 2)  // the tile's second 128 rows (zero-filled past m)
+            load_part<BM, BK, C::kElt>(st + C::kA, &maps.a_hi, &full[s], a_kmajor,
+                                       maps.a_chunked, tl.m0 + BM, k0, tl.z);
+          uint8_t* sb = st + C::kA * C::kAParts * MP;
           load_part<BN, BK, C::kElt>(sb, &maps.b_hi, &full[s], b_kmajor, maps.b_chunked, tl.n0,
                                      k0, tl.z);
           if (C::kBParts == 2)
@@ -479,12 +491,13 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int it = 0, j = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++j) {
-        const Tile tl = tile_at<BN, BK>(sh, t);
-        const int b = j & 1;
-        if (j >= 2) ok = mbar_wait(&tmem_empty[b], ((j >> 1) - 1) & 1);
+        const Tile tl = tile_at<BN, BK, MP>(sh, t);
+        const int b = j % C::kBufs;
+        const int use = j / C::kBufs;
+        if (j >= C::kBufs) ok = mbar_wait(&tmem_empty[b], (use - 1) & 1);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem + uint32_t(b * C::kAccCols);
+        const uint32_t d = tmem + uint32_t(b * C::kAccCols);  // MP = 2: b = 0, halves at 0, 256
         bool first = true;
         for (int kt = 0; kt < tl.kt_end; ++kt) {
           if (!k_active<BK>(sh, tl.m0, kt)) continue;
@@ -495,7 +508,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t st = smem_u32(smem + s * C::kStage);
           const uint32_t a_hi = st;
           const uint32_t a_lo = st + C::kA;
-          const uint32_t b_hi = st + C::kA * C::kAParts;
+          const uint32_t b_hi = st + C::kA * C::kAParts * MP;
           const uint32_t b_lo = b_hi + C::kB;
 #pragma unroll
           for (int ks = 0; ks < BK / C::kMmaK; ++ks) {
@@ -504,6 +517,9 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t dbh = part_desc<BN, BK, C::kElt>(b_hi, b_kmajor, ks);
             if constexpr (C::kTf32) {
               umma_tf32(d, dah, dbh, idesc, acc0);
+              if constexpr (MP == 2)
+                umma_tf32(d + uint32_t(C::kAccCols), part_desc<BM, BK, C::kElt>(a_hi + C::kA, a_kmajor, ks),
+                          dbh, idesc, acc0);
             } else {
               umma_bf16(d, dah, dbh, idesc, acc0);
               if (PREC == 3)
@@ -530,78 +546,82 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
-      const Tile tl = tile_at<BN, BK>(sh, t);
-      const int b = j & 1;
-      ok = mbar_wait(&tmem_full[b], (j >> 1) & 1);
+      const Tile tl = tile_at<BN, BK, MP>(sh, t);
+      const int b = j % C::kBufs;
+      ok = mbar_wait(&tmem_full[b], (j / C::kBufs) & 1);
       tc_fence_after();
       ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int*>(&g_gemm_status) == 0);
       if (!ok) break;
       if (!tl.skip) {
         float* cz = c + int64_t(tl.z) * stride_c;
-        const int row = tl.m0 + quarter * 32 + lane;
-        const uint32_t lane_base =
-            tmem + uint32_t(b * C::kAccCols) + (uint32_t(quarter * 32) << 16);
 #pragma unroll 1
-        for (int col = 0; col < BN; col += 32) {
-          float v[32];
-          tmem_ld32(lane_base + col, v);
-          if (tl.n_active == 0) {
-#pragma unroll
-            for (int q = 0; q < 32; ++q) v[q] = 0.f;
-          }
-          const int gc = tl.n0 + col;
-          if (remote.active) {
-            // Peer stores: lane i holds row i's 32 columns; through the staging
-            // block, each store instruction writes 4 rows x 128 contiguous bytes
-            // (8 lanes per row) instead of 32 scattered 16-byte pieces, so
-            // NVLink carries full-line writes.
-#pragma unroll
-            for (int q = 0; q < 32; ++q) stage[lane * 33 + q] = v[q];
-            __syncwarp();
-            const int sub = lane >> 3, c4 = (lane & 7) * 4;
-#pragma unroll 2
-            for (int p = 0; p < 8; ++p) {
-              const int r = p * 4 + sub;
-              const int grow = tl.m0 + quarter * 32 + r;
-              const int gcol = gc + c4;
-              if (grow < m && gcol < n) {
-                const int owner = int(grow / remote.rows_per_rank);
-                float* dst = remote.dst[owner] +
-                             (grow - owner * remote.rows_per_rank) * remote.ldd + gcol;
-                const float* src = stage + r * 33 + c4;
-                if (gcol + 4 <= n) {
-                  *reinterpret_cast<float4*>(dst) = make_float4(src[0], src[1], src[2], src[3]);
-                } else {
-                  for (int i = 0; gcol + i < n; ++i) dst[i] = src[i];
-                }
-              }
+        for (int h = 0; h < MP; ++h) {  // MP = 2: rows m0 .. +127 at column 0, +128 .. at 256
+          const int m0 = tl.m0 + h * BM;
+          const int row = m0 + quarter * 32 + lane;
+          const uint32_t lane_base =
+              tmem + uint32_t((b + h) * C::kAccCols) + (uint32_t(quarter * 32) << 16);
+  #pragma unroll 1
+          for (int col = 0; col < BN; col += 32) {
+            float v[32];
+            tmem_ld32(lane_base + col, v);
+            if (tl.n_active == 0) {
+  #pragma unroll
+              for (int q = 0; q < 32; ++q) v[q] = 0.f;
             }
-            __syncwarp();
-            continue;
-          }
-          if (row < m && gc < n) {
-            float* dst = cz + int64_t(row) * ldc + gc;
-            const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
-            if (full_chunk) {
-#pragma unroll
-              for (int q = 0; q < 32; q += 4) {
-                float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-                if (bias) {
-                  o.x += bias[gc + q]; o.y += bias[gc + q + 1];
-                  o.z += bias[gc + q + 2]; o.w += bias[gc + q + 3];
+            const int gc = tl.n0 + col;
+            if (remote.active) {
+              // Peer stores: lane i holds row i's 32 columns; through the staging
+              // block, each store instruction writes 4 rows x 128 contiguous bytes
+              // (8 lanes per row) instead of 32 scattered 16-byte pieces, so
+              // NVLink carries full-line writes.
+  #pragma unroll
+              for (int q = 0; q < 32; ++q) stage[lane * 33 + q] = v[q];
+              __syncwarp();
+              const int sub = lane >> 3, c4 = (lane & 7) * 4;
+  #pragma unroll 2
+              for (int p = 0; p < 8; ++p) {
+                const int r = p * 4 + sub;
+                const int grow = m0 + quarter * 32 + r;
+                const int gcol = gc + c4;
+                if (grow < m && gcol < n) {
+                  const int owner = int(grow / remote.rows_per_rank);
+                  float* dst = remote.dst[owner] +
+                               (grow - owner * remote.rows_per_rank) * remote.ldd + gcol;
+                  const float* src = stage + r * 33 + c4;
+                  if (gcol + 4 <= n) {
+                    *reinterpret_cast<float4*>(dst) = make_float4(src[0], src[1], src[2], src[3]);
+                  } else {
+                    for (int i = 0; gcol + i < n; ++i) dst[i] = src[i];
+                  }
                 }
-                if (accumulate) {
-                  const float4 p = *reinterpret_cast<const float4*>(dst + q);
-                  o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
-                }
-                *reinterpret_cast<float4*>(dst + q) = o;
               }
-            } else {
-              for (int q = 0; q < 32 && gc + q < n; ++q) {
-                float o = v[q];
-                if (bias) o += bias[gc + q];
-                if (accumulate) o += dst[q];
-                dst[q] = o;
+              __syncwarp();
+              continue;
+            }
+            if (row < m && gc < n) {
+              float* dst = cz + int64_t(row) * ldc + gc;
+              const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+              if (full_chunk) {
+  #pragma unroll
+                for (int q = 0; q < 32; q += 4) {
+                  float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+                  if (bias) {
+                    o.x += bias[gc + q]; o.y += bias[gc + q + 1];
+                    o.z += bias[gc + q + 2]; o.w += bias[gc + q + 3];
+                  }
+                  if (accumulate) {
+                    const float4 p = *reinterpret_cast<const float4*>(dst + q);
+                    o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+                  }
+                  *reinterpret_cast<float4*>(dst + q) = o;
+                }
+              } else {
+                for (int q = 0; q < 32 && gc + q < n; ++q) {
+                  float o = v[q];
+                  if (bias) o += bias[gc + q];
+                  if (accumulate) o += dst[q];
+                  dst[q] = o;
+                }
               }
             }
           }
@@ -760,16 +780,16 @@ int sm_count() {
   return count;
 }
 
-template <int BN, int BK, int PREC>
+template <int BN, int BK, int PREC, int MP = 1>
 int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const float* bias,
            int accumulate, int m, int n, int k, int a_kmajor, int b_kmajor, int batch,
            int causal, int clen, const RemoteOut& remote, cudaStream_t stream) {
-  using C = Cfg<BN, BK, PREC>;
+  using C = Cfg<BN, BK, PREC, MP>;
   static std::atomic<bool> configured[kMaxDevices];
   const int dev = current_device();
   if (dev < 0) return MR_ERR_DEVICE;
   if (!configured[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BK, PREC>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, BK, PREC, MP>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) {
       set_cuda_error(e);
@@ -777,10 +797,10 @@ int launch(const Maps& maps, float* c, int64_t ldc, int64_t stride_c, const floa
     }
     configured[dev].store(true, std::memory_order_release);
   }
-  const int64_t tiles = int64_t((m + BM - 1) / BM) * ((n + BN - 1) / BN) * batch;
+  const int64_t tiles = int64_t((m + BM * MP - 1) / (BM * MP)) * ((n + BN - 1) / BN) * batch;
   if (tiles > (1ll << 31) - 1) return MR_ERR_ARGUMENT;
   const int grid = int(tiles < sm_count() ? tiles : sm_count());
-  gemm_kernel<BN, BK, PREC><<<grid, kThreads, C::kSmem, stream>>>(
+  gemm_kernel<BN, BK, PREC, MP><<<grid, kThreads, C::kSmem, stream>>>(
       maps, c, ldc, stride_c, bias, accumulate, m, n, k, a_kmajor, b_kmajor, causal, clen,
       int(tiles), remote);
   return launch_status();
@@ -793,29 +813,54 @@ using namespace mr;
 
 namespace {
 
-// Output tile width.  128 for narrow outputs (attention's head dimension);
-// otherwise 256, or 224 for the tf32 products where that evens out the
-// persistent schedule: every tile of one launch costs about the same, CTA i
-// takes tiles i, i + grid, ..., so a launch lasts ceil(tiles / SMs) tiles.
-// 224 needs every B chunk whole (MN-major tf32: 7 chunks of 32; K-major: any)
-// and no batch or causal mode.  Measured on the 7B step's shapes (CUDA
-// events, same box, against a 256-only build): tf32 dW through qkv 0.95-0.96x
-// the time and dX through o at 2048 tokens 0.97x, the long-K shapes
-// unchanged; the three-product bf16 forward at 224 ran up to 6 % slower at
-// 16384 tokens, so it keeps 256.
-int select_bn(int64_t m, int64_t n, int64_t batch, int precision, int b_kmajor, int causal,
-              int bk) {
-  if (n <= 128) return 128;
-  (void)b_kmajor;
-  (void)bk;
-  const bool can224 = batch == 1 && causal == 0 && precision == 4;
-  if (!can224) return 256;
-  const int64_t sms = sm_count();
-  const int64_t mt = (m + BM - 1) / BM;
-  const int64_t w256 = (mt * ((n + 255) / 256) + sms - 1) / sms;
-  const int64_t w224 = (mt * ((n + 223) / 224) + sms - 1) / sms;
-  // at least 3 % less: a 224-wide tile moves a little more A per flop
-  return w224 * 224 * 100 <= w256 * 256 * 97 ? 224 : 256;
+// Output tile shape.  128 x 128 for narrow outputs (attention's head
+// dimension); 128 x 256 for the bf16 products; for the tf32 products (no
+// batch, no causal mode) the shape of 128 or 256 rows (MP = 1 or 2) by 224 or
+// 256 columns whose persistent schedule is shortest.  CTA i takes tiles i,
+// i + grid, ..., so a launch lasts ceil(tiles / SMs) tile-times; a tile's time
+// is modelled as the larger of its staged operand bytes at one SM's share of
+// L2 bandwidth and its flops at one SM's tf32 rate (ratio ~55 flop/byte):
+// the 128 x 256 tile stages 384 rows of K per 2 x 128 x 256 flops (43.7
+// flop/byte) and is bandwidth-bound; the 256 x 256 tile, 512 rows for twice
+// the flops (65.5), is not.  224 needs every B chunk whole (MN-major tf32: 7
+// chunks of 32; K-major: any).  Measured 224 against 256 at MP = 1 (same box,
+// CUDA events): tf32 dW through qkv 0.95x the time, dX through o at 2048
+// tokens 0.97x, the long-K shapes unchanged; the bf16 split's forward at 224
+// ran up to 6 % slower, so it keeps 256.
+struct TileChoice {
+  int bn;
+  int mp;
+};
+
+TileChoice select_tile(int64_t m, int64_t n, int64_t k, int64_t batch, int precision,
+                       int causal) {
+  if (n <= 128) return {128, 1};
+  if (!(batch == 1 && causal == 0 && precision == 4)) return {256, 1};
+  const double sms = double(sm_count());
+  constexpr double kFlopPerByte = 55.0;
+  // a 256-row tile's epilogue does not overlap MMAs: measured as ~640 K
+  // elements of its main loop (dW through o at 2048 tokens, K = 2048, ran
+  // 1.14x slower with 256-row tiles; at K >= 3584 they won)
+  constexpr double kEpilogueK = 640.0;
+  TileChoice best{256, 1};
+  double best_cost = -1.0;
+  for (int mp = 1; mp <= 2; ++mp) {
+    for (int bn : {256, 224}) {
+      const double rows = double(BM) * mp;
+      const double tiles = std::ceil(double(m) / rows) * std::ceil(double(n) / bn);
+      const double waves = std::ceil(tiles / sms);
+      const double staged = (rows + bn) * 4.0 * kFlopPerByte;
+      const double flops = rows * bn * 2.0;
+      const double per_k = staged > flops ? staged : flops;
+      const double cost = waves * (double(k) + (mp == 2 ? kEpilogueK : 0.0)) * per_k;
+      // a later shape must be at least 3 % cheaper
+      if (best_cost < 0.0 || cost <= 0.97 * best_cost) {
+        best = {bn, mp};
+        best_cost = cost;
+      }
+    }
+  }
+  return best;
 }
 
 int select_bk(int64_t k, int tf32, int a_kmajor, int b_kmajor) {
@@ -863,7 +908,8 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
   // K-major rows as two 128-byte chunks, so it needs K a multiple of 32),
   // else 32-wide.
   const int BKsel = select_bk(k, tf32, a_kmajor, b_kmajor);
-  const int BNsel = select_bn(m, n, batch, precision, b_kmajor, causal, BKsel);
+  const TileChoice tile = select_tile(m, n, k, batch, precision, causal);
+  const int BNsel = tile.bn;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   int a_lo_chunked = 0, b_lo_chunked = 0;
@@ -891,7 +937,14 @@ int gemm_impl(const void* a_hi, const void* a_lo, int64_t lda, int64_t stride_a,
                                         a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);  \
   }
   if (tf32) {
-    static_assert(kTf32BK == 32, "one 224-wide tf32 instantiation serves both K slices");
+    static_assert(kTf32BK == 32, "one tf32 instantiation per tile shape serves both K slices");
+    if (tile.mp == 2) {
+      if (BNsel == 224)
+        return launch<224, 32, 4, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk,
+                                     a_kmajor, b_kmajor, bt, causal, int(seq), remote, s);
+      return launch<256, 32, 4, 2>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
+                                   b_kmajor, bt, causal, int(seq), remote, s);
+    }
     if (BNsel == 224)
       return launch<224, 32, 4>(maps, c, ldc, stride_c, bias, accumulate, M, N, Kk, a_kmajor,
                                 b_kmajor, bt, causal, int(seq), remote, s);
@@ -1001,13 +1054,24 @@ extern "C" int mr_gemm_rs_tf32(const float* a, int64_t lda, int a_kmajor, const 
                       rows_per_rank, flags, world, done, epoch, stream);
 }
 
-// The output tile width a launch of this shape uses (128, 224 or 256).
+// The output tile width (128, 224 or 256) and height (128 or 256) a launch
+// of this shape uses.
 extern "C" int mr_gemm_tile_n(int64_t m, int64_t n, int64_t k, int64_t batch, int precision,
                               int a_kmajor, int b_kmajor, int causal) {
   if (m <= 0 || n <= 0 || k <= 0 || batch <= 0 || precision < 1 || precision > 4)
     return MR_ERR_ARGUMENT;
-  return select_bn(m, n, batch, precision, b_kmajor, causal,
-                   select_bk(k, precision == 4, a_kmajor, b_kmajor));
+  (void)a_kmajor;
+  (void)b_kmajor;
+  return select_tile(m, n, k, batch, precision, causal).bn;
+}
+
+extern "C" int mr_gemm_tile_m(int64_t m, int64_t n, int64_t k, int64_t batch, int precision,
+                              int a_kmajor, int b_kmajor, int causal) {
+  if (m <= 0 || n <= 0 || k <= 0 || batch <= 0 || precision < 1 || precision > 4)
+    return MR_ERR_ARGUMENT;
+  (void)a_kmajor;
+  (void)b_kmajor;
+  return BM * select_tile(m, n, k, batch, precision, causal).mp;
 }
 
 // Device status word of the GEMM (0 ok, MR_ERR_TIMEOUT after a wait gave up).

@@ -429,13 +429,20 @@ def gemm_rs(a_hi, a_lo, b_hi, b_lo, *, m: int, n: int, k: int, a_kmajor: bool, b
 TF32_PRODUCT_COST = 2
 
 
+def gemm_tile(*, m: int, n: int, k: int, precision: int, a_kmajor: bool, b_kmajor: bool,
+              batch: int = 1, causal: int = 0) -> tuple[int, int]:
+    """The output tile (rows, columns) K3 uses for this shape."""
+    args = (m, n, k, batch, precision, int(a_kmajor), int(b_kmajor), causal)
+    rows, width = int(lib().mr_gemm_tile_m(*args)), int(lib().mr_gemm_tile_n(*args))
+    check(min(rows, width, 0), "mr_gemm_tile")
+    return rows, width
+
+
 def gemm_tile_n(*, m: int, n: int, k: int, precision: int, a_kmajor: bool, b_kmajor: bool,
                 batch: int = 1, causal: int = 0) -> int:
     """The output tile width (128, 224 or 256) K3 uses for this shape."""
-    width = int(lib().mr_gemm_tile_n(m, n, k, batch, precision, int(a_kmajor), int(b_kmajor),
-                                     causal))
-    check(min(width, 0), "mr_gemm_tile_n")
-    return width
+    return gemm_tile(m=m, n=n, k=k, precision=precision, a_kmajor=a_kmajor, b_kmajor=b_kmajor,
+                     batch=batch, causal=causal)[1]
 
 
 def gemm_tf32(a, b, c, *, m: int, n: int, k: int, a_kmajor: bool, b_kmajor: bool, lda: int,

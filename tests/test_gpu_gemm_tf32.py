@@ -93,6 +93,21 @@ def test_224_wide_tiles(K, a_kmajor, b_kmajor, m, n):
     run_case(K, m, n, 64, a_kmajor, b_kmajor, accumulate=True, seed=1)
 
 
+@pytest.mark.parametrize("a_kmajor", [True, False])
+@pytest.mark.parametrize("b_kmajor", [True, False])
+@pytest.mark.parametrize("m,n", [(1900, 4096), (16384, 3584)])
+def test_256_row_tiles(K, a_kmajor, b_kmajor, m, n):
+    """256-row tiles (two 128-row MMAs per K step sharing the B tile; chosen
+    for K long enough to cover their unoverlapped epilogue): a last tile
+    whose second half lies wholly past m (1900 = 7 x 256 + 108), and the 7B
+    step's 16384 x 3584 shape at 224 columns."""
+    for k in (6144, 6400):
+        assert K.gemm_tile(m=m, n=n, k=k, precision=4, a_kmajor=a_kmajor,
+                           b_kmajor=b_kmajor)[0] == 256
+    run_case(K, m, n, 6144, a_kmajor, b_kmajor, bias=True)
+    run_case(K, m, n, 6400, a_kmajor, b_kmajor, accumulate=True, seed=2)
+
+
 def test_bias_and_accumulate(K):
     run_case(K, 256, 384, 192, True, True, bias=True)
     run_case(K, 256, 384, 192, False, False, accumulate=True)

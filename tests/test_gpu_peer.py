@@ -47,6 +47,30 @@ def test_gemm_rs_single_rank_equals_gemm(K, m, n, k):
     assert torch.equal(out, want)
 
 
+def test_gemm_rs_tf32_two_owners_equals_gemm(K):
+    """The tf32 remote epilogue with 256-row tiles (two 128-row MMAs per K
+    step): rows split between two owners (local buffers standing in for two
+    ranks' slots; 2240 rows each, so a tile straddles the owners) hold
+    exactly what mr_gemm_tf32 writes, and both flags carry the epoch."""
+    m, n, k = 4480, 3584, 4096
+    assert K.gemm_tile(m=m, n=n, k=k, precision=4, a_kmajor=False, b_kmajor=False)[0] == 256
+    g = torch.Generator(device="cuda").manual_seed(3)
+    dy = K.round_tf32(torch.randn(k, m, device="cuda", generator=g))  # MN-major A
+    x = K.round_tf32(torch.randn(k, n, device="cuda", generator=g) * 0.02)  # MN-major B
+    want = torch.empty(m, n, device="cuda")
+    K.gemm_tf32(dy, x, want, m=m, n=n, k=k, a_kmajor=False, b_kmajor=False, lda=m, ldb=n, ldc=n)
+    slots = torch.zeros(2, m // 2, n, device="cuda")
+    flags = torch.zeros(2, dtype=torch.int64, device="cuda")
+    done = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.gemm_rs_tf32(dy, x, m=m, n=n, k=k, a_kmajor=False, b_kmajor=False, lda=m, ldb=n,
+                   dst_ptrs=[slots[0].data_ptr(), slots[1].data_ptr()], ldd=n,
+                   rows_per_rank=m // 2, flag_ptrs=[flags[0].data_ptr(), flags[1].data_ptr()],
+                   done=done, epoch=5)
+    torch.cuda.synchronize()
+    assert torch.equal(slots.view(m, n), want)
+    assert flags.tolist() == [5, 5] and int(done.item()) == 0
+
+
 def test_reduce_slots_sums_in_rank_order(K):
     world, rows, cols = 4, 64, 96
     slots = torch.randn(world, rows, cols, device="cuda")

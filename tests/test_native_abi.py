@@ -113,7 +113,7 @@ def test_gemm_tile_width_follows_the_persistent_schedule():
     assert width(2048, 3584, 4, batch=2) == 256
     assert width(16384, 37888, 4) == 256         # 128 whole waves already
     assert width(16384, 3584, 4) == 224          # 13 waves of 256 against 14 of 224
-    assert width(3584, 3584, 4) == 256           # 3 waves of 256 against 4 of 224
+    assert width(3584, 3584, 1) == 256
     assert width(2048, 128, 4) == 128
     assert width(2048, 4608, 4) == 256           # a ragged 224 tile would lengthen it
     from mround_b200.exceptions import SchemeError
@@ -164,3 +164,23 @@ def test_k2_segment_layout_matches_the_header(tmp_path):
     for f in fields:
         assert int(got[f]) == getattr(_native.K2Segment, f).offset, f
     assert int(got["size"]) == ctypes.sizeof(_native.K2Segment)
+
+
+def test_gemm_tile_height_follows_the_schedule_model():
+    """tf32 products take 256-row tiles where whole waves of them finish
+    first and K covers their unoverlapped epilogue (the 7B backward at one
+    GPU), 128 rows for small M or short K; the bf16 products keep 128."""
+    from mround_b200 import kernels
+
+    def tile(m, n, k, precision=4):
+        return kernels.gemm_tile(m=m, n=n, k=k, precision=precision, a_kmajor=False,
+                                 b_kmajor=False)
+
+    assert tile(16384, 3584, 37888) == (256, 224)  # dX through gate_up, one GPU
+    assert tile(2048, 3584, 37888) == (256, 224)   # the same at 2048 tokens (8 ranks)
+    assert tile(37888, 3584, 16384) == (256, 256)  # dW through gate_up, one GPU
+    assert tile(3584, 18944, 16384) == (256, 256)  # dW through down, one GPU
+    assert tile(3584, 3584, 2048) == (128, 256)    # dW through o at 8 ranks: K too short
+    assert tile(256, 3584, 4096) == (128, 224)     # one 256-row tile would leave SMs idle
+    assert tile(16384, 3584, 37888, precision=3) == (128, 256)
+    assert tile(2048, 128, 2048) == (128, 128)
