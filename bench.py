@@ -177,8 +177,8 @@ class ClockSampler:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
 #       --clock-control none -k regex:gemm_kernel --csv
 #       python -m mround_b200.kernel_sweep --gemm-all 16384
-# (51.8 GB per step for 17.8 GB of operands and outputs).
-GEMM_TRAFFIC_7B = 4.71e9
+# (50.8 GB per step for 17.8 GB of operands and outputs).
+GEMM_TRAFFIC_7B = 4.62e9
 
 
 # ----------------------------------------------------------------- workload
