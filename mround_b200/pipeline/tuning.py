@@ -177,6 +177,8 @@ class TunableLayer:
         return (self.group, self.symmetric, self.init_scale is not None)
 
     def run_segments(self, segments: list[dict]) -> None:
+        """K2 over ``segments`` (of tunables sharing this one's ``launch_key``),
+        ``kernels.MAX_K2_SEGMENTS`` to a launch."""
         for i in range(0, len(segments), kernels.MAX_K2_SEGMENTS):
             kernels.ste_signsgd_segments(segments[i:i + kernels.MAX_K2_SEGMENTS], group=self.group,
                                          eps=self.eps, symmetric=self.symmetric)
@@ -407,11 +409,11 @@ class BlockTuner:
                 per = out // dist.world
                 s0, s1 = dist.rank * per, (dist.rank + 1) * per
                 grad = torch.empty((per, inn), dtype=torch.float32, device=block.device)
-                # untuned rows of a partly tuned fused weight keep their exact operand
                 if gather == "codes" and t.whole and inn % 8 == 0:
                     self._shards[id(t.layer)] = _Shard(s0, s1, grad, None, None, None,
                                                        self._codes_buffers(t, per))
                     continue
+                # untuned rows of a partly tuned fused weight keep their exact operand
                 t32 = t.layer.wq_t32
                 self._shards[id(t.layer)] = _Shard(
                     s0, s1, grad, t.layer.wq_hi[s0:s1].clone(), t.layer.wq_lo[s0:s1].clone(),
@@ -504,12 +506,12 @@ class BlockTuner:
         if not self._sharded_step:
             # every fused weight's gradient is whole; tunables of one scheme and
             # group share a launch
-            launches: dict[tuple, list] = {}
+            launches: dict[tuple, list[TunableLayer]] = {}
             for t in self.tunables:
                 self._wait(t.layer)
                 launches.setdefault(t.launch_key, []).append(t)
-            for group in launches.values():
-                group[0].run_segments([sg for t in group for sg in t.segments(step, iters)])
+            for alike in launches.values():
+                alike[0].run_segments([sg for t in alike for sg in t.segments(step, iters)])
             return
         # Copy-engine exchange: every copy and flag release of this rank ends
         # before the first owner-side sum spins on this GPU, so no flag kernel
