@@ -517,9 +517,10 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t dbh = part_desc<BN, BK, C::kElt>(b_hi, b_kmajor, ks);
             if constexpr (C::kTf32) {
               umma_tf32(d, dah, dbh, idesc, acc0);
-              if constexpr (MP == 2)
-                umma_tf32(d + uint32_t(C::kAccCols), part_desc<BM, BK, C::kElt>(a_hi + C::kA, a_kmajor, ks),
-                          dbh, idesc, acc0);
+              if constexpr (MP == 2)  // the second 128 rows on the same B tile
+                umma_tf32(d + uint32_t(C::kAccCols),
+                          part_desc<BM, BK, C::kElt>(a_hi + C::kA, a_kmajor, ks), dbh, idesc,
+                          acc0);
             } else {
               umma_bf16(d, dah, dbh, idesc, acc0);
               if (PREC == 3)
@@ -560,12 +561,12 @@ __global__ void __launch_bounds__(192, 1)
           const int row = m0 + quarter * 32 + lane;
           const uint32_t lane_base =
               tmem + uint32_t((b + h) * C::kAccCols) + (uint32_t(quarter * 32) << 16);
-  #pragma unroll 1
+#pragma unroll 1
           for (int col = 0; col < BN; col += 32) {
             float v[32];
             tmem_ld32(lane_base + col, v);
             if (tl.n_active == 0) {
-  #pragma unroll
+#pragma unroll
               for (int q = 0; q < 32; ++q) v[q] = 0.f;
             }
             const int gc = tl.n0 + col;
@@ -574,11 +575,11 @@ __global__ void __launch_bounds__(192, 1)
               // block, each store instruction writes 4 rows x 128 contiguous bytes
               // (8 lanes per row) instead of 32 scattered 16-byte pieces, so
               // NVLink carries full-line writes.
-  #pragma unroll
+#pragma unroll
               for (int q = 0; q < 32; ++q) stage[lane * 33 + q] = v[q];
               __syncwarp();
               const int sub = lane >> 3, c4 = (lane & 7) * 4;
-  #pragma unroll 2
+#pragma unroll 2
               for (int p = 0; p < 8; ++p) {
                 const int r = p * 4 + sub;
                 const int grow = m0 + quarter * 32 + r;
@@ -600,9 +601,10 @@ __global__ void __launch_bounds__(192, 1)
             }
             if (row < m && gc < n) {
               float* dst = cz + int64_t(row) * ldc + gc;
-              const bool full_chunk = gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+              const bool full_chunk =
+                  gc + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
               if (full_chunk) {
-  #pragma unroll
+#pragma unroll
                 for (int q = 0; q < 32; q += 4) {
                   float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
                   if (bias) {
