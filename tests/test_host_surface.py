@@ -190,3 +190,29 @@ def test_exchange_default_follows_the_measured_rank_count():
     from mround_b200.pipeline.tuning import auto_exchange
 
     assert [auto_exchange(n) for n in (1, 2, 4, 8)] == ["p2p", "p2p", "p2p", "nccl"]
+
+
+def test_k2_segments_and_codes_wrappers_refuse_before_any_launch():
+    """The segmented K2 launch takes 1 to 8 matrices; CPU tensors are refused
+    (no CPU fallback) before the library is called; the tuner refuses an
+    unknown gather form."""
+    from mround_b200 import kernels
+    from mround_b200.exceptions import PlatformError
+
+    with pytest.raises(SchemeError):
+        kernels.ste_signsgd_segments([], group=64, eps=1e-8)
+    with pytest.raises(SchemeError):
+        kernels.ste_signsgd_segments([{}] * (kernels.MAX_K2_SEGMENTS + 1), group=64, eps=1e-8)
+    w = torch.zeros(4, 64, dtype=torch.bfloat16)
+    seg = {"gq": torch.zeros(4, 64), "w": w, "v": torch.zeros(4, 64), "alpha": torch.ones(4, 1),
+           "beta": torch.ones(4, 1), "bits": 2, "lr": 0.01, "lo": 0.5, "hi": 1.0}
+    with pytest.raises(PlatformError):
+        kernels.ste_signsgd_segments([seg], group=64, eps=1e-8)
+    with pytest.raises(PlatformError):
+        kernels.dequant_split(torch.zeros(4, 64, dtype=torch.uint8), torch.ones(4), torch.zeros(4),
+                              group=64, symmetric=False)
+    from mround_b200.pipeline.tuning import BlockTuner
+
+    with pytest.raises(ValueError, match="gather"):
+        BlockTuner(None, {}, {}, suppress=False, eps=1e-8, precision=None, dist=None,
+                   gather="rows")
