@@ -183,10 +183,6 @@ class TunableLayer:
             kernels.ste_signsgd_segments(segments[i:i + kernels.MAX_K2_SEGMENTS], group=self.group,
                                          eps=self.eps, symmetric=self.symmetric)
 
-    def update(self, step: int, iters: int) -> None:
-        """K2 on every member with the linearly decayed rate of this step (one launch)."""
-        self.run_segments(self.segments(step, iters))
-
     def update_rows(self, step: int, iters: int, s0: int, s1: int, grad: torch.Tensor,
                     hi: torch.Tensor, lo: torch.Tensor, t32: torch.Tensor | None = None) -> None:
         """K2 on rows [s0, s1) only: ``grad`` holds the summed gradient of those
